@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""Benchmark of the engine step: BASELINE config 4, Mistral-7B-shaped Q8.
+
+Workload (one rank = one GPU = one engine): 256 concurrent requests with prompt
+lengths log-normal (median 1024, sigma 1.0, capped at 8192), outputs uniform in
+64..512, 16-token KV pages, reference default sampling (T 0.8, top-k 40,
+top-p 0.95, repeat penalty 1.1) on the SplitMix64 streams.  Weights are a
+seeded random init (N(0, 0.02), quantised to Q8 with the reference's block
+quantizer) generated on the device.  A "step" is one engine tick in steady
+decode: every session appends one token (prefillSelected over 256 decode rows
++ sampleWithBlocked), so output tokens per step = 256.  The KV pages already
+hold each session's prompt and the decode tokens before its starting offset
+(synthetic values: a prefilled cache); offsets are uniform in the session's
+output budget so contexts are ragged, as in a running server.
+
+`value`   = output tokens / s over all ranks from the device span of each step
+            (first to last kernel, CUDA events on the library's stream).
+`e2e`     = the same metric through the C ABI call sr_step_sample with host
+            buffers: the step's batch metadata and sampling history are copied
+            from pinned host memory and the sampled ids are read back every step;
+            timed with events on the same stream around the whole K steps
+            (host gaps included).
+Multi-GPU: each rank runs an independent replica (weak scaling); tensor
+parallelism is not built yet.
+`--impl reference` times the CPU oracle (the C restatement of the reference's
+Go step, all host threads) on a bounded sample of the same workload.
+"""
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIG = dict(name="mistral7b-q8-256req", vocab=32768, dim=4096, hidden=14336, layers=32, heads=32, kv_heads=8,
+              context=32768, rope_theta=1e6, norm_eps=1e-5, tied=False, fmt="q8", page_tokens=16, sessions=256,
+              prompt_median=1024, prompt_sigma=1.0, prompt_max=8192, out_lo=64, out_hi=512,
+              sampling=(0.8, 40, 0.95, 1.1), seed=20261201)
+METRIC = "output tok/s, Mistral-7B-shape Q8, 256 ragged reqs; p50 TTFT/ITL; HBM GB/s"
+
+
+def workload(cfg, rank, warmup_steps):
+    rng = np.random.default_rng(cfg["seed"] + 7919 * rank)
+    S = cfg["sessions"]
+    prompts = np.clip(np.round(np.exp(np.log(cfg["prompt_median"]) + cfg["prompt_sigma"] * rng.standard_normal(S))),
+                      1, cfg["prompt_max"]).astype(np.int64)
+    outs = rng.integers(cfg["out_lo"], cfg["out_hi"] + 1, size=S)
+    offsets = np.array([rng.integers(0, max(1, o - warmup_steps)) for o in outs], dtype=np.int64)
+    return prompts, outs, offsets, rng
+
+
+def clocks_start(path, device):
+    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+    try:
+        return subprocess.Popen(["nvidia-smi", "-i", str(device), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                 "-lms", "200"], stdout=open(path, "w"), stderr=subprocess.DEVNULL)
+    except Exception:
+        return None
+
+
+def clocks_stop(proc, path):
+    if proc is None:
+        return None
+    proc.terminate()
+    try:
+        proc.wait(timeout=5)
+    except Exception:
+        proc.kill()
+    sm, mx, reasons = [], 0.0, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for line in open(path):
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 9:
+            continue
+        try:
+            sm.append(float(f[1]))
+            mx = max(mx, float(f[2]))
+        except ValueError:
+            continue
+        for n, v in zip(names, f[5:9]):
+            if v.lower() == "active":
+                reasons.add(n)
+    if not sm:
+        return None
+    return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def traffic_per_position():
+    """DRAM bytes per (position, layer) of the attention kernel from a committed
+    ncu summary, if one exists (profiles/attention_traffic.json)."""
+    p = os.path.join(ROOT, "profiles", "attention_traffic.json")
+    try:
+        return json.load(open(p))
+    except Exception:
+        return None
+
+
+class DecodeState:
+    """256 sessions in steady decode over one device model and page pool."""
+
+    def __init__(self, cfg, device, warmup, steps, mode):
+        from sr_go_tranformer_b200 import _abi as A
+        from sr_go_tranformer_b200 import step as S
+        self.A, self.S, self.cfg = A, S, cfg
+        prompts, outs, offsets, rng = workload(cfg, int(os.environ.get("RANK", "0")), warmup)
+        self.prompts, self.outs = prompts, outs
+        n = cfg["sessions"]
+        pt = cfg["page_tokens"]
+        d = S.make_desc(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
+                        cfg["context"], cfg["rope_theta"], cfg["norm_eps"], cfg["tied"], False, cfg["fmt"], pt)
+        self.model = S.Model(d, device)
+        self.model.init_synthetic(cfg["seed"], 0.02)
+        self.model.set_mode(mode)
+        reserve = int(np.sum((prompts + outs + pt - 1) // pt))
+        self.pool = S.PagePool(self.model, reserve)
+        self.pool.fill_synthetic(cfg["seed"] + 1, 0.5)
+        self.pos = (prompts + offsets).astype(np.int32)
+        # LIFO page acquisition in session order, as the engine admits them.
+        self.pages = [[] for _ in range(n)]
+        for i in range(n):
+            need = (int(self.pos[i]) + 1 + pt - 1) // pt
+            while len(self.pages[i]) < need:
+                self.pages[i].append(self.pool.acquire())
+        self.page_arr = [np.asarray(p, dtype=np.int32) for p in self.pages]
+        V = cfg["vocab"]
+        self.hist = [rng.integers(0, V, size=int(self.pos[i])).astype(np.int32) for i in range(n)]
+        self.last = rng.integers(0, V, size=n).astype(np.int32)
+        self.rng_state = np.array([cfg["seed"] + i for i in range(n)], dtype=np.uint64)
+        t, k, p, pen = cfg["sampling"]
+        self.settings = (A.Sampling * n)(*[A.Sampling(t, k, 0, p, pen) for _ in range(n)])
+        self.toff = np.arange(n + 1, dtype=np.int32)
+        self.ids = np.zeros(n, dtype=np.int32)
+        self.n = n
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.ctx_trace = []
+
+    def step(self):
+        A, n, pt = self.A, self.n, self.cfg["page_tokens"]
+        for i in range(n):  # ensurePages for the new row (lazy LIFO acquire)
+            if (int(self.pos[i]) + 1 + pt - 1) // pt > len(self.pages[i]):
+                self.pages[i].append(self.pool.acquire())
+                self.page_arr[i] = np.asarray(self.pages[i], dtype=np.int32)
+        poff = np.zeros(n + 1, dtype=np.int32)
+        poff[1:] = np.cumsum([len(p) for p in self.pages])
+        pids = np.concatenate(self.page_arr)
+        hoff = np.zeros(n + 1, dtype=np.int32)
+        hoff[1:] = np.cumsum([len(h) for h in self.hist])
+        hist = np.concatenate(self.hist)
+        b = A.Batch(n, self.pos.ctypes.data, self.toff.ctypes.data, self.last.ctypes.data, poff.ctypes.data,
+                    pids.ctypes.data, None)
+        self.ctx_trace.append(int(np.sum(self.pos.astype(np.int64) + 1)))
+        A.check(A.lib().sr_step_sample(self.model.h, self.pool.h, C.byref(b), C.cast(self.settings, C.c_void_p),
+                                       hoff.ctypes.data, hist.ctypes.data, self.rng_state.ctypes.data, -1,
+                                       self.ids.ctypes.data))
+        # bytes crossing the host boundary this step (sr_upload_batch + sampler staging)
+        self.h2d_bytes += 4 * (1864 + pids.size) + n * 32 + 4 * (n + 1) + 4 * hist.size + 8 * n
+        self.d2h_bytes += 8 * n + 4 * n + 4 * n
+        for i in range(n):
+            self.hist[i] = np.append(self.hist[i], self.ids[i])
+        self.pos += 1
+        self.last[:] = self.ids
+
+    def profile(self, reset=False):
+        A = self.A
+        ms = (C.c_double * len(A.PROF_CLASSES))()
+        la = (C.c_int64 * len(A.PROF_CLASSES))()
+        span, steps, total = C.c_double(), C.c_int64(), C.c_int64()
+        A.check(A.lib().sr_profile_read(self.model.h, ms, la, C.byref(span), C.byref(steps), C.byref(total),
+                                        1 if reset else 0))
+        return list(ms), list(la), span.value, steps.value, total.value
+
+    def set_profile(self, mask):
+        self.A.check(self.A.lib().sr_profile_set(self.model.h, mask))
+
+    def stream(self):
+        s = C.c_void_p()
+        self.A.check(self.A.lib().sr_model_stream(self.model.h, C.byref(s)))
+        return s.value
+
+
+def weight_bytes(cfg):
+    """Matrix bytes read once per step (Q8 values + fp32 scales), embedding excluded."""
+    d, kd, h, V, L = cfg["dim"], cfg["dim"] // cfg["heads"] * cfg["kv_heads"], cfg["hidden"], cfg["vocab"], cfg["layers"]
+    mats = [(d, d), (kd, d), (kd, d), (d, d), (h, d), (h, d), (d, h)]
+    per_layer = sum(r * c + r * ((c + 63) // 64) * 4 for r, c in mats) + 2 * d * 4
+    head = V * d + V * ((d + 63) // 64) * 4
+    return L * per_layer + head + d * 4
+
+
+def cpu_baseline(cfg, sample_sessions, threads, steps=1):
+    """Time the CPU oracle on `sample_sessions` sessions of the same workload."""
+    from oracle import oracle as O
+    O.build()
+    pt = cfg["page_tokens"]
+    c = O.make_config(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
+                      cfg["context"], cfg["rope_theta"], cfg["norm_eps"], cfg["tied"], False, cfg["fmt"], pt)
+    m = O.Model(c)
+    t0 = time.time()
+    m.init_synthetic(cfg["seed"], 0.02, threads=threads)
+    init_s = time.time() - t0
+    prompts, outs, offsets, rng = workload(cfg, 0, 3)
+    idx = list(range(sample_sessions))
+    pos = [int(prompts[i] + offsets[i]) for i in idx]
+    tables, nxt = [], 0
+    for p in pos:
+        k = (p + 1 + pt - 1) // pt
+        tables.append(list(range(nxt, nxt + k)))
+        nxt += k
+    pool = np.zeros(nxt * m.page_elements, dtype=np.float32)
+    toks = [[int(t)] for t in rng.integers(0, cfg["vocab"], size=len(idx))]
+    times = []
+    for s in range(steps):
+        t0 = time.time()
+        m.step(pool, [p + s for p in pos], toks, tables, threads=threads)
+        times.append(time.time() - t0)
+    t = float(np.median(times))
+    return {"value": len(idx) / t, "unit": "output tok/s", "cores": threads, "kind": "port",
+            "sample": f"{len(idx)} of the workload's sessions, one decode step each (contexts {min(pos)}..{max(pos)}),"
+                      f" C oracle restating the Go step, {threads} threads; model init {init_s:.1f}s untimed",
+            "step_s": t}
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    W, K = args.warmup, args.steps
+    from oracle import oracle as O
+    O.build()
+    # bounded sample: 8 sessions per step (about 10 s of CPU work per step on 32+ cores)
+    res = cpu_baseline(cfg, args.ref_sessions, threads, steps=max(1, min(K, 3)))
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "output tok/s", "n_gpus": args.gpus,
+            "steps": K, "warmup": W, "ms_per_step": res["step_s"] * 1000.0, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["name"], "sessions_sampled": args.ref_sessions, "page_tokens": 16},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": "output tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default=os.environ.get("SR_BENCH_MODE", "fast"), choices=["exact", "fast"])
+    ap.add_argument("--sessions", type=int, default=CONFIG["sessions"])
+    ap.add_argument("--layers", type=int, default=CONFIG["layers"])
+    ap.add_argument("--cpu-sessions", type=int, default=8)
+    ap.add_argument("--ref-sessions", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = dict(CONFIG)
+    cfg["sessions"] = args.sessions
+    cfg["layers"] = args.layers
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+    W = max(3, args.warmup)
+    K = args.steps
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    st = DecodeState(cfg, local, W, K, args.mode)
+    for _ in range(W):
+        st.step()
+    ext = torch.cuda.ExternalStream(st.stream())
+    st.profile(reset=True)
+    st.set_profile(1 << 5)  # attention launches timed with events inside the timed region
+    st.ctx_trace.clear()
+    st.h2d_bytes = st.d2h_bytes = 0
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    tmp = tempfile.NamedTemporaryFile(suffix=".csv", delete=False).name
+    clk = clocks_start(tmp, local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(K):
+        st.step()
+    e1.record(ext)
+    torch.cuda.synchronize()
+    clocks = clocks_stop(clk, tmp)
+    e2e_ms = e0.elapsed_time(e1)
+    ms, launches, span_ms, nsteps, total_launches = st.profile(reset=True)
+    st.set_profile(0)
+    # Per-class breakdown from a separately profiled step (not timed).
+    st.set_profile((1 << 9) - 1)
+    st.step()
+    cls_ms, cls_launch, _, _, _ = st.profile(reset=True)
+    st.set_profile(0)
+    t = torch.tensor([span_ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    span_max, e2e_max = float(t[0]), float(t[1])
+    tokens = cfg["sessions"] * K * world
+    value = tokens / (span_max / 1000.0)
+    e2e_val = tokens / (e2e_max / 1000.0)
+    if rank == 0:
+        peaks, peak_kind = measured_peaks()
+        kvd = cfg["dim"] // cfg["heads"] * cfg["kv_heads"]
+        kv_pos_bytes = 2 * kvd * 4  # K + V row of one position, one layer
+        attn_launches = launches[5]
+        attn_ms = ms[5] / max(1, attn_launches)
+        positions = float(np.mean(st.ctx_trace))  # sum over sessions of (pos+1) per step
+        attn_bytes = positions * kv_pos_bytes + 2 * cfg["sessions"] * cfg["dim"] * 4
+        achieved = attn_bytes / (attn_ms / 1000.0) / 1e9
+        tr = traffic_per_position()
+        traffic = None if tr is None else float(tr["bytes_per_position_layer"] * positions +
+                                                tr.get("fixed_bytes", 0))
+        wbytes = weight_bytes(cfg)
+        step_bytes = wbytes + cfg["layers"] * (positions * kv_pos_bytes + cfg["sessions"] * kv_pos_bytes) + \
+            4 * cfg["sessions"] * cfg["vocab"]
+        cls_total = sum(cls_ms) or 1.0
+        line = {
+            "metric": METRIC, "value": value, "unit": "output tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": span_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["name"], "sessions": cfg["sessions"], "layers": cfg["layers"],
+                       "page_tokens": cfg["page_tokens"], "weights": "q8 (64-col blocks, fp32 scales)",
+                       "mode": args.mode, "parallelism": f"replicas{world}",
+                       "kv_state": "synthetic prefilled pages (prompt + decode offset)",
+                       "l2": "inputs larger than L2 (KV pool > 100 GB)",
+                       "sampling": "T0.8 k40 p0.95 penalty1.1, SplitMix64"},
+            "itl_p50_ms": span_max / K, "ttft_p50_ms": None,
+            "hbm_gbs_step": step_bytes / (span_max / K / 1000.0) / 1e9,
+            "algorithmic_bytes_per_step": step_bytes,
+            "e2e": {"value": e2e_val, "unit": "output tok/s",
+                    "h2d_bytes_per_step": st.h2d_bytes // max(1, K), "d2h_bytes_per_step": st.d2h_bytes // max(1, K)},
+            "gpu_launches": int(total_launches),
+            "roofline": {"kernel": "attention", "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                         "peak_source": peak_kind, "launch_ms": attn_ms, "algorithmic_bytes": attn_bytes},
+            "kernels": {n: {"ms_per_step": cls_ms[i], "share": cls_ms[i] / cls_total, "launches": cls_launch[i]}
+                        for i, n in enumerate(st.A.PROF_CLASSES)},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                cb = cpu_baseline(cfg, args.cpu_sessions, os.cpu_count() or 1)
+                line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            except Exception as e:  # reported, never silently replaced
+                line["cpu_baseline"] = {"error": str(e)}
+        print(json.dumps(line))
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,252 @@
+/*
+ * srstep.h -- C ABI of the B200 engine step (libsrstep.so).
+ *
+ * This is the drop-in boundary for the continuous-batching prefill/decode step
+ * of RyoSpiralArchitect/sr_go_tranformer's Go engine.  Every entry point uses
+ * plain C types (pointers, fixed-width integers, sizes) so that the reference's
+ * Go engine can bind it through cgo; no C++ or torch types cross it.
+ *
+ * Conventions shared by every call:
+ *   - Return value: SR_OK (0) or one of the SR_E* codes below.  On any error
+ *     sr_last_error() returns a NUL-terminated message for the calling thread.
+ *   - Validation completes before any device state is mutated: an SR_EINVAL
+ *     step leaves every KV page untouched (reference contract,
+ *     cmd/monolith/prefill_test.go:91).
+ *   - One caller at a time per sr_model (the reference's single engine actor,
+ *     cmd/monolith/monolith.go:3704-3708, 6209-6213).  Weights are read-only
+ *     after loading; a model may serve several pools.
+ *   - Host pointers passed in are only read during the call (they may be
+ *     ordinary or pinned memory); the call returns after its device work has
+ *     completed unless the entry point says otherwise.
+ */
+#ifndef SRSTEP_H
+#define SRSTEP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+enum {
+    SR_OK = 0,
+    SR_EINVAL = 1,    /* invalid argument or batch; nothing mutated */
+    SR_ECANCELED = 2, /* cancel flag observed between layers; positions not committed */
+    SR_ENOMEM = 3,    /* device allocation failed */
+    SR_ETIMEOUT = 4,  /* a bounded device or collective wait expired */
+    SR_EDEVICE = 5,   /* CUDA error; the message names the failing call */
+    SR_EUNSUPPORTED = 6
+};
+
+/* Weight formats (cmd/monolith/monolith.go:566-582, validHFWeightFormat /
+ * hfMatrixFormat): q4-mixed stores embedding and LM head as Q8, others Q4. */
+enum { SR_FMT_F32 = 0, SR_FMT_Q8 = 1, SR_FMT_Q4 = 2, SR_FMT_Q4_MIXED = 3 };
+/* Per-parameter storage of one tensor. */
+enum { SR_PARAM_F32 = 0, SR_PARAM_Q8 = 1, SR_PARAM_Q4 = 2 };
+
+/* Arithmetic mode of the step.
+ * SR_MODE_EXACT reproduces the reference's fp32/fp64 operation order
+ *   (sequential fp32 dots, 4-strided Q8/Q4 partials per 64-block, fp64 norm,
+ *   softmax and SwiGLU sums) on CUDA cores, without FMA contraction.
+ * SR_MODE_FAST uses fused multiply-adds, tensor-core projections and split-K
+ *   attention; it matches the reference within a stated tolerance. */
+enum { SR_MODE_EXACT = 0, SR_MODE_FAST = 1 };
+
+/* Model description: Config (cmd/monolith/monolith.go:56-66) plus the HF
+ * switches the step reads (hfConfig, :134-150; readHFConfig, :253-385). */
+typedef struct sr_model_desc {
+    int32_t vocab, dim, hidden, layers, heads, kv_heads, context;
+    double rope_theta, norm_eps;
+    int32_t tied;          /* 1: LM head is the token embedding (:6440-6443) */
+    int32_t qkv_bias;      /* 1: qwen2 q/k/v biases (:5022-5029) */
+    int32_t weight_format; /* SR_FMT_* */
+    int32_t page_tokens;   /* KV positions per page; the reference uses 32 (:5846) */
+    int32_t rope_scaling;  /* 1: llama3 frequency scaling (:4961-4977) */
+    double rope_factor, rope_low_freq_factor, rope_high_freq_factor;
+    int32_t rope_original_max_positions;
+} sr_model_desc;
+
+typedef struct sr_param_info {
+    int32_t rows, cols, format; /* SR_PARAM_* */
+    int32_t reserved;
+    int64_t value_bytes; /* f32: rows*cols*4; q8: rows*cols; q4: rows*ceil(cols/2) */
+    int64_t scale_count; /* q8/q4: rows*ceil(cols/64); f32: 0 */
+} sr_param_info;
+
+typedef struct sr_model sr_model;
+typedef struct sr_kvpool sr_kvpool;
+
+/* Ragged step batch, structure of arrays.  Session i owns step rows
+ * token_offsets[i] .. token_offsets[i+1]-1 (its chunk) starting at committed
+ * position pos[i] (KVCache.Pos), and pages page_ids[page_offsets[i] ..
+ * page_offsets[i+1]) in position order (KVCache.Pages).  want_logits may be
+ * NULL (all sessions).  Mirrors prefillSelected's arguments (caches, chunks,
+ * wantLogits), cmd/monolith/monolith.go:6245. */
+typedef struct sr_batch {
+    int32_t n_sessions;
+    const int32_t *pos;
+    const int32_t *token_offsets; /* n_sessions + 1 entries, [0] == 0 */
+    const int32_t *tokens;
+    const int32_t *page_offsets; /* n_sessions + 1 entries, [0] == 0 */
+    const int32_t *page_ids;
+    const uint8_t *want_logits;
+} sr_batch;
+
+/* Sampling settings per session: Sampling (cmd/monolith/monolith.go:7253-7260). */
+typedef struct sr_sampling {
+    double temperature; /* 0 = greedy */
+    int32_t top_k;      /* 0 = no top-k */
+    int32_t reserved;
+    double top_p;
+    double repeat_penalty;
+} sr_sampling;
+
+const char *sr_last_error(void);
+const char *sr_version(void);
+
+/* ---------------------------------------------------------------- model */
+/* Replaces loadHFModelFormatKV's storage allocation (:4985-5050).  Allocates
+ * device storage for every parameter in hfProfileSpecs order (:407-442), the
+ * RoPE tables (:5034-5043) and the step workspace (decodeWorkspace,
+ * :6064-6096; bounded by maxActivationElements, :50). */
+int sr_model_create(const sr_model_desc *desc, int device, sr_model **out);
+int sr_model_destroy(sr_model *m);
+int sr_model_param_count(const sr_model *m, int32_t *count);
+int sr_model_param_info(const sr_model *m, int32_t index, sr_param_info *out);
+/* Upload one parameter in the reference's storage layout, verbatim (Param,
+ * :3784-3850): f32 [rows,cols]; q8 int8 [rows,cols] + f32 scales
+ * [rows,ceil(cols/64)]; q4 packed nibbles (low first) [rows,ceil(cols/2)] +
+ * scales.  `values` and `scales` are host pointers. */
+int sr_model_load_param(sr_model *m, int32_t index, const void *values, size_t value_bytes, const float *scales,
+                        size_t scale_count);
+/* Upload one parameter as fp32 [rows,cols] and store it in the parameter's
+ * format, quantising on the device with the reference's streaming block
+ * quantizer (readParam, :857-880; lowBitScale, :3877-3891; q8Value, :3893).
+ * This is the path of loadHFModelFormatKV for f32/q8/q4/q4-mixed models. */
+int sr_model_load_param_f32(sr_model *m, int32_t index, const float *values, size_t count);
+/* Read one parameter back (same layout), for verification. */
+int sr_model_read_param(const sr_model *m, int32_t index, void *values, size_t value_bytes, float *scales,
+                        size_t scale_count);
+/* Synthetic random init on the device (no reference counterpart beyond
+ * NewModel(c, seed), :5195-5199): every matrix and bias element e, counted in
+ * hfProfileSpecs order, is float32(Normal()*scale) where Normal() uses the
+ * SplitMix64 outputs number 2e+1 and 2e+2 of a generator seeded with `seed`
+ * (RNG.Normal, :1437-1439); norms are 1; matrices are then quantized with the
+ * reference's block quantizer (readParam, :857-880). */
+int sr_model_init_synthetic(sr_model *m, uint64_t seed, double scale);
+/* Select SR_MODE_EXACT (default) or SR_MODE_FAST for subsequent steps. */
+int sr_model_set_mode(sr_model *m, int32_t mode);
+
+/* ---------------------------------------------------------------- KV pool */
+/* Device page pool holding num_pages pages of 2*page_tokens*kvDim*layers fp32
+ * values each; page layout [layer][K plane | V plane] (KVCache.row,
+ * :6038-6043).  Page ids are chosen by the caller (the engine's LIFO pagePool,
+ * :5854-5866, stays on the host). */
+int sr_kvpool_create(sr_model *m, int64_t num_pages, sr_kvpool **out);
+int sr_kvpool_destroy(sr_kvpool *p);
+/* Copy one K and one V row (kvDim floats each) of (page, layer, slot) to host. */
+int sr_kvpool_read_row(const sr_kvpool *p, int64_t page, int32_t layer, int32_t slot, float *k_out, float *v_out);
+/* Fill every page with deterministic pseudo-random values (benchmark state). */
+int sr_kvpool_fill_synthetic(sr_kvpool *p, uint64_t seed, float scale);
+
+/* ---------------------------------------------------------------- step */
+/* One engine step: replaces Model.prefillSelected (:6245-6456).  Validates the
+ * batch (1..256 sessions, >=1 token per chunk, <=1024 rows, tokens in
+ * [0,vocab), pos+len <= context, pages covering pos+len), then runs every layer
+ * and writes logits [n_sessions x vocab] fp32 (unselected rows zeroed) into the
+ * model's device buffer, borrowed until the next step (:6236-6237).
+ * logits_host may be NULL; when set, the logits are copied there.  cancel may
+ * be NULL; when *cancel becomes nonzero between layers the step stops with
+ * SR_ECANCELED (future KV rows may be written; positions are never committed
+ * here: the caller commits Pos += len on SR_OK, :6452-6454). */
+int sr_step(sr_model *m, sr_kvpool *pool, const sr_batch *batch, float *logits_host, const volatile int32_t *cancel);
+/* Device pointer of the last step's logits [n_sessions x vocab]. */
+int sr_step_logits(sr_model *m, const float **device_logits);
+
+/* Sample one token per session from the last step's logits on the device:
+ * sampleWithBlocked (:7320-7426) with the SplitMix64 RNG (:1411-1439).
+ * history: per session the prompt+output ids (history_offsets[n+1]).
+ * rng_state: per session, advanced exactly as RNG.Float64 does (one draw per
+ * sampled, non-greedy token).  blocked: id never sampled (-1 for HF models).
+ * Supports top_k in 1..256 or temperature 0; other settings return
+ * SR_EUNSUPPORTED.  ids_out[i] receives the token; a nonfinite logit or empty
+ * distribution returns SR_EINVAL naming the session. */
+int sr_sample(sr_model *m, int32_t n_sessions, const sr_sampling *settings, const int32_t *history_offsets,
+              const int32_t *history, uint64_t *rng_state, int32_t blocked, int32_t *ids_out);
+
+/* Step + sample in one call (one host round trip per engine tick). */
+int sr_step_sample(sr_model *m, sr_kvpool *pool, const sr_batch *batch, const sr_sampling *settings,
+                   const int32_t *history_offsets, const int32_t *history, uint64_t *rng_state, int32_t blocked,
+                   int32_t *ids_out);
+
+/* ---------------------------------------------------------------- profiling */
+/* Kernel classes timed with CUDA events on the model's stream (no reference
+ * counterpart; the reference traces regions with runtime/trace, :6380, :8392). */
+enum {
+    SR_PROF_META = 0, SR_PROF_EMBED, SR_PROF_NORM, SR_PROF_LINEAR, SR_PROF_ROPE_KV, SR_PROF_ATTENTION,
+    SR_PROF_SWIGLU, SR_PROF_HEAD, SR_PROF_SAMPLE, SR_PROF_CLASSES
+};
+/* Time every launch of the classes in class_mask (bit i = class i); 0 = off.
+ * Step spans (first to last kernel of each step) and launch counts are always
+ * recorded. */
+int sr_profile_set(sr_model *m, uint32_t class_mask);
+/* Accumulated milliseconds and launches per class (arrays of SR_PROF_CLASSES),
+ * summed step spans, step count and total kernel launches; reset clears them. */
+int sr_profile_read(sr_model *m, double *ms, int64_t *launches, double *span_ms, int64_t *steps,
+                    int64_t *total_launches, int32_t reset);
+/* The cudaStream_t every step of this model runs on (for external events). */
+int sr_model_stream(sr_model *m, void **stream);
+
+/* ---------------------------------------------------------------- host engine */
+/* C++ restatement of the reference's Engine actor loop (:7629-8476) over this
+ * step: request queue, page-reserving admission (:8325-8366), scheduleTokens
+ * (:8180-8210), the LIFO page pool (:5854-5866, :6023-6062), sampling and
+ * finishing.  Used where no Go engine drives the step (tests, benchmarks). */
+typedef struct sr_engine sr_engine;
+typedef struct sr_engine_config {
+    int32_t max_batch;           /* 1..256 */
+    int32_t token_budget;        /* max_batch..1024 */
+    int32_t prefill_chunk;       /* 1..1024 */
+    int32_t mixed_prefill_chunk; /* 1..1024 */
+    int64_t cache_bytes;         /* KV budget; pool Limit = cache_bytes / page bytes */
+    int32_t eos_id;              /* -1: no EOS */
+    int32_t blocked_id;          /* -1 for HF models */
+} sr_engine_config;
+typedef struct sr_request {
+    const int32_t *ids;
+    int32_t n_ids;
+    int32_t max_tokens;
+    sr_sampling sampling;
+    uint64_t seed;
+} sr_request;
+typedef struct sr_engine_stats {
+    int64_t submitted, completed, rejected, failed, active, queued;
+    int64_t input_tokens, generated_tokens, ticks, peak_tick_tokens;
+    int64_t pool_limit, pool_reserved, pool_allocated;
+} sr_engine_stats;
+
+int sr_engine_create(sr_model *m, const sr_engine_config *c, sr_engine **out);
+int sr_engine_destroy(sr_engine *e);
+/* Queue a request (enqueue, :8071-8148).  Returns SR_EINVAL if it can never fit
+ * the pool ("request exceeds total KV cache budget", :8097-8100). */
+int sr_engine_submit(sr_engine *e, const sr_request *r, int64_t *request_id);
+/* Run one actor tick (admit, schedule, step, sample, finish).  *rows receives
+ * the step's row count (0 when idle). */
+int sr_engine_tick(sr_engine *e, int32_t *rows);
+/* Pop one finished request: ids and count (up to cap), finish reason
+ * (0 length, 1 eos, 2 error, 3 rejected/busy).  Returns SR_OK with
+ * *request_id = -1 when none is finished. */
+int sr_engine_poll(sr_engine *e, int64_t *request_id, int32_t *out_ids, int32_t cap, int32_t *n_out,
+                   int32_t *reason);
+int sr_engine_stats_get(const sr_engine *e, sr_engine_stats *s);
+/* Last tick's schedule: counts[i] rows for session i (up to cap), pages owned. */
+int sr_engine_last_schedule(const sr_engine *e, int32_t *counts, int32_t cap, int32_t *n_sessions);
+/* Page table of active session i in admission order (up to cap ids). */
+int sr_engine_session_pages(const sr_engine *e, int32_t i, int32_t *pages, int32_t cap, int32_t *n_pages);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,341 @@
+// engine.cu -- host-side restatement of the reference's Engine actor
+// (cmd/monolith/monolith.go:7629-8476, "M:line") over the device step.
+//
+// The Go engine keeps its own loop and calls sr_step / sr_sample through cgo;
+// this C++ engine reproduces that loop's integer decisions (admission, page
+// reservation, scheduleTokens, the LIFO page pool, finishing) for callers that
+// have no Go runtime (tests, benchmarks).  HTTP, SSE streaming, tokenisation,
+// prefix caching and cancellation watchers are outside this restatement.
+#include <algorithm>
+#include <deque>
+#include <string>
+#include <vector>
+
+#include "../../include/srstep.h"
+#include "srstep_internal.h"
+
+namespace {
+
+struct EngRequest {
+  int64_t id;
+  std::vector<int32_t> ids;
+  int32_t max_tokens;
+  sr_sampling s;
+  uint64_t seed;
+};
+
+struct EngSession {
+  EngRequest req;
+  std::vector<int32_t> pages;  // KVCache.Pages (page ids)
+  int32_t reserved = 0;        // KVCache.reserved
+  int32_t pos = 0;             // KVCache.Pos
+  int32_t cursor = 0;          // engineSession.Cursor
+  std::vector<int32_t> output, history;
+  uint64_t rng = 0;            // engineSession.RNG
+};
+
+struct Finished {
+  int64_t id;
+  std::vector<int32_t> out;
+  int32_t reason;  // 0 length, 1 eos, 2 error, 3 busy
+};
+
+}  // namespace
+
+struct sr_engine {
+  sr_model* m = nullptr;
+  sr_kvpool* pool = nullptr;
+  sr_engine_config c;
+  // pagePool (M:5849-5866): Limit, Reserved, Allocated and the LIFO free list.
+  int64_t limit = 0, reserved = 0, allocated = 0;
+  std::vector<int32_t> free_pages;
+  std::deque<EngRequest> queue;
+  std::vector<EngSession> sessions;
+  int32_t rotation = 0;
+  int64_t next_id = 0;
+  std::deque<Finished> finished;
+  sr_engine_stats st{};
+  std::vector<int32_t> last_counts;
+  // per-tick scratch
+  std::vector<int32_t> pos, toff, tokens, poff, pids, counts, hoff, hist, ids_out;
+  std::vector<uint8_t> want;
+  std::vector<sr_sampling> settings;
+  std::vector<uint64_t> rng;
+};
+
+// pagePool.acquire (M:5854-5866): pop the tail of the free list, else allocate.
+static int32_t acquire(sr_engine* e) {
+  if (!e->free_pages.empty()) {
+    int32_t p = e->free_pages.back();
+    e->free_pages.pop_back();
+    return p;
+  }
+  return (int32_t)(e->allocated++);
+}
+
+// KVCache.Close (M:6044-6062): pages return to the free list in page order.
+static void close_session(sr_engine* e, EngSession& s) {
+  e->free_pages.insert(e->free_pages.end(), s.pages.begin(), s.pages.end());
+  e->reserved -= s.reserved;
+  s.pages.clear();
+}
+
+static void finish(sr_engine* e, EngSession& s, int32_t reason) {
+  close_session(e, s);
+  e->st.active--;
+  if (reason <= 1) e->st.completed++;
+  else e->st.failed++;
+  e->finished.push_back(Finished{s.req.id, s.output, reason});
+}
+
+// scheduleTokens (M:8180-8210).
+static int32_t schedule_tokens(const std::vector<EngSession>& ss, std::vector<int32_t>& counts, int32_t budget,
+                               int32_t chunk, int32_t mixed_chunk, int32_t start) {
+  const int32_t n = (int32_t)ss.size();
+  for (const auto& s : ss)
+    if (s.cursor == (int32_t)s.req.ids.size()) {
+      chunk = std::min(chunk, mixed_chunk);
+      break;
+    }
+  int32_t total = n;
+  counts.assign(n, 1);
+  while (total < budget) {
+    bool progress = false;
+    for (int32_t j = 0; j < n; j++) {
+      int32_t i = (start + j) % n;
+      int32_t remaining = (int32_t)ss[i].req.ids.size() - ss[i].cursor;
+      if (counts[i] < std::min(chunk, remaining)) {
+        counts[i]++;
+        total++;
+        progress = true;
+        if (total == budget) break;
+      }
+    }
+    if (!progress) break;
+  }
+  return total;
+}
+
+extern "C" int sr_engine_create(sr_model* m, const sr_engine_config* cfg, sr_engine** out) {
+  if (!m || !cfg || !out) return sr_fail(SR_EINVAL, "null argument");
+  *out = nullptr;
+  sr_engine_config c = *cfg;
+  // normalizeEngineConfig (M:7983-8012).
+  if (c.prefill_chunk == 0) c.prefill_chunk = 16;
+  if (c.mixed_prefill_chunk == 0) c.mixed_prefill_chunk = 1;
+  if (c.token_budget == 0) c.token_budget = std::max(c.max_batch, 64);
+  if (c.max_batch < 1 || c.max_batch > 256 || c.cache_bytes < 1 || c.prefill_chunk < 1 || c.prefill_chunk > 1024 ||
+      c.mixed_prefill_chunk < 1 || c.mixed_prefill_chunk > 1024 || c.token_budget < c.max_batch ||
+      c.token_budget > 1024)
+    return sr_fail(SR_EINVAL, "invalid engine capacity or token budget");
+  const int64_t page_bytes = m->dm.page_elems * 4;
+  const int64_t limit = c.cache_bytes / page_bytes;  // newEngine (M:8031-8035)
+  if (limit < 1) return sr_fail(SR_EINVAL, "cache budget cannot hold one KV page");
+  sr_engine* e = new sr_engine();
+  e->m = m;
+  e->c = c;
+  e->limit = limit;
+  int rc = sr_kvpool_create(m, limit, &e->pool);
+  if (rc != SR_OK) {
+    delete e;
+    return rc;
+  }
+  e->st.pool_limit = limit;
+  *out = e;
+  return SR_OK;
+}
+
+extern "C" int sr_engine_destroy(sr_engine* e) {
+  if (!e) return sr_fail(SR_EINVAL, "null engine");
+  if (e->pool) sr_kvpool_destroy(e->pool);
+  delete e;
+  return SR_OK;
+}
+
+extern "C" int sr_engine_submit(sr_engine* e, const sr_request* r, int64_t* request_id) {
+  if (!e || !r || !request_id) return sr_fail(SR_EINVAL, "null argument");
+  if (r->n_ids < 1 || !r->ids) return sr_fail(SR_EINVAL, "empty prompt");
+  const sr_model_desc& d = e->m->d;
+  // prepareInput's bounds (M:7466-7497): ids in vocabulary, prompt+max_tokens <= context.
+  if (r->max_tokens < 1 || r->max_tokens > d.context || (int64_t)r->n_ids + r->max_tokens > d.context)
+    return sr_fail(SR_EINVAL, "prompt plus max_tokens exceeds the model context");
+  for (int32_t i = 0; i < r->n_ids; i++)
+    if (r->ids[i] < 0 || r->ids[i] >= d.vocab) return sr_fail(SR_EINVAL, "token outside vocabulary");
+  const int64_t pt = d.page_tokens;
+  const int64_t pages = ((int64_t)r->n_ids + r->max_tokens + pt - 1) / pt;
+  if (pages > e->limit) return sr_fail(SR_EINVAL, "request exceeds total KV cache budget");  // M:8097-8100
+  EngRequest q;
+  q.id = e->next_id++;
+  q.ids.assign(r->ids, r->ids + r->n_ids);
+  q.max_tokens = r->max_tokens;
+  q.s = r->sampling;
+  q.seed = r->seed;
+  e->queue.push_back(std::move(q));
+  e->st.submitted++;
+  *request_id = e->next_id - 1;
+  return SR_OK;
+}
+
+extern "C" int sr_engine_tick(sr_engine* e, int32_t* rows) {
+  if (!e || !rows) return sr_fail(SR_EINVAL, "null argument");
+  *rows = 0;
+  const int64_t pt = e->m->d.page_tokens;
+  // Admission (M:8325-8366): reserve whole pages for prompt + max_tokens.
+  while ((int)e->sessions.size() < e->c.max_batch && !e->queue.empty()) {
+    EngRequest r = std::move(e->queue.front());
+    e->queue.pop_front();
+    const int64_t pages = ((int64_t)r.ids.size() + r.max_tokens + pt - 1) / pt;
+    if (e->reserved + pages > e->limit) {
+      e->st.rejected++;
+      e->finished.push_back(Finished{r.id, {}, 3});
+      continue;
+    }
+    EngSession s;
+    s.reserved = (int32_t)pages;
+    e->reserved += pages;
+    s.history = r.ids;
+    s.rng = r.seed;  // RNG{r.Sampling.Seed}
+    s.req = std::move(r);
+    e->sessions.push_back(std::move(s));
+    e->st.active++;
+  }
+  e->st.queued = (int64_t)e->queue.size();
+  if (e->sessions.empty()) return SR_OK;
+  const int32_t n = (int32_t)e->sessions.size();
+  const int32_t total = schedule_tokens(e->sessions, e->counts, e->c.token_budget, e->c.prefill_chunk,
+                                        e->c.mixed_prefill_chunk, e->rotation % n);
+  e->rotation = (e->rotation + 1) % n;
+  e->last_counts = e->counts;
+  // Build the ragged batch: chunks, wantLogits, lazily acquired pages (M:8372-8381, 6362-6364).
+  e->pos.assign(n, 0);
+  e->toff.assign(n + 1, 0);
+  e->poff.assign(n + 1, 0);
+  e->want.assign(n, 0);
+  e->tokens.clear();
+  e->pids.clear();
+  e->hoff.assign(n + 1, 0);
+  e->hist.clear();
+  e->settings.resize(n);
+  e->rng.resize(n);
+  e->ids_out.assign(n, -1);
+  for (int32_t i = 0; i < n; i++) {
+    EngSession& s = e->sessions[i];
+    const int32_t plen = (int32_t)s.req.ids.size();
+    e->want[i] = (s.cursor + e->counts[i] >= plen) ? 1 : 0;
+    if (s.cursor < plen)
+      e->tokens.insert(e->tokens.end(), s.req.ids.begin() + s.cursor, s.req.ids.begin() + s.cursor + e->counts[i]);
+    else
+      e->tokens.push_back(s.output.back());
+    e->toff[i + 1] = (int32_t)e->tokens.size();
+    const int32_t len = e->toff[i + 1] - e->toff[i];
+    const int64_t needed = ((int64_t)s.pos + len + pt - 1) / pt;  // ensurePages (M:6023-6037)
+    while ((int64_t)s.pages.size() < needed) s.pages.push_back(acquire(e));
+    e->pos[i] = s.pos;
+    e->pids.insert(e->pids.end(), s.pages.begin(), s.pages.end());
+    e->poff[i + 1] = (int32_t)e->pids.size();
+    if (e->want[i]) e->hist.insert(e->hist.end(), s.history.begin(), s.history.end());
+    e->hoff[i + 1] = (int32_t)e->hist.size();
+    e->settings[i] = s.req.s;
+    e->rng[i] = s.rng;
+  }
+  sr_batch b;
+  b.n_sessions = n;
+  b.pos = e->pos.data();
+  b.token_offsets = e->toff.data();
+  b.tokens = e->tokens.data();
+  b.page_offsets = e->poff.data();
+  b.page_ids = e->pids.data();
+  b.want_logits = e->want.data();
+  *rows = total;
+  e->st.ticks++;
+  e->st.peak_tick_tokens = std::max<int64_t>(e->st.peak_tick_tokens, total);
+  int rc = sr_step_sample(e->m, e->pool, &b, e->settings.data(), e->hoff.data(), e->hist.data(), e->rng.data(),
+                          e->c.blocked_id, e->ids_out.data());
+  if (rc != SR_OK) {
+    // A failed step finishes every active session with the error (M:8409-8418).
+    std::string msg = sr_last_error();
+    for (auto& s : e->sessions) finish(e, s, 2);
+    e->sessions.clear();
+    e->st.pool_reserved = e->reserved;
+    e->st.pool_allocated = e->allocated;
+    sr_fail(rc, msg);
+    return rc;
+  }
+  // Commit positions (M:6452-6454), advance cursors, sample, finish (M:8419-8474).
+  std::vector<EngSession> alive;
+  alive.reserve(n);
+  for (int32_t i = 0; i < n; i++) {
+    EngSession& s = e->sessions[i];
+    s.pos += e->toff[i + 1] - e->toff[i];
+    const int32_t plen = (int32_t)s.req.ids.size();
+    if (s.cursor < plen) {
+      s.cursor += e->counts[i];
+      e->st.input_tokens += e->counts[i];
+    }
+    if (s.cursor < plen) {
+      alive.push_back(std::move(s));
+      continue;
+    }
+    const int32_t id = e->ids_out[i];
+    s.rng = e->rng[i];
+    e->st.generated_tokens++;
+    s.output.push_back(id);
+    s.history.push_back(id);
+    int32_t reason = -1;
+    if (e->c.eos_id >= 0 && id == e->c.eos_id) reason = 1;
+    else if ((int32_t)s.output.size() == s.req.max_tokens) reason = 0;
+    if (reason >= 0) finish(e, s, reason);
+    else alive.push_back(std::move(s));
+  }
+  e->sessions = std::move(alive);
+  e->st.pool_reserved = e->reserved;
+  e->st.pool_allocated = e->allocated;
+  return SR_OK;
+}
+
+extern "C" int sr_engine_poll(sr_engine* e, int64_t* request_id, int32_t* out_ids, int32_t cap, int32_t* n_out,
+                              int32_t* reason) {
+  if (!e || !request_id || !n_out || !reason) return sr_fail(SR_EINVAL, "null argument");
+  if (e->finished.empty()) {
+    *request_id = -1;
+    *n_out = 0;
+    *reason = -1;
+    return SR_OK;
+  }
+  Finished f = std::move(e->finished.front());
+  e->finished.pop_front();
+  *request_id = f.id;
+  *reason = f.reason;
+  *n_out = (int32_t)f.out.size();
+  if (out_ids) std::copy(f.out.begin(), f.out.begin() + std::min<size_t>(f.out.size(), (size_t)std::max(cap, 0)), out_ids);
+  return SR_OK;
+}
+
+extern "C" int sr_engine_stats_get(const sr_engine* e, sr_engine_stats* s) {
+  if (!e || !s) return sr_fail(SR_EINVAL, "null argument");
+  *s = e->st;
+  s->active = (int64_t)e->sessions.size();
+  s->queued = (int64_t)e->queue.size();
+  s->pool_limit = e->limit;
+  s->pool_reserved = e->reserved;
+  s->pool_allocated = e->allocated;
+  return SR_OK;
+}
+
+extern "C" int sr_engine_last_schedule(const sr_engine* e, int32_t* counts, int32_t cap, int32_t* n_sessions) {
+  if (!e || !n_sessions) return sr_fail(SR_EINVAL, "null argument");
+  *n_sessions = (int32_t)e->last_counts.size();
+  if (counts)
+    std::copy(e->last_counts.begin(),
+              e->last_counts.begin() + std::min<size_t>(e->last_counts.size(), (size_t)std::max(cap, 0)), counts);
+  return SR_OK;
+}
+
+extern "C" int sr_engine_session_pages(const sr_engine* e, int32_t i, int32_t* pages, int32_t cap, int32_t* n_pages) {
+  if (!e || !n_pages) return sr_fail(SR_EINVAL, "null argument");
+  if (i < 0 || i >= (int32_t)e->sessions.size()) return sr_fail(SR_EINVAL, "session index out of range");
+  const auto& p = e->sessions[i].pages;
+  *n_pages = (int32_t)p.size();
+  if (pages) std::copy(p.begin(), p.begin() + std::min<size_t>(p.size(), (size_t)std::max(cap, 0)), pages);
+  return SR_OK;
+}

@@ -1,0 +1,917 @@
+// srstep.cu -- C ABI of the engine step (include/srstep.h): model storage,
+// KV page pool, step orchestration and the device sampler entry points.
+//
+// Reference: RyoSpiralArchitect/sr_go_tranformer cmd/monolith/monolith.go (M:line).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/srstep.h"
+#include "common.cuh"
+#include "exact_kernels.cuh"
+#include "fast_kernels.cuh"
+#include "sampler.cuh"
+#include "srstep_internal.h"
+
+using namespace sr;
+
+// ------------------------------------------------------------------ errors --
+static thread_local std::string g_err;
+int sr_fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+extern "C" const char* sr_last_error(void) { return g_err.c_str(); }
+extern "C" const char* sr_version(void) { return "srstep 0.1 sm_100a"; }
+
+#define CK(call)                                                                            \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess) return sr_fail(SR_EDEVICE, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+// ------------------------------------------------------------------- model --
+static int64_t param_value_bytes(int rows, int cols, int fmt) {
+  if (fmt == kQ8) return (int64_t)rows * cols;
+  if (fmt == kQ4) return (int64_t)rows * ((cols + 1) / 2);
+  return (int64_t)rows * cols * 4;
+}
+static int64_t param_scale_count(int rows, int cols, int fmt) {
+  return fmt == kF32 ? 0 : (int64_t)rows * ((cols + kQBlock - 1) / kQBlock);
+}
+static int matrix_format(int model_fmt, bool embed_or_head) {
+  switch (model_fmt) {
+    case SR_FMT_Q8: return kQ8;
+    case SR_FMT_Q4: return kQ4;
+    case SR_FMT_Q4_MIXED: return embed_or_head ? kQ8 : kQ4;  // hfMatrixFormat (M:572-582)
+    default: return kF32;
+  }
+}
+
+// hfInverseFrequency (M:4961-4977), evaluated on the host at load time.
+static float hf_inverse_frequency(const sr_model_desc& c, int hd, int index) {
+  float inv = 1.0f / (float)std::pow(c.rope_theta, (double)((float)(2 * index) / (float)hd));
+  if (!c.rope_scaling) return inv;
+  volatile float two_pi = (float)(2 * M_PI);
+  float wave = two_pi / inv;
+  float low_wave = (float)((double)c.rope_original_max_positions / c.rope_low_freq_factor);
+  float high_wave = (float)((double)c.rope_original_max_positions / c.rope_high_freq_factor);
+  float factor = (float)c.rope_factor;
+  if (wave > low_wave) return inv / factor;
+  if (wave >= high_wave) {
+    volatile float smooth = ((float)c.rope_original_max_positions / wave - (float)c.rope_low_freq_factor) /
+                            (float)(c.rope_high_freq_factor - c.rope_low_freq_factor);
+    volatile float t1 = (1 - smooth) * inv;
+    volatile float t2 = t1 / factor;
+    volatile float t3 = smooth * inv;
+    return t2 + t3;
+  }
+  return inv;
+}
+
+static void free_model(sr_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->h_stage) cudaFreeHost(m->h_stage);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  for (auto& f : m->fast_free) f();
+  delete m;
+}
+
+int sr_model_alloc(sr_model* m, void** p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return sr_fail(SR_ENOMEM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+  }
+  m->allocs.push_back(*p);
+  return SR_OK;
+}
+
+extern "C" int sr_model_create(const sr_model_desc* desc, int device, sr_model** out) {
+  if (!desc || !out) return sr_fail(SR_EINVAL, "null argument");
+  *out = nullptr;
+  const sr_model_desc& c = *desc;
+  // Config.validateShapeLimits (M:98-118) plus this implementation's limits.
+  if (c.vocab < 1 || c.vocab > 262144 || c.dim < 2 || c.dim > 8192 || c.hidden < 1 || c.hidden > 32768 ||
+      c.layers < 1 || c.layers > 128 || c.heads < 1 || c.heads > c.dim || c.kv_heads < 1 || c.kv_heads > c.heads ||
+      c.context < 1 || c.context > 32768)
+    return sr_fail(SR_EINVAL, "invalid model dimensions");
+  if (c.dim % c.heads || c.heads % c.kv_heads || (c.dim / c.heads) % 2)
+    return sr_fail(SR_EINVAL, "dim must be divisible by heads with an even head dimension; heads must be divisible by kv_heads");
+  if (!std::isfinite(c.rope_theta) || c.rope_theta <= 1 || !std::isfinite(c.norm_eps) || c.norm_eps < 1e-12 ||
+      c.norm_eps > 1)
+    return sr_fail(SR_EINVAL, "invalid RoPE theta or RMS epsilon");
+  if (c.weight_format < SR_FMT_F32 || c.weight_format > SR_FMT_Q4_MIXED) return sr_fail(SR_EINVAL, "invalid weight format");
+  if (c.page_tokens < 1 || c.page_tokens > 1024) return sr_fail(SR_EINVAL, "page_tokens must be 1..1024");
+  const int hd = c.dim / c.heads, group = c.heads / c.kv_heads;
+  if (hd % 4) return sr_fail(SR_EUNSUPPORTED, "head_dim must be a multiple of 4 on this device path");
+  if (group * hd / 4 > 1024) return sr_fail(SR_EUNSUPPORTED, "query heads per KV head x head_dim exceeds 4096");
+  if (c.rope_scaling && (c.rope_low_freq_factor <= 0 || c.rope_high_freq_factor <= c.rope_low_freq_factor))
+    return sr_fail(SR_EINVAL, "invalid llama3 rope scaling");
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return sr_fail(SR_EINVAL, "invalid device ordinal");
+  CK(cudaSetDevice(device));
+
+  sr_model* m = new sr_model();
+  m->d = c;
+  m->device = device;
+  m->mode = SR_MODE_EXACT;
+  ModelDims& dm = m->dm;
+  dm.vocab = c.vocab;
+  dm.dim = c.dim;
+  dm.hidden = c.hidden;
+  dm.layers = c.layers;
+  dm.heads = c.heads;
+  dm.kv_heads = c.kv_heads;
+  dm.context = c.context;
+  dm.hd = hd;
+  dm.kvd = hd * c.kv_heads;
+  dm.group = group;
+  dm.page_tokens = c.page_tokens;
+  dm.page_elems = 2LL * c.page_tokens * dm.kvd * c.layers;
+
+  // Parameter table in hfProfileSpecs order (M:407-442).
+  auto add = [&](int rows, int cols, bool matrix, bool eh) {
+    Param p;
+    p.rows = rows;
+    p.cols = cols;
+    p.format = matrix ? matrix_format(c.weight_format, eh) : kF32;
+    p.values = nullptr;
+    p.scales = nullptr;
+    m->params.push_back(p);
+  };
+  const int L = c.layers, d = c.dim, kd = dm.kvd, h = c.hidden;
+  add(c.vocab, d, true, true);
+  for (int l = 0; l < L; l++) {
+    add(1, d, false, false);
+    add(d, d, true, false);
+    add(kd, d, true, false);
+    add(kd, d, true, false);
+    add(d, d, true, false);
+    add(1, d, false, false);
+    add(h, d, true, false);
+    add(h, d, true, false);
+    add(d, h, true, false);
+  }
+  add(1, d, false, false);
+  if (c.qkv_bias)
+    for (int l = 0; l < L; l++) {
+      add(1, d, false, false);
+      add(1, kd, false, false);
+      add(1, kd, false, false);
+    }
+  if (!c.tied) add(c.vocab, d, true, true);
+
+  int rc;
+  for (auto& p : m->params) {
+    int64_t vb = param_value_bytes(p.rows, p.cols, p.format);
+    int64_t sc = param_scale_count(p.rows, p.cols, p.format);
+    if ((rc = sr_model_alloc(m, &p.values, (size_t)vb)) != SR_OK) { free_model(m); return rc; }
+    if (sc && (rc = sr_model_alloc(m, (void**)&p.scales, (size_t)sc * 4)) != SR_OK) { free_model(m); return rc; }
+    cudaMemset(p.values, 0, (size_t)vb);
+    if (sc) cudaMemset(p.scales, 0, (size_t)sc * 4);
+  }
+  // HF RoPE tables (M:5034-5043).
+  {
+    const int half = hd / 2;
+    std::vector<float> cs((size_t)c.context * half), sn((size_t)c.context * half);
+    std::vector<float> inv(half);
+    for (int j = 0; j < half; j++) inv[j] = hf_inverse_frequency(c, hd, j);
+    for (int pos = 0; pos < c.context; pos++)
+      for (int j = 0; j < half; j++) {
+        volatile float prod = (float)pos * inv[j];
+        double angle = (double)prod;
+        cs[(size_t)pos * half + j] = (float)std::cos(angle);
+        sn[(size_t)pos * half + j] = (float)std::sin(angle);
+      }
+    if ((rc = sr_model_alloc(m, (void**)&m->cos_t, cs.size() * 4)) != SR_OK ||
+        (rc = sr_model_alloc(m, (void**)&m->sin_t, sn.size() * 4)) != SR_OK) {
+      free_model(m);
+      return rc;
+    }
+    cudaMemcpy(m->cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+  }
+  // Step workspace (decodeWorkspace, M:6064-6096) at the 1024-row bound.
+  {
+    const int64_t R = kMaxRows;
+    float** bufs[] = {&m->X, &m->N, &m->Q, &m->A, &m->T};
+    for (float** b : bufs)
+      if ((rc = sr_model_alloc(m, (void**)b, (size_t)(R * d * 4))) != SR_OK) { free_model(m); return rc; }
+    if ((rc = sr_model_alloc(m, (void**)&m->K, (size_t)(R * kd * 4))) != SR_OK ||
+        (rc = sr_model_alloc(m, (void**)&m->V, (size_t)(R * kd * 4))) != SR_OK ||
+        (rc = sr_model_alloc(m, (void**)&m->G, (size_t)(R * h * 4))) != SR_OK ||
+        (rc = sr_model_alloc(m, (void**)&m->U, (size_t)(R * h * 4))) != SR_OK ||
+        (rc = sr_model_alloc(m, (void**)&m->H, (size_t)(R * h * 4))) != SR_OK ||
+        (rc = sr_model_alloc(m, (void**)&m->logits, (size_t)kMaxSessions * c.vocab * 4)) != SR_OK) {
+      free_model(m);
+      return rc;
+    }
+  }
+  // Metadata: upload region (host-staged) followed by the device-built region.
+  m->max_pages_per_session = (c.context + c.page_tokens - 1) / c.page_tokens;
+  m->page_cap = (int64_t)kMaxSessions * m->max_pages_per_session;
+  m->upload_ints = kMetaHeader + m->page_cap;
+  const int64_t meta_ints = m->upload_ints + kMetaComputed;
+  if ((rc = sr_model_alloc(m, (void**)&m->meta_dev, (size_t)meta_ints * 4)) != SR_OK) { free_model(m); return rc; }
+  if (cudaMallocHost(&m->h_stage, (size_t)(m->upload_ints * 4 + kSampleStageBytes)) != cudaSuccess) {
+    cudaGetLastError();
+    free_model(m);
+    return sr_fail(SR_ENOMEM, "cudaMallocHost for the batch staging buffer failed");
+  }
+  {
+    int32_t* b = m->meta_dev;
+    StepMeta& s = m->meta;
+    s.sess_pos = b + kOffSessPos;
+    s.tok_off = b + kOffTokOff;
+    s.page_off = b + kOffPageOff;
+    s.want = (uint8_t*)(b + kOffWant);
+    s.tokens = b + kOffTokens;
+    s.page_ids = b + kMetaHeader;
+    int32_t* cbase = b + m->upload_ints;
+    s.row_pos = cbase;
+    s.row_pbase = cbase + kMaxRows;
+    s.head_src = cbase + 2 * kMaxRows;
+    s.head_dst = cbase + 2 * kMaxRows + kMaxSessions;
+    s.n_heads = cbase + 2 * kMaxRows + 2 * kMaxSessions;
+  }
+  // Sampler device buffers.
+  {
+    static_assert(sizeof(SampleSetting) == 32, "sampler settings layout");
+    if ((rc = sr_model_alloc(m, (void**)&m->samp_dev, kSampleStageBytes)) != SR_OK) { free_model(m); return rc; }
+  }
+  if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    free_model(m);
+    return sr_fail(SR_EDEVICE, "cudaStreamCreate failed");
+  }
+  cudaFuncSetAttribute(k_attention_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+  if ((rc = fast_init(m)) != SR_OK) { free_model(m); return rc; }
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    free_model(m);
+    return sr_fail(SR_EDEVICE, std::string("model init: ") + cudaGetErrorString(e));
+  }
+  *out = m;
+  return SR_OK;
+}
+
+extern "C" int sr_model_destroy(sr_model* m) {
+  if (!m) return sr_fail(SR_EINVAL, "null model");
+  free_model(m);
+  return SR_OK;
+}
+extern "C" int sr_model_param_count(const sr_model* m, int32_t* count) {
+  if (!m || !count) return sr_fail(SR_EINVAL, "null argument");
+  *count = (int32_t)m->params.size();
+  return SR_OK;
+}
+extern "C" int sr_model_param_info(const sr_model* m, int32_t index, sr_param_info* out) {
+  if (!m || !out) return sr_fail(SR_EINVAL, "null argument");
+  if (index < 0 || index >= (int32_t)m->params.size()) return sr_fail(SR_EINVAL, "parameter index out of range");
+  const Param& p = m->params[index];
+  out->rows = p.rows;
+  out->cols = p.cols;
+  out->format = p.format;
+  out->reserved = 0;
+  out->value_bytes = param_value_bytes(p.rows, p.cols, p.format);
+  out->scale_count = param_scale_count(p.rows, p.cols, p.format);
+  return SR_OK;
+}
+extern "C" int sr_model_load_param(sr_model* m, int32_t index, const void* values, size_t value_bytes,
+                                   const float* scales, size_t scale_count) {
+  if (!m || !values) return sr_fail(SR_EINVAL, "null argument");
+  if (index < 0 || index >= (int32_t)m->params.size()) return sr_fail(SR_EINVAL, "parameter index out of range");
+  Param& p = m->params[index];
+  int64_t vb = param_value_bytes(p.rows, p.cols, p.format), sc = param_scale_count(p.rows, p.cols, p.format);
+  if ((int64_t)value_bytes != vb) return sr_fail(SR_EINVAL, "value byte count does not match the parameter layout");
+  if ((int64_t)scale_count != sc || (sc && !scales)) return sr_fail(SR_EINVAL, "scale count does not match the parameter layout");
+  CK(cudaSetDevice(m->device));
+  CK(cudaMemcpy(p.values, values, (size_t)vb, cudaMemcpyHostToDevice));
+  if (sc) CK(cudaMemcpy(p.scales, scales, (size_t)sc * 4, cudaMemcpyHostToDevice));
+  m->weights_version++;
+  return SR_OK;
+}
+extern "C" int sr_model_read_param(const sr_model* m, int32_t index, void* values, size_t value_bytes, float* scales,
+                                   size_t scale_count) {
+  if (!m || !values) return sr_fail(SR_EINVAL, "null argument");
+  if (index < 0 || index >= (int32_t)m->params.size()) return sr_fail(SR_EINVAL, "parameter index out of range");
+  const Param& p = m->params[index];
+  int64_t vb = param_value_bytes(p.rows, p.cols, p.format), sc = param_scale_count(p.rows, p.cols, p.format);
+  if ((int64_t)value_bytes != vb) return sr_fail(SR_EINVAL, "value byte count does not match the parameter layout");
+  if ((int64_t)scale_count != sc || (sc && !scales)) return sr_fail(SR_EINVAL, "scale count does not match the parameter layout");
+  CK(cudaSetDevice(m->device));
+  CK(cudaMemcpy(values, p.values, (size_t)vb, cudaMemcpyDeviceToHost));
+  if (sc) CK(cudaMemcpy(scales, p.scales, (size_t)sc * 4, cudaMemcpyDeviceToHost));
+  return SR_OK;
+}
+
+// ------------------------------------------------------------ synthetic init --
+// Counter-based SplitMix64: the k-th output (1-based) of a generator seeded with
+// `seed` is mix(seed + k*gamma), so element e (two draws per Normal) can be
+// generated independently of every other element.
+__device__ __forceinline__ uint64_t splitmix_at(uint64_t seed, uint64_t k) {
+  uint64_t z = seed + k * 0x9e3779b97f4a7c15ULL;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ float synth_value(uint64_t seed, uint64_t e, double scale) {
+  double u1 = (double)(splitmix_at(seed, 2 * e + 1) >> 11) * (1.0 / 9007199254740992.0);
+  double u2 = (double)(splitmix_at(seed, 2 * e + 2) >> 11) * (1.0 / 9007199254740992.0);
+  double nrm = sqrt(__dmul_rn(-2.0, log(__dsub_rn(1.0, u1)))) * cos(__dmul_rn(2 * M_PI, u2));
+  return (float)__dmul_rn(nrm, scale);
+}
+// One thread per (row, 64-column block): generate, then quantize with the
+// reference's block quantizer (readParam M:857-880, lowBitScale M:3877-3891).
+__global__ void k_init_param(Param p, uint64_t seed, uint64_t e0, double scale, int norm, const float* src) {
+  const int64_t groups = (p.cols + kQBlock - 1) / kQBlock;
+  const int64_t total = (int64_t)p.rows * groups;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = t / groups, g = t % groups;
+    const int j0 = (int)(g * kQBlock), j1 = min(j0 + kQBlock, p.cols);
+    float v[kQBlock];
+    float amax = 0.f;
+    for (int j = j0; j < j1; j++) {
+      float x = src ? src[row * p.cols + j] : (norm ? 1.0f : synth_value(seed, e0 + (uint64_t)(row * p.cols + j), scale));
+      v[j - j0] = x;
+      amax = fmaxf(amax, fabsf(x));
+    }
+    if (p.format == kF32) {
+      for (int j = j0; j < j1; j++) ((float*)p.values)[row * p.cols + j] = v[j - j0];
+      continue;
+    }
+    const double levels = p.format == kQ4 ? 7.0 : 127.0;
+    float sc = 0.f;
+    if (amax != 0.f) {
+      sc = (float)__ddiv_rn((double)amax, levels);
+      if (sc == 0.f) {
+        sc = 1.40129846e-45f;
+      } else if (sc > 1.40129846e-45f && __dmul_rn((double)sc, levels) > (double)amax) {
+        sc = nextafterf(sc, 0.f);
+      }
+    }
+    p.scales[row * groups + g] = sc;
+    for (int j = j0; j < j1; j++) {
+      double q = 0.0;
+      if (sc != 0.f) q = fmin(levels, fmax(-levels, round(__ddiv_rn((double)v[j - j0], (double)sc))));
+      if (p.format == kQ8) {
+        ((int8_t*)p.values)[row * p.cols + j] = (int8_t)q;
+      } else {
+        uint8_t* b = (uint8_t*)p.values + row * ((p.cols + 1) / 2) + j / 2;
+        uint8_t nib = (uint8_t)((int)q & 15);
+        // Each thread owns whole 64-column blocks, i.e. whole bytes.
+        *b = (j & 1) ? (uint8_t)((*b & 0x0f) | (nib << 4)) : (uint8_t)((*b & 0xf0) | nib);
+      }
+    }
+  }
+}
+
+extern "C" int sr_model_init_synthetic(sr_model* m, uint64_t seed, double scale) {
+  if (!m) return sr_fail(SR_EINVAL, "null model");
+  CK(cudaSetDevice(m->device));
+  const int L = m->d.layers;
+  uint64_t e0 = 0;
+  for (size_t i = 0; i < m->params.size(); i++) {
+    Param& p = m->params[i];
+    bool norm = (i >= 1 && i < (size_t)(1 + 9 * L) && ((i - 1) % 9 == 0 || (i - 1) % 9 == 5)) || i == (size_t)(1 + 9 * L);
+    if (p.format == kQ4) CK(cudaMemsetAsync(p.values, 0, (size_t)param_value_bytes(p.rows, p.cols, p.format), m->stream));
+    int64_t work = (int64_t)p.rows * ((p.cols + kQBlock - 1) / kQBlock);
+    int blocks = (int)std::min<int64_t>((work + 255) / 256, 148 * 32);
+    k_init_param<<<blocks, 256, 0, m->stream>>>(p, seed, e0, scale, norm ? 1 : 0, nullptr);
+    CK(cudaGetLastError());
+    if (!norm) e0 += (uint64_t)p.rows * p.cols;
+  }
+  CK(cudaStreamSynchronize(m->stream));
+  m->weights_version++;
+  return SR_OK;
+}
+
+extern "C" int sr_model_load_param_f32(sr_model* m, int32_t index, const float* values, size_t count) {
+  if (!m || !values) return sr_fail(SR_EINVAL, "null argument");
+  if (index < 0 || index >= (int32_t)m->params.size()) return sr_fail(SR_EINVAL, "parameter index out of range");
+  Param& p = m->params[index];
+  if ((int64_t)count != (int64_t)p.rows * p.cols) return sr_fail(SR_EINVAL, "value count does not match rows*cols");
+  CK(cudaSetDevice(m->device));
+  float* tmp = nullptr;
+  cudaError_t e = cudaMalloc((void**)&tmp, count * 4);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return sr_fail(SR_ENOMEM, "staging allocation for a parameter failed");
+  }
+  e = cudaMemcpy(tmp, values, count * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && p.format == kQ4)
+    e = cudaMemset(p.values, 0, (size_t)param_value_bytes(p.rows, p.cols, p.format));
+  if (e == cudaSuccess) {
+    int64_t work = (int64_t)p.rows * ((p.cols + kQBlock - 1) / kQBlock);
+    int blocks = (int)std::min<int64_t>((work + 255) / 256, 148 * 32);
+    k_init_param<<<blocks, 256, 0, 0>>>(p, 0, 0, 0.0, 0, tmp);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  }
+  cudaFree(tmp);
+  if (e != cudaSuccess) return sr_fail(SR_EDEVICE, std::string("parameter upload: ") + cudaGetErrorString(e));
+  m->weights_version++;
+  return SR_OK;
+}
+
+extern "C" int sr_model_set_mode(sr_model* m, int32_t mode) {
+  if (!m) return sr_fail(SR_EINVAL, "null model");
+  if (mode != SR_MODE_EXACT && mode != SR_MODE_FAST) return sr_fail(SR_EINVAL, "invalid mode");
+  m->mode = mode;
+  return SR_OK;
+}
+
+// ----------------------------------------------------------------- KV pool --
+extern "C" int sr_kvpool_create(sr_model* m, int64_t num_pages, sr_kvpool** out) {
+  if (!m || !out) return sr_fail(SR_EINVAL, "null argument");
+  *out = nullptr;
+  if (num_pages < 1 || num_pages > (int64_t)INT32_MAX) return sr_fail(SR_EINVAL, "num_pages must be 1..2^31-1");
+  CK(cudaSetDevice(m->device));
+  sr_kvpool* p = new sr_kvpool();
+  p->m = m;
+  p->num_pages = num_pages;
+  size_t bytes = (size_t)num_pages * (size_t)m->dm.page_elems * 4;
+  cudaError_t e = cudaMalloc((void**)&p->data, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    delete p;
+    return sr_fail(SR_ENOMEM, "KV pool allocation of " + std::to_string(bytes) + " bytes failed");
+  }
+  e = cudaMemset(p->data, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p->data);
+    delete p;
+    return sr_fail(SR_EDEVICE, std::string("cudaMemset: ") + cudaGetErrorString(e));
+  }
+  *out = p;
+  return SR_OK;
+}
+extern "C" int sr_kvpool_destroy(sr_kvpool* p) {
+  if (!p) return sr_fail(SR_EINVAL, "null pool");
+  cudaSetDevice(p->m->device);
+  cudaFree(p->data);
+  delete p;
+  return SR_OK;
+}
+extern "C" int sr_kvpool_read_row(const sr_kvpool* p, int64_t page, int32_t layer, int32_t slot, float* k_out,
+                                  float* v_out) {
+  if (!p || !k_out || !v_out) return sr_fail(SR_EINVAL, "null argument");
+  const ModelDims& dm = p->m->dm;
+  if (page < 0 || page >= p->num_pages || layer < 0 || layer >= dm.layers || slot < 0 || slot >= dm.page_tokens)
+    return sr_fail(SR_EINVAL, "page, layer or slot out of range");
+  CK(cudaSetDevice(p->m->device));
+  const float* base = p->data + page * dm.page_elems + (int64_t)layer * 2 * dm.page_tokens * dm.kvd +
+                      (int64_t)slot * dm.kvd;
+  CK(cudaMemcpy(k_out, base, (size_t)dm.kvd * 4, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(v_out, base + (int64_t)dm.page_tokens * dm.kvd, (size_t)dm.kvd * 4, cudaMemcpyDeviceToHost));
+  return SR_OK;
+}
+__global__ void k_fill_pool(float* data, int64_t count, uint64_t seed, float scale) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+    uint64_t z = seed + (uint64_t)(i + 1) * 0x9e3779b97f4a7c15ULL;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+    z ^= z >> 31;
+    data[i] = scale * ((float)(z >> 40) * (1.0f / 16777216.0f) * 2.0f - 1.0f);
+  }
+}
+extern "C" int sr_kvpool_fill_synthetic(sr_kvpool* p, uint64_t seed, float scale) {
+  if (!p) return sr_fail(SR_EINVAL, "null pool");
+  CK(cudaSetDevice(p->m->device));
+  int64_t count = p->num_pages * p->m->dm.page_elems;
+  k_fill_pool<<<148 * 16, 256, 0, p->m->stream>>>(p->data, count, seed, scale);
+  CK(cudaGetLastError());
+  CK(cudaStreamSynchronize(p->m->stream));
+  return SR_OK;
+}
+
+// --------------------------------------------------------------------- step --
+// Host validation mirroring prefillSelected (M:6246-6339): completes before any
+// device state changes.
+int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* b, BatchInfo* info) {
+  if (!b) return sr_fail(SR_EINVAL, "null batch");
+  const sr_model_desc& c = m->d;
+  const int S = b->n_sessions;
+  if (S < 1 || S > kMaxSessions) return sr_fail(SR_EINVAL, "invalid prefill batch (1..256 sessions)");
+  if (!b->pos || !b->token_offsets || !b->tokens || !b->page_offsets || !b->page_ids)
+    return sr_fail(SR_EINVAL, "null batch array");
+  if (b->token_offsets[0] != 0 || b->page_offsets[0] != 0) return sr_fail(SR_EINVAL, "offsets must start at 0");
+  const int pt = c.page_tokens;
+  int64_t n = 0, max_end = 0, heads = 0;
+  for (int i = 0; i < S; i++) {
+    int64_t len = (int64_t)b->token_offsets[i + 1] - b->token_offsets[i];
+    if (len < 1 || len > kMaxRows - n)
+      return sr_fail(SR_EINVAL, "prefill requires nonempty chunks totaling at most 1024 tokens");
+    int64_t pos = b->pos[i];
+    if (pos < 0 || pos > c.context || len > c.context - pos)
+      return sr_fail(SR_EINVAL, "KV cache context exhausted or invalid position");
+    for (int64_t j = b->token_offsets[i]; j < b->token_offsets[i + 1]; j++)
+      if (b->tokens[j] < 0 || b->tokens[j] >= c.vocab) return sr_fail(SR_EINVAL, "token outside vocabulary");
+    int64_t np = (int64_t)b->page_offsets[i + 1] - b->page_offsets[i];
+    int64_t need = (pos + len + pt - 1) / pt;
+    if (np < need || np > m->max_pages_per_session) return sr_fail(SR_EINVAL, "invalid KV page coverage");
+    for (int64_t j = b->page_offsets[i]; j < b->page_offsets[i + 1]; j++)
+      if (b->page_ids[j] < 0 || b->page_ids[j] >= pool->num_pages) return sr_fail(SR_EINVAL, "invalid KV page id");
+    n += len;
+    max_end = std::max(max_end, pos + len);
+    heads += (!b->want_logits || b->want_logits[i]) ? 1 : 0;
+  }
+  // A page this step writes must belong to exactly one session (the reference
+  // rejects duplicate caches, M:6264-6266; shared prefix pages are read-only).
+  {
+    std::unordered_map<int32_t, int> owner;
+    owner.reserve((size_t)b->page_offsets[S] * 2);
+    for (int i = 0; i < S; i++)
+      for (int64_t j = b->page_offsets[i]; j < b->page_offsets[i + 1]; j++) {
+        auto it = owner.find(b->page_ids[j]);
+        if (it == owner.end())
+          owner.emplace(b->page_ids[j], i);
+        else if (it->second != i)
+          it->second = -1;  // listed by several sessions
+      }
+    for (int i = 0; i < S; i++) {
+      int64_t len = (int64_t)b->token_offsets[i + 1] - b->token_offsets[i];
+      int64_t first = b->pos[i] / pt, last = (b->pos[i] + len - 1) / pt;
+      for (int64_t pg = first; pg <= last; pg++) {
+        int32_t id = b->page_ids[b->page_offsets[i] + pg];
+        if (owner[id] != i) return sr_fail(SR_EINVAL, "a written KV page is shared with another session");
+        for (int64_t q = b->page_offsets[i]; q < b->page_offsets[i] + pg; q++)
+          if (b->page_ids[q] == id) return sr_fail(SR_EINVAL, "duplicate page in one session's page table");
+      }
+    }
+  }
+  // resizeInferenceArrays bound (M:6149-6174) with maxActivationElements (M:50),
+  // counting one attention lane.
+  {
+    const int64_t d = c.dim, kd = m->dm.kvd, hid = c.hidden;
+    int64_t stride = std::min<int64_t>(c.context, ((max_end + 31) / 32) * 32);
+    int64_t required = n * (5 * d + 2 * kd + 3 * hid) + 2 * (int64_t)S * c.vocab + stride;
+    if (required > 128LL * 1024 * 1024)
+      return sr_fail(SR_EINVAL, "inference workspace budget exceeded; reduce prefill tokens or batch size");
+  }
+  info->sessions = S;
+  info->rows = (int)n;
+  info->max_len = (int)max_end;
+  info->heads = (int)heads;
+  info->pages = b->page_offsets[S];
+  return SR_OK;
+}
+
+int sr_upload_batch(sr_model* m, const sr_batch* b, const BatchInfo& info) {
+  int32_t* h = (int32_t*)m->h_stage;
+  const int S = info.sessions;
+  memset(h, 0, (size_t)kMetaHeader * 4);
+  memcpy(h + kOffSessPos, b->pos, (size_t)S * 4);
+  memcpy(h + kOffTokOff, b->token_offsets, (size_t)(S + 1) * 4);
+  memcpy(h + kOffPageOff, b->page_offsets, (size_t)(S + 1) * 4);
+  uint8_t* want = (uint8_t*)(h + kOffWant);
+  for (int i = 0; i < S; i++) want[i] = (!b->want_logits || b->want_logits[i]) ? 1 : 0;
+  memcpy(h + kOffTokens, b->tokens, (size_t)info.rows * 4);
+  memcpy(h + kMetaHeader, b->page_ids, (size_t)info.pages * 4);
+  m->last_want.assign(want, want + S);
+  m->last_sessions = S;
+  CK(cudaMemcpyAsync(m->meta_dev, h, (size_t)(kMetaHeader + info.pages) * 4, cudaMemcpyHostToDevice, m->stream));
+  return SR_OK;
+}
+
+static void launch_linear_exact(sr_model* m, const float* X, int n, const Param& W, LinearOut O) {
+  const int in = W.cols, out = W.rows;
+  cudaStream_t s = m->stream;
+  auto grid = [&](int ot, int rt) { return dim3((out + ot - 1) / ot, (n + rt - 1) / rt); };
+  int choice;  // 0: (32,4)  1: (32,8)  2: (64,8)
+  if (n <= 4) choice = 0;
+  else if ((int64_t)((out + 63) / 64) * ((n + 7) / 8) >= 2 * 148) choice = 2;
+  else choice = 1;
+  if (W.format == kF32) {
+    if (choice == 0) k_linear_f32_exact<32, 4><<<grid(32, 4), 128, 0, s>>>(X, n, in, out, W, O);
+    else if (choice == 1) k_linear_f32_exact<32, 8><<<grid(32, 8), 128, 0, s>>>(X, n, in, out, W, O);
+    else k_linear_f32_exact<64, 8><<<grid(64, 8), 256, 0, s>>>(X, n, in, out, W, O);
+  } else if (W.format == kQ8) {
+    if (choice == 0) k_linear_q_exact<kQ8, 32, 4><<<grid(32, 4), 128, 0, s>>>(X, n, in, out, W, O);
+    else if (choice == 1) k_linear_q_exact<kQ8, 32, 8><<<grid(32, 8), 128, 0, s>>>(X, n, in, out, W, O);
+    else k_linear_q_exact<kQ8, 64, 8><<<grid(64, 8), 256, 0, s>>>(X, n, in, out, W, O);
+  } else {
+    if (choice == 0) k_linear_q_exact<kQ4, 32, 4><<<grid(32, 4), 128, 0, s>>>(X, n, in, out, W, O);
+    else if (choice == 1) k_linear_q_exact<kQ4, 32, 8><<<grid(32, 8), 128, 0, s>>>(X, n, in, out, W, O);
+    else k_linear_q_exact<kQ4, 64, 8><<<grid(64, 8), 256, 0, s>>>(X, n, in, out, W, O);
+  }
+}
+void sr_launch_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O, int cls = SR_PROF_LINEAR) {
+  ProfScope ps(m, cls);
+  if (m->mode == SR_MODE_FAST && fast_linear(m, X, n, W, O)) return;
+  launch_linear_exact(m, X, n, W, O);
+}
+
+static void launch_attention_exact(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer) {
+  const ModelDims& dm = m->dm;
+  AttnArgs a;
+  a.Q = m->Q;
+  a.A = m->A;
+  a.pool = pool->data;
+  a.meta = m->meta;
+  a.dm = dm;
+  a.layer = layer;
+  a.scale = (float)(1.0 / std::sqrt((double)dm.hd));
+  a.ls = attn_align4(max_len);
+  AttnSmem with_scores(dm.group, dm.hd, 1, a.ls);
+  a.smem_scores = with_scores.total * 4 <= 160 * 1024 ? 1 : 0;
+  AttnSmem lay(dm.group, dm.hd, a.smem_scores, a.ls);
+  int threads = std::max(128, ((dm.group * dm.hd / 4 + 31) / 32) * 32);
+  k_attention_exact<<<dim3(n, dm.kv_heads), threads, (size_t)lay.total * 4, m->stream>>>(a);
+}
+
+int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel) {
+  const ModelDims& dm = m->dm;
+  const int n = info.rows, d = dm.dim, kd = dm.kvd, L = dm.layers;
+  const double eps = m->d.norm_eps;
+  cudaStream_t s = m->stream;
+  sr_prof_span_begin(m);
+  SR_LAUNCH(m, SR_PROF_META, k_meta<<<1, 1024, 0, s>>>(m->meta, info.sessions, n));
+  SR_LAUNCH(m, SR_PROF_EMBED, k_embed<<<n, 256, 0, s>>>(m->params[0], m->meta.tokens, m->X, d));
+  const int norm_blocks = (n + kNormWarps - 1) / kNormWarps;
+  const bool fast = m->mode == SR_MODE_FAST;
+  for (int l = 0; l < L; l++) {
+    if (cancel && *cancel) {
+      sr_prof_span_end(m);
+      cudaStreamSynchronize(s);
+      sr_prof_resolve(m);
+      return sr_fail(SR_ECANCELED, "step canceled between layers");
+    }
+    const Param* P = &m->params[1 + 9 * l];
+    const Param* B = m->d.qkv_bias ? &m->params[2 + 9 * L + 3 * l] : nullptr;
+    LinearOut o;
+    o.ldy = 0;
+    o.resid = nullptr;
+    o.out_map = nullptr;
+    SR_LAUNCH(m, SR_PROF_NORM,
+              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps);
+              else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps));
+    o.y = m->Q; o.ldy = d; o.bias = B ? (const float*)B[0].values : nullptr;
+    sr_launch_linear(m, m->N, n, P[1], o);
+    o.y = m->K; o.ldy = kd; o.bias = B ? (const float*)B[1].values : nullptr;
+    sr_launch_linear(m, m->N, n, P[2], o);
+    o.y = m->V; o.ldy = kd; o.bias = B ? (const float*)B[2].values : nullptr;
+    sr_launch_linear(m, m->N, n, P[3], o);
+    SR_LAUNCH(m, SR_PROF_ROPE_KV,
+              k_rope_kv_exact<<<n, 128, 0, s>>>(m->Q, m->K, m->V, m->cos_t, m->sin_t, m->meta, pool->data, dm, l));
+    SR_LAUNCH(m, SR_PROF_ATTENTION,
+              if (fast) fast_attention(m, pool, n, info.max_len, l);
+              else launch_attention_exact(m, pool, n, info.max_len, l));
+    o.y = m->X; o.ldy = d; o.bias = nullptr; o.resid = m->X;
+    sr_launch_linear(m, m->A, n, P[4], o);
+    SR_LAUNCH(m, SR_PROF_NORM,
+              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps);
+              else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps));
+    o.resid = nullptr;
+    o.y = m->G; o.ldy = dm.hidden;
+    sr_launch_linear(m, m->N, n, P[6], o);
+    o.y = m->U;
+    sr_launch_linear(m, m->N, n, P[7], o);
+    int64_t cnt = (int64_t)n * dm.hidden;
+    SR_LAUNCH(m, SR_PROF_SWIGLU,
+              k_swiglu_exact<<<(int)std::min<int64_t>((cnt + 255) / 256, 148 * 16), 256, 0, s>>>(m->G, m->U, m->H, cnt));
+    o.y = m->X; o.ldy = d; o.resid = m->X;
+    sr_launch_linear(m, m->H, n, P[8], o);
+  }
+  // Selected head (M:6420-6448): gather last rows, final norm, LM head into
+  // the session's logits row; unselected rows are zero.
+  CK(cudaMemsetAsync(m->logits, 0, (size_t)info.sessions * dm.vocab * 4, s));
+  if (info.heads > 0) {
+    const Param& F = m->params[1 + 9 * L];
+    const int hb = (info.heads + kNormWarps - 1) / kNormWarps;
+    SR_LAUNCH(m, SR_PROF_HEAD,
+              if (fast) fast_rmsnorm(m, m->X, m->meta.head_src, (const float*)F.values, m->N, info.heads, d, eps);
+              else k_rmsnorm_exact<<<hb, kNormWarps * 32, 0, s>>>(m->X, m->meta.head_src, (const float*)F.values, m->N, info.heads, d, eps));
+    const Param& head = m->d.tied ? m->params[0] : m->params.back();
+    LinearOut o;
+    o.y = m->logits;
+    o.ldy = dm.vocab;
+    o.bias = nullptr;
+    o.resid = nullptr;
+    o.out_map = m->meta.head_dst;
+    sr_launch_linear(m, m->N, info.heads, head, o, SR_PROF_HEAD);
+  }
+  CK(cudaGetLastError());
+  return SR_OK;
+}
+
+extern "C" int sr_step(sr_model* m, sr_kvpool* pool, const sr_batch* batch, float* logits_host,
+                       const volatile int32_t* cancel) {
+  if (!m || !pool || !batch) return sr_fail(SR_EINVAL, "null argument");
+  if (pool->m != m) return sr_fail(SR_EINVAL, "KV pool belongs to another model");
+  BatchInfo info;
+  int rc = sr_validate_batch(m, pool, batch, &info);
+  if (rc != SR_OK) return rc;
+  CK(cudaSetDevice(m->device));
+  if (cancel && *cancel) return sr_fail(SR_ECANCELED, "step canceled before it started");
+  if ((rc = sr_upload_batch(m, batch, info)) != SR_OK) return rc;
+  if ((rc = sr_step_enqueue(m, pool, info, cancel)) != SR_OK) return rc;
+  sr_prof_span_end(m);
+  if (logits_host)
+    CK(cudaMemcpyAsync(logits_host, m->logits, (size_t)info.sessions * m->dm.vocab * 4, cudaMemcpyDeviceToHost,
+                       m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  sr_prof_resolve(m);
+  return SR_OK;
+}
+
+extern "C" int sr_step_logits(sr_model* m, const float** device_logits) {
+  if (!m || !device_logits) return sr_fail(SR_EINVAL, "null argument");
+  *device_logits = m->logits;
+  return SR_OK;
+}
+
+// ------------------------------------------------------------------ sampler --
+int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const int32_t* history_offsets,
+                      const int32_t* history, const uint64_t* rng_state, int32_t blocked) {
+  if (n != m->last_sessions) return sr_fail(SR_EINVAL, "session count differs from the last step");
+  if (!settings || !history_offsets || !rng_state) return sr_fail(SR_EINVAL, "null argument");
+  if (history_offsets[0] != 0) return sr_fail(SR_EINVAL, "history offsets must start at 0");
+  const int64_t nh = history_offsets[n];
+  if (nh < 0 || nh > kSampleHistCap) return sr_fail(SR_EINVAL, "history exceeds the device staging capacity");
+  if (nh > 0 && !history) return sr_fail(SR_EINVAL, "null history");
+  for (int i = 0; i < n; i++) {
+    if (history_offsets[i + 1] < history_offsets[i]) return sr_fail(SR_EINVAL, "history offsets must be nondecreasing");
+    if (!m->last_want[i]) continue;
+    const sr_sampling& s = settings[i];
+    if (!std::isfinite(s.temperature) || s.temperature < 0 || s.temperature > 100 || !std::isfinite(s.top_p) ||
+        s.top_p <= 0 || s.top_p > 1 || !std::isfinite(s.repeat_penalty) || s.repeat_penalty < 1 ||
+        s.repeat_penalty > 100 || s.top_k < 0)
+      return sr_fail(SR_EINVAL, "invalid sampling settings");  // Sampling.Validate (M:7264-7269)
+    if (s.temperature != 0 && (s.top_k < 1 || s.top_k > kMaxTopK))
+      return sr_fail(SR_EUNSUPPORTED, "device sampler supports top_k 1..256 when temperature > 0");
+  }
+  // Staging: settings | hist_off | hist | rng
+  uint8_t* h = (uint8_t*)m->h_stage + m->upload_ints * 4;
+  SampleSetting* hs = (SampleSetting*)h;
+  for (int i = 0; i < n; i++) {
+    hs[i].temperature = settings[i].temperature;
+    hs[i].top_p = settings[i].top_p;
+    hs[i].penalty = settings[i].repeat_penalty;
+    hs[i].top_k = settings[i].top_k;
+    hs[i].pad = 0;
+  }
+  const size_t off_hoff = kSampOffHistOff, off_hist = kSampOffHist, off_rng = kSampOffRng, off_ids = kSampOffIds,
+               off_status = kSampOffStatus;
+  memcpy(h + off_hoff, history_offsets, (size_t)(n + 1) * 4);
+  if (nh) memcpy(h + off_hist, history, (size_t)nh * 4);
+  memcpy(h + off_rng, rng_state, (size_t)n * 8);
+  uint8_t* dv = (uint8_t*)m->samp_dev;
+  CK(cudaMemcpyAsync(dv, h, (size_t)n * sizeof(SampleSetting), cudaMemcpyHostToDevice, m->stream));
+  CK(cudaMemcpyAsync(dv + off_hoff, h + off_hoff, (size_t)(n + 1) * 4, cudaMemcpyHostToDevice, m->stream));
+  if (nh) CK(cudaMemcpyAsync(dv + off_hist, h + off_hist, (size_t)nh * 4, cudaMemcpyHostToDevice, m->stream));
+  CK(cudaMemcpyAsync(dv + off_rng, h + off_rng, (size_t)n * 8, cudaMemcpyHostToDevice, m->stream));
+  SampleArgs a;
+  a.logits = m->logits;
+  a.V = m->dm.vocab;
+  a.n = n;
+  a.blocked = blocked;
+  a.want = m->meta.want;
+  a.settings = (const SampleSetting*)dv;
+  a.hist_off = (const int32_t*)(dv + off_hoff);
+  a.hist = (const int32_t*)(dv + off_hist);
+  a.rng = (uint64_t*)(dv + off_rng);
+  a.ids = (int32_t*)(dv + off_ids);
+  a.status = (int32_t*)(dv + off_status);
+  size_t smem = (size_t)((m->dm.vocab + 31) / 32) * 4;
+  SR_LAUNCH(m, SR_PROF_SAMPLE, k_sample<<<n, kSampleThreads, smem, m->stream>>>(a));
+  CK(cudaGetLastError());
+  sr_prof_span_end(m);
+  // results: rng | ids | status are contiguous -> one copy back
+  CK(cudaMemcpyAsync(h + off_rng, dv + off_rng, off_status + (size_t)kMaxSessions * 4 - off_rng, cudaMemcpyDeviceToHost,
+                     m->stream));
+  return SR_OK;
+}
+
+int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_out) {
+  CK(cudaStreamSynchronize(m->stream));
+  sr_prof_resolve(m);
+  uint8_t* h = (uint8_t*)m->h_stage + m->upload_ints * 4;
+  const size_t off_hoff = kSampOffHistOff, off_hist = kSampOffHist, off_rng = kSampOffRng, off_ids = kSampOffIds,
+               off_status = kSampOffStatus;
+  const int32_t* ids = (const int32_t*)(h + off_ids);
+  const int32_t* status = (const int32_t*)(h + off_status);
+  memcpy(ids_out, ids, (size_t)n * 4);
+  for (int i = 0; i < n; i++) {
+    if (!m->last_want[i]) continue;
+    if (status[i] == 1) return sr_fail(SR_EINVAL, "nonfinite sampling logit (session " + std::to_string(i) + ")");
+    if (status[i] == 2) return sr_fail(SR_EINVAL, "empty sampling distribution (session " + std::to_string(i) + ")");
+    if (status[i] == 3) return sr_fail(SR_EUNSUPPORTED, "unsupported sampling settings (session " + std::to_string(i) + ")");
+  }
+  memcpy(rng_state, h + off_rng, (size_t)n * 8);
+  return SR_OK;
+}
+
+extern "C" int sr_sample(sr_model* m, int32_t n_sessions, const sr_sampling* settings, const int32_t* history_offsets,
+                         const int32_t* history, uint64_t* rng_state, int32_t blocked, int32_t* ids_out) {
+  if (!m || !ids_out || !rng_state) return sr_fail(SR_EINVAL, "null argument");
+  CK(cudaSetDevice(m->device));
+  sr_prof_span_begin(m);
+  int rc = sr_sample_enqueue(m, n_sessions, settings, history_offsets, history, rng_state, blocked);
+  if (rc != SR_OK) return rc;
+  return sr_sample_finish(m, n_sessions, rng_state, ids_out);
+}
+
+extern "C" int sr_step_sample(sr_model* m, sr_kvpool* pool, const sr_batch* batch, const sr_sampling* settings,
+                              const int32_t* history_offsets, const int32_t* history, uint64_t* rng_state,
+                              int32_t blocked, int32_t* ids_out) {
+  if (!m || !pool || !batch || !ids_out || !rng_state) return sr_fail(SR_EINVAL, "null argument");
+  if (pool->m != m) return sr_fail(SR_EINVAL, "KV pool belongs to another model");
+  BatchInfo info;
+  int rc = sr_validate_batch(m, pool, batch, &info);
+  if (rc != SR_OK) return rc;
+  CK(cudaSetDevice(m->device));
+  if ((rc = sr_upload_batch(m, batch, info)) != SR_OK) return rc;
+  if ((rc = sr_step_enqueue(m, pool, info, nullptr)) != SR_OK) return rc;
+  if ((rc = sr_sample_enqueue(m, batch->n_sessions, settings, history_offsets, history, rng_state, blocked)) != SR_OK) {
+    sr_prof_span_end(m);
+    cudaStreamSynchronize(m->stream);
+    sr_prof_resolve(m);
+    return rc;
+  }
+  return sr_sample_finish(m, batch->n_sessions, rng_state, ids_out);
+}
+
+// Fast-mode attention entry (split-K kernels live in fast_attention.cu when
+// built; until then the exact kernel serves both modes).
+void sr::fast_attention_launch(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer) {
+  launch_attention_exact(m, pool, n, max_len, layer);
+}
+
+// ---------------------------------------------------------------- profiling --
+void sr_prof_span_begin(sr_model* m) {
+  Profiler& p = m->prof;
+  if (!p.span0) {
+    cudaEventCreate(&p.span0);
+    cudaEventCreate(&p.span1);
+  }
+  if (!p.span_open) {
+    cudaEventRecord(p.span0, m->stream);
+    p.span_open = true;
+  }
+}
+void sr_prof_span_end(sr_model* m) {
+  Profiler& p = m->prof;
+  if (p.span_open) cudaEventRecord(p.span1, m->stream);
+}
+void sr_prof_resolve(sr_model* m) {
+  Profiler& p = m->prof;
+  for (size_t i = 0; i < p.pending.size(); i++) {
+    float t = 0.f;
+    if (cudaEventElapsedTime(&t, p.events[2 * i], p.events[2 * i + 1]) == cudaSuccess) p.ms[p.pending[i]] += t;
+  }
+  p.pending.clear();
+  p.used = 0;
+  if (p.span_open) {
+    float t = 0.f;
+    if (cudaEventElapsedTime(&t, p.span0, p.span1) == cudaSuccess) {
+      p.span_ms += t;
+      p.steps++;
+    }
+    p.span_open = false;
+  }
+  cudaGetLastError();
+}
+extern "C" int sr_profile_set(sr_model* m, uint32_t class_mask) {
+  if (!m) return sr_fail(SR_EINVAL, "null model");
+  m->prof.mask = class_mask & ((1u << SR_PROF_CLASSES) - 1);
+  return SR_OK;
+}
+extern "C" int sr_profile_read(sr_model* m, double* ms, int64_t* launches, double* span_ms, int64_t* steps,
+                               int64_t* total_launches, int32_t reset) {
+  if (!m) return sr_fail(SR_EINVAL, "null model");
+  Profiler& p = m->prof;
+  for (int i = 0; i < SR_PROF_CLASSES; i++) {
+    if (ms) ms[i] = p.ms[i];
+    if (launches) launches[i] = p.launches[i];
+  }
+  if (span_ms) *span_ms = p.span_ms;
+  if (steps) *steps = p.steps;
+  if (total_launches) *total_launches = p.total_launches;
+  if (reset) {
+    for (int i = 0; i < SR_PROF_CLASSES; i++) {
+      p.ms[i] = 0;
+      p.launches[i] = 0;
+    }
+    p.span_ms = 0;
+    p.steps = 0;
+    p.total_launches = 0;
+  }
+  return SR_OK;
+}
+extern "C" int sr_model_stream(sr_model* m, void** stream) {
+  if (!m || !stream) return sr_fail(SR_EINVAL, "null argument");
+  *stream = (void*)m->stream;
+  return SR_OK;
+}

@@ -1,0 +1,131 @@
+// srstep_internal.h -- definitions shared by the step library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <string>
+#include <vector>
+
+#include "../../include/srstep.h"
+#include "common.cuh"
+
+// Metadata upload layout (int32 words): the host stages exactly this prefix and
+// copies it with one cudaMemcpyAsync per step.
+constexpr int kOffSessPos = 0;                  // [256]
+constexpr int kOffTokOff = 256;                 // [257], padded to 260
+constexpr int kOffPageOff = 516;                // [257], padded to 260
+constexpr int kOffWant = 776;                   // 256 bytes
+constexpr int kOffTokens = 840;                 // [1024]
+constexpr int kMetaHeader = 1864;               // page ids follow
+constexpr int kMetaComputed = 2 * 1024 + 2 * 256 + 4;
+constexpr int64_t kSampleHistCap = 4 << 20;     // history ids staged per sampling call
+// Sampler staging layout (host pinned and device copies share it).  Every
+// region starts on a 16-byte boundary: the RNG states are 8-byte words.
+constexpr size_t sr_align16(size_t x) { return (x + 15) & ~(size_t)15; }
+constexpr size_t kSampOffSettings = 0;
+constexpr size_t kSampOffHistOff = sr_align16(kSampOffSettings + 256 * 32);
+constexpr size_t kSampOffHist = sr_align16(kSampOffHistOff + 257 * 4);
+constexpr size_t kSampOffRng = sr_align16(kSampOffHist + (size_t)kSampleHistCap * 4);
+constexpr size_t kSampOffIds = sr_align16(kSampOffRng + 256 * 8);
+constexpr size_t kSampOffStatus = sr_align16(kSampOffIds + 256 * 4);
+constexpr size_t kSampleStageBytes = sr_align16(kSampOffStatus + 256 * 4);
+static_assert(kSampOffRng % 16 == 0, "RNG states must be 8-byte aligned");
+
+struct BatchInfo {
+  int sessions, rows, max_len, heads;
+  int64_t pages;
+};
+
+// Event-based per-kernel-class timing on the model's stream.
+struct Profiler {
+  uint32_t mask = 0;
+  std::vector<cudaEvent_t> events;
+  size_t used = 0;
+  std::vector<int> pending;  // class of each recorded (start, end) event pair
+  double ms[SR_PROF_CLASSES] = {};
+  int64_t launches[SR_PROF_CLASSES] = {};
+  int64_t total_launches = 0;
+  cudaEvent_t span0 = nullptr, span1 = nullptr;
+  bool span_open = false;
+  double span_ms = 0;
+  int64_t steps = 0;
+};
+
+struct sr_model {
+  sr_model_desc d;
+  int device = 0;
+  int mode = SR_MODE_EXACT;
+  sr::ModelDims dm;
+  std::vector<sr::Param> params;
+  std::vector<void*> allocs;
+  uint64_t weights_version = 0;
+  float* cos_t = nullptr;
+  float* sin_t = nullptr;
+  float *X = nullptr, *N = nullptr, *Q = nullptr, *K = nullptr, *V = nullptr, *A = nullptr, *T = nullptr;
+  float *G = nullptr, *U = nullptr, *H = nullptr, *logits = nullptr;
+  int32_t* meta_dev = nullptr;
+  sr::StepMeta meta;
+  int64_t max_pages_per_session = 0, page_cap = 0, upload_ints = 0;
+  void* h_stage = nullptr;
+  void* samp_dev = nullptr;
+  cudaStream_t stream = nullptr;
+  int last_sessions = 0;
+  std::vector<uint8_t> last_want;
+  Profiler prof;
+  // fast-mode state (owned by fast_kernels.cuh)
+  void* fast = nullptr;
+  std::vector<std::function<void()>> fast_free;
+};
+
+struct sr_kvpool {
+  sr_model* m = nullptr;
+  int64_t num_pages = 0;
+  float* data = nullptr;
+};
+
+int sr_fail(int code, const std::string& msg);
+
+// RAII scope around one kernel launch: counts it and, when its class is
+// selected, brackets it with a pair of events on the model's stream.
+struct ProfScope {
+  sr_model* m;
+  int cls;
+  bool timed;
+  ProfScope(sr_model* m_, int cls_) : m(m_), cls(cls_), timed((m_->prof.mask >> cls_) & 1u) {
+    if (timed) {
+      Profiler& p = m->prof;
+      while (p.events.size() < p.used + 2) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        p.events.push_back(e);
+      }
+      cudaEventRecord(p.events[p.used], m->stream);
+    }
+  }
+  ~ProfScope() {
+    Profiler& p = m->prof;
+    p.launches[cls]++;
+    p.total_launches++;
+    if (timed) {
+      cudaEventRecord(p.events[p.used + 1], m->stream);
+      p.used += 2;
+      p.pending.push_back(cls);
+    }
+  }
+};
+#define SR_LAUNCH(m, cls, ...) \
+  do {                         \
+    ProfScope ps_((m), (cls)); \
+    __VA_ARGS__;               \
+  } while (0)
+void sr_prof_span_begin(sr_model* m);
+void sr_prof_span_end(sr_model* m);
+void sr_prof_resolve(sr_model* m);  // after a stream synchronize
+int sr_model_alloc(sr_model* m, void** p, size_t bytes);
+int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* b, BatchInfo* info);
+int sr_upload_batch(sr_model* m, const sr_batch* b, const BatchInfo& info);
+int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel);
+int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const int32_t* history_offsets,
+                      const int32_t* history, const uint64_t* rng_state, int32_t blocked);
+int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_out);
