@@ -1,34 +1,136 @@
-// fast_kernels.cuh -- SR_MODE_FAST: fused-multiply-add kernels checked against
-// the reference within a stated tolerance.  Entry points return false / fall
-// back to the exact kernels for shapes they do not cover.
+// fast_kernels.cuh -- SR_MODE_FAST: fused-multiply-add, split-K and tensor-core
+// kernels, checked against the reference within a stated tolerance.  Shapes a
+// fast kernel does not cover run on the exact kernels.
 #pragma once
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "exact_kernels.cuh"
+#include "fast_attention.cuh"
 #include "srstep_internal.h"
 
 namespace sr {
 
+struct FastState {
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  size_t items_cap = 0;
+};
+
+inline FastState* fast_state(sr_model* m) { return (FastState*)m->fast; }
+
 inline int fast_init(sr_model* m) {
-  (void)m;
+  FastState* st = new FastState();
+  m->fast = st;
+  m->fast_free.push_back([st]() {
+    if (st->part_o) cudaFree(st->part_o);
+    if (st->part_ml) cudaFree(st->part_ml);
+    delete st;
+  });
   return SR_OK;
 }
 
-// Returns true when the fast path handled the projection.
-inline bool fast_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O) {
-  (void)m, (void)X, (void)n, (void)W, (void)O;
-  return false;
+// ------------------------------------------------------------------ RMSNorm --
+// rmsInto (M:6182-6194) with a lane-parallel fp64 sum of squares (reordered).
+__global__ void __launch_bounds__(128)
+k_rmsnorm_fast(const float* __restrict__ X, const int32_t* __restrict__ src_map, const float* __restrict__ w,
+               float* __restrict__ Y, int rows, int d, double eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 4 + warp;
+  if (r >= rows) return;
+  const int srow = src_map ? src_map[r] : r;
+  const float* x = X + (int64_t)srow * d;
+  double ss = 0.0;
+  if ((d & 3) == 0) {
+    for (int j = lane * 4; j < d; j += 128) {
+      float4 v = *(const float4*)(x + j);
+      ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    }
+  } else {
+    for (int j = lane; j < d; j += 32) ss += (double)x[j] * x[j];
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float a = (float)(1.0 / sqrt(ss / (double)d + eps));
+  float* y = Y + (int64_t)r * d;
+  for (int j = lane; j < d; j += 32) y[j] = x[j] * a * w[j];
 }
 
-inline void fast_rmsnorm(sr_model* m, const float* X, const int32_t* src_map, const float* w, float* Y, int rows, int d,
-                         double eps) {
-  k_rmsnorm_exact<<<(rows + kNormWarps - 1) / kNormWarps, kNormWarps * 32, 0, m->stream>>>(X, src_map, w, Y, rows, d,
-                                                                                           eps);
+inline void fast_rmsnorm(sr_model* m, const float* X, const int32_t* src_map, const float* w, float* Y, int rows,
+                         int d, double eps) {
+  k_rmsnorm_fast<<<(rows + 3) / 4, 128, 0, m->stream>>>(X, src_map, w, Y, rows, d, eps);
 }
 
-void fast_attention_launch(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer);
-inline void fast_attention(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer) {
-  fast_attention_launch(m, pool, n, max_len, layer);
+// ---------------------------------------------------------------- attention --
+template <int HD, int G>
+inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n) {
+  static bool configured = false;
+  const size_t smem = fa_smem_bytes<HD, G>();
+  if (!configured) {
+    cudaFuncSetAttribute(k_attn_split<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    configured = true;
+  }
+  k_attn_split<HD, G><<<dim3(a.max_splits, n, a.dm.kv_heads), kFaThreads, smem, m->stream>>>(a);
+  k_attn_combine<HD><<<dim3(n, a.dm.heads), HD, 0, m->stream>>>(a);
+  return true;
 }
+
+template <int HD>
+inline bool fa_dispatch_g(sr_model* m, const FastAttnArgs& a, int n) {
+  switch (a.dm.group) {
+    case 1: return fa_launch<HD, 1>(m, a, n);
+    case 2: return fa_launch<HD, 2>(m, a, n);
+    case 3: return fa_launch<HD, 3>(m, a, n);
+    case 4: return fa_launch<HD, 4>(m, a, n);
+    case 5: return fa_launch<HD, 5>(m, a, n);
+    case 6: return fa_launch<HD, 6>(m, a, n);
+    case 7: return fa_launch<HD, 7>(m, a, n);
+    case 8: return fa_launch<HD, 8>(m, a, n);
+    default: return false;
+  }
+}
+
+// Returns false (exact kernel runs instead) for unsupported shapes or when the
+// split scratch would exceed its cap.
+inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int max_len, int layer) {
+  const ModelDims& dm = m->dm;
+  if ((dm.hd != 64 && dm.hd != 128) || dm.group > 8) return false;
+  FastState* st = fast_state(m);
+  const int max_splits = (max_len + kFaSplit - 1) / kFaSplit;
+  const size_t items = (size_t)n * dm.kv_heads * max_splits;
+  const size_t o_bytes = items * dm.group * dm.hd * 4;
+  if (o_bytes > ((size_t)1 << 30)) return false;
+  if (items > st->items_cap) {
+    if (st->part_o) cudaFree(st->part_o);
+    if (st->part_ml) cudaFree(st->part_ml);
+    st->part_o = st->part_ml = nullptr;
+    st->items_cap = 0;
+    if (cudaMalloc((void**)&st->part_o, o_bytes) != cudaSuccess ||
+        cudaMalloc((void**)&st->part_ml, items * dm.group * 2 * 4) != cudaSuccess) {
+      cudaGetLastError();
+      if (st->part_o) cudaFree(st->part_o);
+      st->part_o = nullptr;
+      return false;
+    }
+    st->items_cap = items;
+  }
+  FastAttnArgs a;
+  a.Q = m->Q;
+  a.A = m->A;
+  a.pool = pool_data;
+  a.meta = m->meta;
+  a.dm = dm;
+  a.layer = layer;
+  a.scale = (float)(1.0 / std::sqrt((double)dm.hd));
+  a.max_splits = max_splits;
+  a.part_o = st->part_o;
+  a.part_ml = st->part_ml;
+  return dm.hd == 128 ? fa_dispatch_g<128>(m, a, n) : fa_dispatch_g<64>(m, a, n);
+}
+
+// ------------------------------------------------------------------- linear --
+// Returns true when a fast projection kernel handled the call.
+bool fast_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O);
 
 }  // namespace sr

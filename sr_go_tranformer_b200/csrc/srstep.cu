@@ -607,6 +607,7 @@ static void launch_linear_exact(sr_model* m, const float* X, int n, const Param&
     else k_linear_q_exact<kQ4, 64, 8><<<grid(64, 8), 256, 0, s>>>(X, n, in, out, W, O);
   }
 }
+static void fast_attention(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer);
 void sr_launch_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O, int cls = SR_PROF_LINEAR) {
   ProfScope ps(m, cls);
   if (m->mode == SR_MODE_FAST && fast_linear(m, X, n, W, O)) return;
@@ -843,10 +844,15 @@ extern "C" int sr_step_sample(sr_model* m, sr_kvpool* pool, const sr_batch* batc
   return sr_sample_finish(m, batch->n_sessions, rng_state, ids_out);
 }
 
-// Fast-mode attention entry (split-K kernels live in fast_attention.cu when
-// built; until then the exact kernel serves both modes).
-void sr::fast_attention_launch(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer) {
-  launch_attention_exact(m, pool, n, max_len, layer);
+// Fast-mode attention: split-K kernels when the shape is covered, else exact.
+static void fast_attention(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer) {
+  if (!fast_attention_try(m, pool->data, n, max_len, layer)) launch_attention_exact(m, pool, n, max_len, layer);
+}
+
+// Fast-mode projections (tensor-core GEMM) are not built yet: exact kernels run.
+bool sr::fast_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O) {
+  (void)m, (void)X, (void)n, (void)W, (void)O;
+  return false;
 }
 
 // ---------------------------------------------------------------- profiling --

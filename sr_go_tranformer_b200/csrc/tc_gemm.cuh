@@ -1,0 +1,328 @@
+// tc_gemm.cuh -- SR_MODE_FAST projections on the 5th-generation tensor cores.
+//
+// Y[n, out] = X[n, in] W[out, in]^T for Q8/Q4 weights (linearQ8Into / linearQ4Into,
+// cmd/monolith/monolith.go:4074-4511) restated for tcgen05:
+//   * W's integer codes are held as bf16 (exact: |q| <= 127) in a shadow copy;
+//     the fp32 activations are split into bf16 hi + lo planes, so each 64-column
+//     block's partial sum  sum_j x_j q_j  is formed by two MMA passes with fp32
+//     accumulation in TMEM (relative error ~2^-16 per term);
+//   * "swap AB": the 128-row MMA M dimension runs over output features, N over
+//     step rows, so a thread of the epilogue owns one output feature and its
+//     per-block scale (the reference's s += p*scale) is a scalar FMA on
+//     registers after each block's accumulator is read from TMEM;
+//   * TMA (SWIZZLE_128B) feeds a 4-stage mbarrier pipeline; one thread issues
+//     MMAs; TMEM holds two accumulator buffers so block b+1's MMAs overlap
+//     block b's epilogue.
+// Every mbarrier wait is bounded (globaltimer); on expiry the kernel records an
+// error flag, stops waiting and finishes, and the host reports SR_ETIMEOUT.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+
+namespace sr {
+namespace tc {
+
+constexpr int kM = 128;          // output features per tile (MMA M)
+constexpr int kN = 128;          // step rows per tile (MMA N)
+constexpr int kKB = 64;          // K per block (one scale block, one 128-byte bf16 row)
+constexpr int kStages = 4;
+constexpr int kThreads = 192;    // warp 0: TMA, warp 1: MMA, warps 2-5: epilogue
+constexpr uint32_t kTileA = kM * kKB * 2;  // 16 KiB
+constexpr uint32_t kTileB = kN * kKB * 2;  // 16 KiB
+constexpr uint32_t kStageBytes = kTileA + 2 * kTileB;
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait, then abort
+
+struct Segment {
+  int32_t rows;        // output features in this segment
+  int32_t ldy;
+  float* y;
+  const float* bias;
+  const float* resid;  // may alias y
+};
+
+struct GemmArgs {
+  int n;             // step rows
+  int out;           // total output features (sum of segment rows)
+  int in;            // K
+  int groups;        // ceil(in/64) scale blocks per output row
+  int kb_per_split;  // K-blocks per split
+  int splits;
+  const float* scales;   // [out][groups] (concatenated for fused segments)
+  float* partial;        // [splits][n][out] when splits > 1
+  const int32_t* out_map;  // compacted head rows -> destination row
+  Segment seg[3];
+  int nseg;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded parity wait.  Returns false (and raises *err) when it expires or
+// when another thread already raised the error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const uint32_t addr = smem_u32(bar);
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; it++) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 63) == 0) {
+      if (*(volatile int*)err) return false;
+      const uint64_t now = globaltimer();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > kWaitNs) {
+        atomicExch(err, 1);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+// K-major, SWIZZLE_128B shared-memory matrix descriptor (rows of 128 bytes,
+// 8-row groups 1024 bytes apart).
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+  const uint64_t addr = smem_u32(tile);
+  uint64_t d = (addr >> 4) & 0x3FFFull;
+  d |= 1ull << 16;                // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset
+  d |= 1ull << 46;                // descriptor version
+  d |= 2ull << 61;                // SWIZZLE_128B
+  return d;
+}
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void store_out(const GemmArgs& a, int row, int o, float v) {
+  int s = 0, base = 0;
+  while (s + 1 < a.nseg && o >= base + a.seg[s].rows) {
+    base += a.seg[s].rows;
+    s++;
+  }
+  const Segment& g = a.seg[s];
+  const int ol = o - base;
+  const int orow = a.out_map ? a.out_map[row] : row;
+  float* dst = g.y + (int64_t)orow * g.ldy + ol;
+  if (g.bias) v += g.bias[ol];
+  if (g.resid) v = g.resid[(int64_t)orow * g.ldy + ol] + v;
+  *dst = v;
+}
+
+// grid: (ceil(out/128), ceil(n/128), splits)
+__global__ void __launch_bounds__(kThreads, 1)
+k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xh,
+         const __grid_constant__ CUtensorMap tm_xl, GemmArgs a) {
+  extern __shared__ __align__(1024) uint8_t gsm_raw[];
+  uint8_t* gsm = (uint8_t*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(gsm + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kM, n0 = blockIdx.y * kN, split = blockIdx.z;
+  const int kb0 = split * a.kb_per_split;
+  const int kb1 = min(a.groups, kb0 + a.kb_per_split);
+  const int nkb = max(0, kb1 - kb0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);  // one arrive per epilogue warp
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // one warp allocates 2*kN TMEM columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * kN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      for (int i = 0; i < nkb; i++) {
+        const int s = i % kStages, use = i / kStages;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, a.err)) break;
+        uint8_t* st = gsm + s * kStageBytes;
+        mbar_expect_tx(&full[s], kStageBytes);
+        const int k = (kb0 + i) * kKB;
+        tma_load_2d(st, &tm_w, &full[s], k, m0);
+        tma_load_2d(st + kTileA, &tm_xh, &full[s], k, n0);
+        tma_load_2d(st + kTileA + kTileB, &tm_xl, &full[s], k, n0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      const uint32_t idesc = idesc_bf16(kM, kN);
+      for (int i = 0; i < nkb; i++) {
+        const int s = i % kStages, b = i & 1;
+        if (!mbar_wait(&full[s], (i / kStages) & 1, a.err)) break;
+        if (i >= 2 && !mbar_wait(&tempty[b], ((i >> 1) - 1) & 1, a.err)) break;
+        tc_fence_after();
+        const uint8_t* st = gsm + s * kStageBytes;
+        const uint64_t da = sw128_desc(st), dh = sw128_desc(st + kTileA), dl = sw128_desc(st + kTileA + kTileB);
+        const uint32_t td = tmem + b * kN;
+#pragma unroll
+        for (int k = 0; k < kKB / 16; k++) umma_bf16(td, da + 2 * k, dh + 2 * k, idesc, k > 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < kKB / 16; k++) umma_bf16(td, da + 2 * k, dl + 2 * k, idesc, 1u);
+        umma_commit(&empty[s]);
+        umma_commit(&tfull[b]);
+      }
+    }
+  } else {  // epilogue warps 2..5: TMEM lane quarter = warp % 4
+    const int q = warp & 3;
+    const int o = m0 + q * 32 + lane;
+    float acc[kN];
+#pragma unroll
+    for (int j = 0; j < kN; j++) acc[j] = 0.f;
+    const float* srow = a.scales + (int64_t)min(o, a.out - 1) * a.groups;
+    for (int i = 0; i < nkb; i++) {
+      const int b = i & 1;
+      const float sc = srow[kb0 + i];
+      if (!mbar_wait(&tfull[b], (i >> 1) & 1, a.err)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * kN;
+#pragma unroll
+      for (int c = 0; c < kN; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(taddr + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j++) acc[c + j] = fmaf(__uint_as_float(v[j]), sc, acc[c + j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+    if (o < a.out) {
+      if (a.splits > 1) {
+        float* P = a.partial + (int64_t)split * a.n * a.out;
+#pragma unroll 4
+        for (int j = 0; j < kN; j++) {
+          const int row = n0 + j;
+          if (row < a.n) P[(int64_t)row * a.out + o] = acc[j];
+        }
+      } else {
+#pragma unroll 4
+        for (int j = 0; j < kN; j++) {
+          const int row = n0 + j;
+          if (row < a.n) store_out(a, row, o, acc[j]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kN));
+  }
+}
+
+// Deterministic split-K reduction (splits summed in order) + epilogue.
+__global__ void k_gemm_reduce(GemmArgs a) {
+  const int64_t total = (int64_t)a.n * a.out;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(t / a.out), o = (int)(t % a.out);
+    float v = 0.f;
+    for (int s = 0; s < a.splits; s++) v += a.partial[(int64_t)s * total + t];
+    store_out(a, row, o, v);
+  }
+}
+
+// fp32 activations -> bf16 hi/lo planes: x ~= hi + lo, |x - hi - lo| <= 2^-17 |x|.
+__global__ void k_split_bf16(const float* __restrict__ X, int n, int in, __nv_bfloat16* __restrict__ H,
+                             __nv_bfloat16* __restrict__ Lo) {
+  const int64_t total = (int64_t)n * in;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const float x = X[t];
+    const __nv_bfloat16 h = __float2bfloat16_rn(x);
+    H[t] = h;
+    Lo[t] = __float2bfloat16_rn(x - __bfloat162float(h));
+  }
+}
+
+// Integer codes of a Q8/Q4 matrix as bf16 (exact), rows [0, rows) written at dst_row0.
+__global__ void k_codes_bf16(const void* __restrict__ values, int fmt, int rows, int cols,
+                             __nv_bfloat16* __restrict__ dst) {
+  const int64_t total = (int64_t)rows * cols;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = t / cols, c = t % cols;
+    float q;
+    if (fmt == kQ8) {
+      q = (float)((const int8_t*)values)[t];
+    } else {
+      const uint32_t b = ((const uint8_t*)values)[r * ((cols + 1) / 2) + c / 2];
+      q = (c & 1) ? q4_hi(b) : q4_lo(b);
+    }
+    dst[t] = __float2bfloat16_rn(q);
+  }
+}
+
+}  // namespace tc
+}  // namespace sr

@@ -1,0 +1,95 @@
+"""GPU parity of SR_MODE_FAST (split-K attention, FFMA norms, tensor-core
+projections) against the CPU oracle within a stated tolerance.
+
+Fast mode reorders fp32 sums (online softmax over 256-position splits, FMA
+contraction, bf16x2-split tensor-core products), so logits are compared with
+an absolute tolerance of FAST_ATOL on logits of magnitude ~1 and greedy ids
+must agree except on recorded near-ties (margin below FAST_TIE).
+"""
+
+import numpy as np
+import pytest
+
+from test_gpu_step import device_from_oracle
+
+pytestmark = pytest.mark.gpu
+
+FAST_ATOL = 5e-4
+FAST_TIE = 2 * FAST_ATOL
+
+
+def run_pair(oracle, srlib, om, prompts, chunk, decode_steps, threads=8):
+    from sr_go_tranformer_b200 import step as S
+    dm = device_from_oracle(om, srlib, mode="fast")
+    pages = sum((len(p) + decode_steps + om.cfg.page_tokens) // om.cfg.page_tokens + 1 for p in prompts)
+    pool = S.PagePool(dm, pages)
+    opool = np.zeros(pages * om.page_elements, dtype=np.float32)
+    caches = [dm.new_cache(pool) for _ in prompts]
+    cursor = [0] * len(prompts)
+    worst, ties = 0.0, 0
+    last = [None] * len(prompts)
+    while True:
+        chunks, want = [], []
+        for i, p in enumerate(prompts):
+            if cursor[i] < len(p):
+                chunks.append(p[cursor[i]:cursor[i] + chunk])
+            else:
+                chunks.append([last[i]])
+            want.append(cursor[i] + len(chunks[-1]) >= len(p))
+        pos = [c.pos for c in caches]
+        got = dm.prefill_selected(caches, chunks, want)
+        exp = om.step(opool, pos, chunks, [c.pages for c in caches], want, threads=threads)
+        err = float(np.abs(got - exp).max())
+        worst = max(worst, err)
+        assert err <= FAST_ATOL, f"fast logits differ by {err:.3g} at positions {pos}"
+        for i in range(len(prompts)):
+            if want[i]:
+                a, b = int(np.argmax(got[i])), int(np.argmax(exp[i]))
+                if a != b:
+                    srt = np.sort(exp[i])
+                    assert srt[-1] - srt[-2] < FAST_TIE, "greedy id differs without a near-tie"
+                    ties += 1
+                last[i] = b
+            if cursor[i] < len(prompts[i]):
+                cursor[i] += len(chunks[i])
+        if all(cursor[i] >= len(prompts[i]) for i in range(len(prompts))):
+            decode_steps -= 1
+            if decode_steps < 0:
+                break
+    return worst, ties
+
+
+def test_fast_smollm_shape_long_contexts(oracle, srlib):
+    """hd 64, 3 query heads per KV head; contexts up to 700 (3 splits)."""
+    cfg = oracle.make_config(4096, 576, 1536, 2, 9, 3, 1024, rope_theta=1e5, tied=True, weight_format="q8",
+                             page_tokens=16)
+    om = oracle.Model(cfg)
+    om.init_synthetic(3, 0.02)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, 4096, size=n).tolist() for n in (700, 300, 65, 9)]
+    worst, ties = run_pair(oracle, srlib, om, prompts, chunk=256, decode_steps=3)
+    assert worst <= FAST_ATOL
+
+
+def test_fast_mistral_shape_one_layer(oracle, srlib):
+    """hd 128, 4 query heads per KV head, Q8; contexts up to 600."""
+    cfg = oracle.make_config(2048, 4096, 14336, 1, 32, 8, 1024, rope_theta=1e6, tied=False, weight_format="q8",
+                             page_tokens=16)
+    om = oracle.Model(cfg)
+    om.init_synthetic(5, 0.02)
+    rng = np.random.default_rng(6)
+    prompts = [rng.integers(0, 2048, size=n).tolist() for n in (600, 257, 31)]
+    worst, ties = run_pair(oracle, srlib, om, prompts, chunk=300, decode_steps=2)
+    assert worst <= FAST_ATOL
+
+
+def test_fast_qwen_shape_bias_q4(oracle, srlib):
+    """hd 128, 7 query heads per KV head, QKV bias, q4-mixed."""
+    cfg = oracle.make_config(1024, 896, 1024, 1, 7, 1, 1024, rope_theta=1e6, tied=False, qkv_bias=True,
+                             weight_format="q4-mixed", page_tokens=32)
+    om = oracle.Model(cfg)
+    om.init_synthetic(8, 0.02)
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, 1024, size=n).tolist() for n in (520, 40)]
+    worst, ties = run_pair(oracle, srlib, om, prompts, chunk=200, decode_steps=2)
+    assert worst <= FAST_ATOL
