@@ -1,0 +1,328 @@
+// fast_gemm.cuh -- host side of the tensor-core projections (tc_gemm.cuh):
+// bf16 code shadows of every Q8/Q4 matrix (Q|K|V and gate|up fused row-wise),
+// TMA descriptors, split-K selection and the per-layer entry points.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <vector>
+
+#include "fast_kernels.cuh"
+#include "srstep_internal.h"
+#include "tc_gemm.cuh"
+
+namespace sr {
+
+struct TcMatrix {
+  __nv_bfloat16* w16 = nullptr;
+  float* scales = nullptr;
+  bool own_scales = false;
+  int rows = 0, cols = 0;
+  CUtensorMap map;
+};
+
+struct TcState {
+  uint64_t version = ~0ull;
+  bool disabled = false;
+  std::vector<TcMatrix> qkv, o, gateup, down;
+  TcMatrix head;
+  __nv_bfloat16* xh = nullptr;
+  __nv_bfloat16* xl = nullptr;
+  CUtensorMap xh_d, xl_d, xh_h, xl_h;
+  float* partial = nullptr;
+  size_t partial_cap = 0;
+  int* err = nullptr;
+  int* h_err = nullptr;
+  bool ran = false;
+  std::vector<void*> allocs;
+};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+    cudaGetLastError();
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor [rows][cols], box 64 x box_rows, 128-byte swizzle.
+inline bool make_map(CUtensorMap* map, void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (cols * 2) % 16 != 0 || ((uintptr_t)base) % 16 != 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline TcState* tc_state(sr_model* m) { return (TcState*)m->tc; }
+
+inline void tc_free(TcState* t) {
+  for (void* p : t->allocs) cudaFree(p);
+  t->allocs.clear();
+  if (t->h_err) cudaFreeHost(t->h_err);
+  t->h_err = nullptr;
+  t->qkv.clear();
+  t->o.clear();
+  t->gateup.clear();
+  t->down.clear();
+  t->partial = nullptr;
+  t->partial_cap = 0;
+}
+
+inline bool tc_alloc(TcState* t, void** p, size_t bytes) {
+  if (cudaMalloc(p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  t->allocs.push_back(*p);
+  return true;
+}
+
+// Build one (optionally row-fused) code shadow from parameters.
+inline bool tc_build(sr_model* m, TcState* t, TcMatrix& dst, const std::vector<const Param*>& parts) {
+  int rows = 0;
+  const int cols = parts[0]->cols;
+  for (const Param* p : parts) {
+    if (p->format == kF32 || p->cols != cols) return false;
+    rows += p->rows;
+  }
+  const int groups = (cols + kQBlock - 1) / kQBlock;
+  dst.rows = rows;
+  dst.cols = cols;
+  if (!tc_alloc(t, (void**)&dst.w16, (size_t)rows * cols * 2)) return false;
+  if (parts.size() == 1) {
+    dst.scales = parts[0]->scales;
+    dst.own_scales = false;
+  } else {
+    if (!tc_alloc(t, (void**)&dst.scales, (size_t)rows * groups * 4)) return false;
+    dst.own_scales = true;
+  }
+  int r0 = 0;
+  for (const Param* p : parts) {
+    const int64_t total = (int64_t)p->rows * cols;
+    tc::k_codes_bf16<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 64), 256, 0, m->stream>>>(
+        p->values, p->format, p->rows, cols, dst.w16 + (int64_t)r0 * cols);
+    if (dst.own_scales)
+      cudaMemcpyAsync(dst.scales + (int64_t)r0 * groups, p->scales, (size_t)p->rows * groups * 4,
+                      cudaMemcpyDeviceToDevice, m->stream);
+    r0 += p->rows;
+  }
+  return make_map(&dst.map, dst.w16, (uint64_t)cols, (uint64_t)rows, tc::kM);
+}
+
+// Lazily (re)build the shadows after the weights change.  Returns false when
+// the tensor-core path is unavailable (f32 weights, shapes, memory).
+inline bool tc_prepare(sr_model* m) {
+  if (!m->tc) {
+    TcState* t = new TcState();
+    m->tc = t;
+    m->fast_free.push_back([t]() {
+      tc_free(t);
+      delete t;
+    });
+  }
+  TcState* t = tc_state(m);
+  if (t->version == m->weights_version) return !t->disabled;
+  tc_free(t);
+  t->version = m->weights_version;
+  t->disabled = true;
+  const ModelDims& dm = m->dm;
+  if (m->d.weight_format == SR_FMT_F32 || dm.dim % 8 || dm.hidden % 8 || !encode_fn()) return false;
+  cudaFuncSetAttribute(tc::k_gemm_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
+  const int L = dm.layers;
+  t->qkv.resize(L);
+  t->o.resize(L);
+  t->gateup.resize(L);
+  t->down.resize(L);
+  for (int l = 0; l < L; l++) {
+    const Param* P = &m->params[1 + 9 * l];
+    if (!tc_build(m, t, t->qkv[l], {&P[1], &P[2], &P[3]}) || !tc_build(m, t, t->o[l], {&P[4]}) ||
+        !tc_build(m, t, t->gateup[l], {&P[6], &P[7]}) || !tc_build(m, t, t->down[l], {&P[8]})) {
+      tc_free(t);
+      return false;
+    }
+  }
+  const Param& head = m->d.tied ? m->params[0] : m->params.back();
+  if (!tc_build(m, t, t->head, {&head})) {
+    tc_free(t);
+    return false;
+  }
+  const int xcols = std::max(dm.dim, dm.hidden);
+  if (!tc_alloc(t, (void**)&t->xh, (size_t)kMaxRows * xcols * 2) ||
+      !tc_alloc(t, (void**)&t->xl, (size_t)kMaxRows * xcols * 2) || !tc_alloc(t, (void**)&t->err, 16)) {
+    tc_free(t);
+    return false;
+  }
+  cudaMemsetAsync(t->xh, 0, (size_t)kMaxRows * xcols * 2, m->stream);
+  cudaMemsetAsync(t->xl, 0, (size_t)kMaxRows * xcols * 2, m->stream);
+  cudaMemsetAsync(t->err, 0, 16, m->stream);
+  if (cudaMallocHost((void**)&t->h_err, 16) != cudaSuccess) {
+    cudaGetLastError();
+    tc_free(t);
+    return false;
+  }
+  if (!make_map(&t->xh_d, t->xh, dm.dim, kMaxRows, tc::kN) || !make_map(&t->xl_d, t->xl, dm.dim, kMaxRows, tc::kN) ||
+      !make_map(&t->xh_h, t->xh, dm.hidden, kMaxRows, tc::kN) ||
+      !make_map(&t->xl_h, t->xl, dm.hidden, kMaxRows, tc::kN)) {
+    tc_free(t);
+    return false;
+  }
+  if (cudaStreamSynchronize(m->stream) != cudaSuccess) {
+    cudaGetLastError();
+    tc_free(t);
+    return false;
+  }
+  t->disabled = false;
+  return true;
+}
+
+// Minimum step rows for the tensor-core path (below it the CUDA-core kernels run).
+constexpr int kTcMinRows = 32;
+
+inline void tc_split_x(sr_model* m, const float* X, int n, int in) {
+  TcState* t = tc_state(m);
+  const int64_t total = (int64_t)n * in;
+  tc::k_split_bf16<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 16), 256, 0, m->stream>>>(X, n, in, t->xh,
+                                                                                                   t->xl);
+}
+
+inline bool tc_gemm(sr_model* m, const TcMatrix& W, bool hidden_in, int n, tc::GemmArgs a) {
+  TcState* t = tc_state(m);
+  a.n = n;
+  a.out = W.rows;
+  a.in = W.cols;
+  a.groups = (W.cols + kQBlock - 1) / kQBlock;
+  a.scales = W.scales;
+  a.err = t->err;
+  const int mt = (W.rows + tc::kM - 1) / tc::kM, nt = (n + tc::kN - 1) / tc::kN;
+  const int tiles = mt * nt;
+  int splits = 1;
+  if (tiles < 148) splits = std::min(std::max(1, a.groups / 4), (148 + tiles - 1) / tiles);
+  while (splits > 1 && (size_t)splits * n * W.rows * 4 > ((size_t)512 << 20)) splits--;
+  int kbps = (a.groups + splits - 1) / splits;
+  splits = (a.groups + kbps - 1) / kbps;
+  a.kb_per_split = kbps;
+  a.splits = splits;
+  if (splits > 1) {
+    const size_t need = (size_t)splits * n * W.rows * 4;
+    if (need > t->partial_cap) {
+      if (t->partial) {
+        cudaFree(t->partial);
+        t->allocs.erase(std::find(t->allocs.begin(), t->allocs.end(), (void*)t->partial));
+      }
+      t->partial = nullptr;
+      t->partial_cap = 0;
+      if (!tc_alloc(t, (void**)&t->partial, need)) return false;
+      t->partial_cap = need;
+    }
+    a.partial = t->partial;
+  } else {
+    a.partial = nullptr;
+  }
+  const CUtensorMap& xh = hidden_in ? t->xh_h : t->xh_d;
+  const CUtensorMap& xl = hidden_in ? t->xl_h : t->xl_d;
+  tc::k_gemm_q<<<dim3(mt, nt, splits), tc::kThreads, tc::kSmemBytes, m->stream>>>(W.map, xh, xl, a);
+  if (splits > 1) {
+    const int64_t total = (int64_t)n * W.rows;
+    tc::k_gemm_reduce<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, m->stream>>>(a);
+  }
+  t->ran = true;
+  return true;
+}
+
+inline tc::Segment seg(int rows, float* y, int ldy, const float* bias, const float* resid) {
+  tc::Segment s;
+  s.rows = rows;
+  s.y = y;
+  s.ldy = ldy;
+  s.bias = bias;
+  s.resid = resid;
+  return s;
+}
+
+// Q|K|V in one GEMM (+ qwen2 biases).
+inline bool tc_qkv(sr_model* m, int l, int n) {
+  if (n < kTcMinRows || !tc_prepare(m)) return false;
+  const ModelDims& dm = m->dm;
+  const Param* B = m->d.qkv_bias ? &m->params[2 + 9 * dm.layers + 3 * l] : nullptr;
+  tc::GemmArgs a{};
+  a.nseg = 3;
+  a.seg[0] = seg(dm.dim, m->Q, dm.dim, B ? (const float*)B[0].values : nullptr, nullptr);
+  a.seg[1] = seg(dm.kvd, m->K, dm.kvd, B ? (const float*)B[1].values : nullptr, nullptr);
+  a.seg[2] = seg(dm.kvd, m->V, dm.kvd, B ? (const float*)B[2].values : nullptr, nullptr);
+  a.out_map = nullptr;
+  tc_split_x(m, m->N, n, dm.dim);
+  return tc_gemm(m, tc_state(m)->qkv[l], false, n, a);
+}
+// gate|up in one GEMM.
+inline bool tc_gateup(sr_model* m, int l, int n) {
+  if (n < kTcMinRows || !tc_prepare(m)) return false;
+  const ModelDims& dm = m->dm;
+  tc::GemmArgs a{};
+  a.nseg = 2;
+  a.seg[0] = seg(dm.hidden, m->G, dm.hidden, nullptr, nullptr);
+  a.seg[1] = seg(dm.hidden, m->U, dm.hidden, nullptr, nullptr);
+  a.out_map = nullptr;
+  tc_split_x(m, m->N, n, dm.dim);
+  return tc_gemm(m, tc_state(m)->gateup[l], false, n, a);
+}
+// O / down projection with the residual add (X += W x).
+inline bool tc_resid(sr_model* m, const TcMatrix& W, const float* X, int n, bool hidden_in) {
+  const ModelDims& dm = m->dm;
+  tc::GemmArgs a{};
+  a.nseg = 1;
+  a.seg[0] = seg(dm.dim, m->X, dm.dim, nullptr, m->X);
+  a.out_map = nullptr;
+  tc_split_x(m, X, n, hidden_in ? dm.hidden : dm.dim);
+  return tc_gemm(m, W, hidden_in, n, a);
+}
+inline bool tc_o(sr_model* m, int l, int n) {
+  if (n < kTcMinRows || !tc_prepare(m)) return false;
+  return tc_resid(m, tc_state(m)->o[l], m->A, n, false);
+}
+inline bool tc_down(sr_model* m, int l, int n) {
+  if (n < kTcMinRows || !tc_prepare(m)) return false;
+  return tc_resid(m, tc_state(m)->down[l], m->H, n, true);
+}
+inline bool tc_head(sr_model* m, int heads) {
+  if (heads < kTcMinRows || !tc_prepare(m)) return false;
+  const ModelDims& dm = m->dm;
+  tc::GemmArgs a{};
+  a.nseg = 1;
+  a.seg[0] = seg(dm.vocab, m->logits, dm.vocab, nullptr, nullptr);
+  a.out_map = m->meta.head_dst;
+  tc_split_x(m, m->N, heads, dm.dim);
+  return tc_gemm(m, tc_state(m)->head, false, heads, a);
+}
+
+// After the step's stream synchronize: SR_ETIMEOUT if a bounded wait expired.
+inline int tc_check(sr_model* m) {
+  TcState* t = tc_state(m);
+  if (!t || !t->ran) return SR_OK;
+  t->ran = false;
+  if (cudaMemcpy(t->h_err, t->err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return sr_fail(SR_EDEVICE, "reading the tensor-core error flag failed");
+  }
+  if (*t->h_err) {
+    cudaMemset(t->err, 0, 4);
+    return sr_fail(SR_ETIMEOUT, "a tensor-core pipeline wait expired; results of this step are invalid");
+  }
+  return SR_OK;
+}
+
+}  // namespace sr

@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "exact_kernels.cuh"
 #include "fast_kernels.cuh"
+#include "fast_gemm.cuh"
 #include "sampler.cuh"
 #include "srstep_internal.h"
 
@@ -658,32 +659,41 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     SR_LAUNCH(m, SR_PROF_NORM,
               if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps));
-    o.y = m->Q; o.ldy = d; o.bias = B ? (const float*)B[0].values : nullptr;
-    sr_launch_linear(m, m->N, n, P[1], o);
-    o.y = m->K; o.ldy = kd; o.bias = B ? (const float*)B[1].values : nullptr;
-    sr_launch_linear(m, m->N, n, P[2], o);
-    o.y = m->V; o.ldy = kd; o.bias = B ? (const float*)B[2].values : nullptr;
-    sr_launch_linear(m, m->N, n, P[3], o);
+    bool done;
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_qkv(m, l, n));
+    if (!done) {
+      o.y = m->Q; o.ldy = d; o.bias = B ? (const float*)B[0].values : nullptr;
+      sr_launch_linear(m, m->N, n, P[1], o);
+      o.y = m->K; o.ldy = kd; o.bias = B ? (const float*)B[1].values : nullptr;
+      sr_launch_linear(m, m->N, n, P[2], o);
+      o.y = m->V; o.ldy = kd; o.bias = B ? (const float*)B[2].values : nullptr;
+      sr_launch_linear(m, m->N, n, P[3], o);
+    }
     SR_LAUNCH(m, SR_PROF_ROPE_KV,
               k_rope_kv_exact<<<n, 128, 0, s>>>(m->Q, m->K, m->V, m->cos_t, m->sin_t, m->meta, pool->data, dm, l));
     SR_LAUNCH(m, SR_PROF_ATTENTION,
               if (fast) fast_attention(m, pool, n, info.max_len, l);
               else launch_attention_exact(m, pool, n, info.max_len, l));
     o.y = m->X; o.ldy = d; o.bias = nullptr; o.resid = m->X;
-    sr_launch_linear(m, m->A, n, P[4], o);
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_o(m, l, n));
+    if (!done) sr_launch_linear(m, m->A, n, P[4], o);
     SR_LAUNCH(m, SR_PROF_NORM,
               if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps));
     o.resid = nullptr;
-    o.y = m->G; o.ldy = dm.hidden;
-    sr_launch_linear(m, m->N, n, P[6], o);
-    o.y = m->U;
-    sr_launch_linear(m, m->N, n, P[7], o);
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_gateup(m, l, n));
+    if (!done) {
+      o.y = m->G; o.ldy = dm.hidden;
+      sr_launch_linear(m, m->N, n, P[6], o);
+      o.y = m->U;
+      sr_launch_linear(m, m->N, n, P[7], o);
+    }
     int64_t cnt = (int64_t)n * dm.hidden;
     SR_LAUNCH(m, SR_PROF_SWIGLU,
               k_swiglu_exact<<<(int)std::min<int64_t>((cnt + 255) / 256, 148 * 16), 256, 0, s>>>(m->G, m->U, m->H, cnt));
     o.y = m->X; o.ldy = d; o.resid = m->X;
-    sr_launch_linear(m, m->H, n, P[8], o);
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_down(m, l, n));
+    if (!done) sr_launch_linear(m, m->H, n, P[8], o);
   }
   // Selected head (M:6420-6448): gather last rows, final norm, LM head into
   // the session's logits row; unselected rows are zero.
@@ -701,7 +711,9 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     o.bias = nullptr;
     o.resid = nullptr;
     o.out_map = m->meta.head_dst;
-    sr_launch_linear(m, m->N, info.heads, head, o, SR_PROF_HEAD);
+    bool done;
+    SR_LAUNCH(m, SR_PROF_HEAD, done = fast && tc_head(m, info.heads));
+    if (!done) sr_launch_linear(m, m->N, info.heads, head, o, SR_PROF_HEAD);
   }
   CK(cudaGetLastError());
   return SR_OK;
@@ -724,7 +736,7 @@ extern "C" int sr_step(sr_model* m, sr_kvpool* pool, const sr_batch* batch, floa
                        m->stream));
   CK(cudaStreamSynchronize(m->stream));
   sr_prof_resolve(m);
-  return SR_OK;
+  return tc_check(m);
 }
 
 extern "C" int sr_step_logits(sr_model* m, const float** device_logits) {
@@ -798,6 +810,7 @@ int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const
 int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_out) {
   CK(cudaStreamSynchronize(m->stream));
   sr_prof_resolve(m);
+  if (int rc = tc_check(m)) return rc;
   uint8_t* h = (uint8_t*)m->h_stage + m->upload_ints * 4;
   const size_t off_hoff = kSampOffHistOff, off_hist = kSampOffHist, off_rng = kSampOffRng, off_ids = kSampOffIds,
                off_status = kSampOffStatus;

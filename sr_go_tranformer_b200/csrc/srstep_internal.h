@@ -75,6 +75,7 @@ struct sr_model {
   Profiler prof;
   // fast-mode state (owned by fast_kernels.cuh)
   void* fast = nullptr;
+  void* tc = nullptr;  // tensor-core shadows (fast_gemm.cuh)
   std::vector<std::function<void()>> fast_free;
 };
 

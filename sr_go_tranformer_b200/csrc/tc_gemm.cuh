@@ -262,13 +262,13 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
     if (o < a.out) {
       if (a.splits > 1) {
         float* P = a.partial + (int64_t)split * a.n * a.out;
-#pragma unroll 4
+#pragma unroll
         for (int j = 0; j < kN; j++) {
           const int row = n0 + j;
           if (row < a.n) P[(int64_t)row * a.out + o] = acc[j];
         }
       } else {
-#pragma unroll 4
+#pragma unroll
         for (int j = 0; j < kN; j++) {
           const int row = n0 + j;
           if (row < a.n) store_out(a, row, o, acc[j]);
