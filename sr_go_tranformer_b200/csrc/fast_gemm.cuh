@@ -198,6 +198,7 @@ inline void tc_split_x(sr_model* m, const float* X, int n, int in) {
   const int64_t total = (int64_t)n * in;
   tc::k_split_bf16<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 16), 256, 0, m->stream>>>(X, n, in, t->xh,
                                                                                                    t->xl);
+  sr_count_launch(m);
 }
 
 inline bool tc_gemm(sr_model* m, const TcMatrix& W, bool hidden_in, int n, tc::GemmArgs a) {
@@ -235,10 +236,12 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, bool hidden_in, int n, tc::G
   }
   const CUtensorMap& xh = hidden_in ? t->xh_h : t->xh_d;
   const CUtensorMap& xl = hidden_in ? t->xl_h : t->xl_d;
-  tc::k_gemm_q<<<dim3(mt, nt, splits), tc::kThreads, tc::kSmemBytes, m->stream>>>(W.map, xh, xl, a);
+  tc::k_gemm_q<<<dim3(nt, mt, splits), tc::kThreads, tc::kSmemBytes, m->stream>>>(W.map, xh, xl, a);
+  sr_count_launch(m);
   if (splits > 1) {
     const int64_t total = (int64_t)n * W.rows;
     tc::k_gemm_reduce<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, m->stream>>>(a);
+    sr_count_launch(m);
   }
   t->ran = true;
   return true;

@@ -613,6 +613,7 @@ void sr_launch_linear(sr_model* m, const float* X, int n, const Param& W, Linear
   ProfScope ps(m, cls);
   if (m->mode == SR_MODE_FAST && fast_linear(m, X, n, W, O)) return;
   launch_linear_exact(m, X, n, W, O);
+  sr_count_launch(m);
 }
 
 static void launch_attention_exact(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer) {
@@ -631,6 +632,7 @@ static void launch_attention_exact(sr_model* m, sr_kvpool* pool, int n, int max_
   AttnSmem lay(dm.group, dm.hd, a.smem_scores, a.ls);
   int threads = std::max(128, ((dm.group * dm.hd / 4 + 31) / 32) * 32);
   k_attention_exact<<<dim3(n, dm.kv_heads), threads, (size_t)lay.total * 4, m->stream>>>(a);
+  sr_count_launch(m);
 }
 
 int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel) {
@@ -641,6 +643,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   sr_prof_span_begin(m);
   SR_LAUNCH(m, SR_PROF_META, k_meta<<<1, 1024, 0, s>>>(m->meta, info.sessions, n));
   SR_LAUNCH(m, SR_PROF_EMBED, k_embed<<<n, 256, 0, s>>>(m->params[0], m->meta.tokens, m->X, d));
+  sr_count_launch(m, 2);
   const int norm_blocks = (n + kNormWarps - 1) / kNormWarps;
   const bool fast = m->mode == SR_MODE_FAST;
   for (int l = 0; l < L; l++) {
@@ -671,6 +674,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     }
     SR_LAUNCH(m, SR_PROF_ROPE_KV,
               k_rope_kv_exact<<<n, 128, 0, s>>>(m->Q, m->K, m->V, m->cos_t, m->sin_t, m->meta, pool->data, dm, l));
+    sr_count_launch(m, 3);  // two norms and RoPE/KV of this layer
     SR_LAUNCH(m, SR_PROF_ATTENTION,
               if (fast) fast_attention(m, pool, n, info.max_len, l);
               else launch_attention_exact(m, pool, n, info.max_len, l));
@@ -691,6 +695,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     int64_t cnt = (int64_t)n * dm.hidden;
     SR_LAUNCH(m, SR_PROF_SWIGLU,
               k_swiglu_exact<<<(int)std::min<int64_t>((cnt + 255) / 256, 148 * 16), 256, 0, s>>>(m->G, m->U, m->H, cnt));
+    sr_count_launch(m);
     o.y = m->X; o.ldy = d; o.resid = m->X;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_down(m, l, n));
     if (!done) sr_launch_linear(m, m->H, n, P[8], o);
@@ -701,6 +706,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   if (info.heads > 0) {
     const Param& F = m->params[1 + 9 * L];
     const int hb = (info.heads + kNormWarps - 1) / kNormWarps;
+    sr_count_launch(m);
     SR_LAUNCH(m, SR_PROF_HEAD,
               if (fast) fast_rmsnorm(m, m->X, m->meta.head_src, (const float*)F.values, m->N, info.heads, d, eps);
               else k_rmsnorm_exact<<<hb, kNormWarps * 32, 0, s>>>(m->X, m->meta.head_src, (const float*)F.values, m->N, info.heads, d, eps));
@@ -799,6 +805,7 @@ int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const
   a.status = (int32_t*)(dv + off_status);
   size_t smem = (size_t)((m->dm.vocab + 31) / 32) * 4;
   SR_LAUNCH(m, SR_PROF_SAMPLE, k_sample<<<n, kSampleThreads, smem, m->stream>>>(a));
+  sr_count_launch(m);
   CK(cudaGetLastError());
   sr_prof_span_end(m);
   // results: rng | ids | status are contiguous -> one copy back

@@ -87,6 +87,10 @@ struct sr_kvpool {
 
 int sr_fail(int code, const std::string& msg);
 
+// Every kernel launch of a step increments this counter (the benchmark's
+// gpu_launches); class scopes below may cover several launches.
+inline void sr_count_launch(sr_model* m, int k = 1) { m->prof.total_launches += k; }
+
 // RAII scope around one kernel launch: counts it and, when its class is
 // selected, brackets it with a pair of events on the model's stream.
 struct ProfScope {
@@ -107,7 +111,6 @@ struct ProfScope {
   ~ProfScope() {
     Profiler& p = m->prof;
     p.launches[cls]++;
-    p.total_launches++;
     if (timed) {
       cudaEventRecord(p.events[p.used + 1], m->stream);
       p.used += 2;

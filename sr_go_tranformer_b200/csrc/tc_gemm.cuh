@@ -29,7 +29,8 @@ constexpr int kM = 128;          // output features per tile (MMA M)
 constexpr int kN = 128;          // step rows per tile (MMA N)
 constexpr int kKB = 64;          // K per block (one scale block, one 128-byte bf16 row)
 constexpr int kStages = 4;
-constexpr int kThreads = 192;    // warp 0: TMA, warp 1: MMA, warps 2-5: epilogue
+constexpr int kThreads = 320;    // warp 0: TMA, warp 1: MMA, warps 2-9: epilogue
+constexpr int kEpiWarps = 8;     // two warps per TMEM lane quarter, 64 columns each
 constexpr uint32_t kTileA = kM * kKB * 2;  // 16 KiB
 constexpr uint32_t kTileB = kN * kKB * 2;  // 16 KiB
 constexpr uint32_t kStageBytes = kTileA + 2 * kTileB;
@@ -163,7 +164,7 @@ __device__ __forceinline__ void store_out(const GemmArgs& a, int row, int o, flo
   *dst = v;
 }
 
-// grid: (ceil(out/128), ceil(n/128), splits)
+// grid: (ceil(n/128), ceil(out/128), splits): the row tiles of one weight tile run together (L2 reuse)
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xh,
          const __grid_constant__ CUtensorMap tm_xl, GemmArgs a) {
@@ -176,7 +177,7 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
   uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kM, n0 = blockIdx.y * kN, split = blockIdx.z;
+  const int m0 = blockIdx.y * kM, n0 = blockIdx.x * kN, split = blockIdx.z;
   const int kb0 = split * a.kb_per_split;
   const int kb1 = min(a.groups, kb0 + a.kb_per_split);
   const int nkb = max(0, kb1 - kb0);
@@ -188,7 +189,7 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty[b], kEpiWarps);  // one arrive per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -234,43 +235,44 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
         umma_commit(&tfull[b]);
       }
     }
-  } else {  // epilogue warps 2..5: TMEM lane quarter = warp % 4
-    const int q = warp & 3;
+  } else {  // epilogue warps 2..9: TMEM lane quarter = warp % 4, column half = (warp - 2) / 4
+    const int q = warp & 3, h = (warp - 2) >> 2;
     const int o = m0 + q * 32 + lane;
-    float acc[kN];
+    constexpr int NC = kN / 2;
+    float acc[NC];
 #pragma unroll
-    for (int j = 0; j < kN; j++) acc[j] = 0.f;
+    for (int j = 0; j < NC; j++) acc[j] = 0.f;
     const float* srow = a.scales + (int64_t)min(o, a.out - 1) * a.groups;
     for (int i = 0; i < nkb; i++) {
       const int b = i & 1;
       const float sc = srow[kb0 + i];
       if (!mbar_wait(&tfull[b], (i >> 1) & 1, a.err)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * kN;
-#pragma unroll
-      for (int c = 0; c < kN; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(taddr + c, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; j++) acc[c + j] = fmaf(__uint_as_float(v[j]), sc, acc[c + j]);
-      }
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * kN + h * NC;
+      uint32_t v0[32], v1[32];
+      tmem_ld32(taddr, v0);
+      tmem_ld32(taddr + 32, v1);
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
+#pragma unroll
+      for (int j = 0; j < 32; j++) acc[j] = fmaf(__uint_as_float(v0[j]), sc, acc[j]);
+#pragma unroll
+      for (int j = 0; j < 32; j++) acc[32 + j] = fmaf(__uint_as_float(v1[j]), sc, acc[32 + j]);
     }
     if (o < a.out) {
       if (a.splits > 1) {
         float* P = a.partial + (int64_t)split * a.n * a.out;
 #pragma unroll
-        for (int j = 0; j < kN; j++) {
-          const int row = n0 + j;
+        for (int j = 0; j < NC; j++) {
+          const int row = n0 + h * NC + j;
           if (row < a.n) P[(int64_t)row * a.out + o] = acc[j];
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < kN; j++) {
-          const int row = n0 + j;
+        for (int j = 0; j < NC; j++) {
+          const int row = n0 + h * NC + j;
           if (row < a.n) store_out(a, row, o, acc[j]);
         }
       }
