@@ -1,13 +1,19 @@
 // fast_attention.cuh -- SR_MODE_FAST paged GQA attention (flash-decoding).
 //
 // Same mathematics as attend (cmd/monolith/monolith.go:5293-5352), reordered
-// for the B200: every (row, KV head) context is cut into splits of kSplit
-// positions, one CTA per split.  A CTA stages K/V tiles of kTile positions
-// from the page pool into shared memory with cp.async (double-buffered),
-// computes the `group` query heads' scores with FFMA, and keeps an online
-// softmax (running max, rescaled sum and output).  A combine kernel merges the
-// splits with their log-sum-exp weights.  Results match the exact path within
-// fp32 rounding (tolerance-checked), not bit for bit.
+// for the B200.  Every (row, KV head) context is cut into splits of kFaSplit
+// positions, one CTA per split; the `group` query heads that share a KV head
+// read each K/V element once (GQA), keep an online softmax (running max,
+// rescaled sum and output) and write the split's (O, m, l); a combine kernel
+// merges the splits with their log-sum-exp weights.  Results match the exact
+// path within fp32 rounding (tolerance-checked), not bit for bit.
+//
+// head_dim 128 (Mistral, Qwen): k_attn_warp128 -- each of the 4 warps streams
+//   its own 64-position sub-split through a private 2-stage cp.async ring of
+//   8-position tiles and keeps its own softmax state, synchronising with
+//   __syncwarp only; the warps merge once at the end of the split.
+// head_dim 64 (SmolLM, Llama-1B): k_attn_tile -- the CTA shares 32-position
+//   double-buffered tiles.
 #pragma once
 
 #include <float.h>
@@ -16,7 +22,6 @@
 namespace sr {
 
 constexpr int kFaThreads = 128;
-constexpr int kFaTile = 32;    // positions per shared-memory tile
 constexpr int kFaSplit = 256;  // positions per CTA
 
 struct FastAttnArgs {
@@ -37,9 +42,231 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
 
-// Stage K and V rows of positions [t0, t0+tn) (tn <= kFaTile) of one KV head.
+__device__ __forceinline__ void fa_write_split(const FastAttnArgs& a, int r, int kh, int split, int G, int HD,
+                                               const float* o_smem, const float* ml_smem) {
+  const int64_t item = ((int64_t)r * a.dm.kv_heads + kh) * a.max_splits + split;
+  for (int idx = threadIdx.x; idx < G * HD; idx += kFaThreads) a.part_o[item * G * HD + idx] = o_smem[idx];
+  if (threadIdx.x < 2 * G) a.part_ml[item * G * 2 + threadIdx.x] = ml_smem[threadIdx.x];
+}
+
+// ===================================================== head_dim 128: per warp
+constexpr int kWpMT = 8;                 // positions per warp tile
+constexpr int kWpSub = kFaSplit / 4;     // positions per warp
+
+template <int G>
+struct WarpSmem {
+  static constexpr int HD = 128;
+  static constexpr int GP = (G + 3) & ~3;
+  static constexpr int KV = 2 * 2 * kWpMT * HD;   // [stage][K|V][pos][HD]
+  static constexpr int SC = G * kWpMT;            // scores [G][MT]
+  static constexpr int PS = kWpMT * GP;           // probabilities [MT][GP]
+  static constexpr int PER_WARP = KV + SC + PS;
+  static constexpr int TOTAL = 4 * PER_WARP;      // floats
+};
+
+template <int G>
+__global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
+  constexpr int HD = 128, MT = kWpMT, GP = WarpSmem<G>::GP;
+  constexpr int ROUNDS = (G + 3) / 4;  // softmax passes: 4 heads x 8 positions per pass
+  extern __shared__ __align__(16) float fsm[];
+  const int split = blockIdx.x, r = blockIdx.y, kh = blockIdx.z;
+  const int L = a.meta.row_pos[r] + 1;
+  const int s0 = split * kFaSplit;
+  if (s0 >= L) return;
+  const int s1 = min(L, s0 + kFaSplit);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* wsm = fsm + warp * WarpSmem<G>::PER_WARP;
+  float* kv = wsm;                                 // [2][2][MT][HD]
+  float* sc = wsm + WarpSmem<G>::KV;               // [G][MT]
+  float* ps = sc + WarpSmem<G>::SC;                // [MT][GP]
+  const int pbase = a.meta.row_pbase[r];
+  const int pt = a.dm.page_tokens;
+  const int64_t lay = (int64_t)a.layer * 2 * pt * a.dm.kvd + (int64_t)kh * HD;
+  const int64_t vofs = (int64_t)pt * a.dm.kvd;
+  const int ws0 = s0 + warp * kWpSub;
+  const int ws1 = min(s1, ws0 + kWpSub);
+  const int nw = max(0, ws1 - ws0);
+  const int ntiles = (nw + MT - 1) / MT;
+
+  // lane copies 16-byte chunk `lane` of each K and V row of a tile
+  auto load_tile = [&](int t) {
+    float* dst = kv + (t & 1) * 2 * MT * HD;
+    const int t0 = ws0 + t * MT, tn = min(MT, ws1 - t0);
+    for (int s = 0; s < tn; s++) {
+      const int pos = t0 + s;
+      const int64_t page = a.meta.page_ids[pbase + pos / pt];
+      const float* krow = a.pool + page * a.dm.page_elems + lay + (int64_t)(pos % pt) * a.dm.kvd + 4 * lane;
+      cp_async16(dst + s * HD + 4 * lane, krow);
+      cp_async16(dst + (MT + s) * HD + 4 * lane, krow + vofs);
+    }
+  };
+  if (ntiles > 0) load_tile(0);
+  cp_async_commit();
+
+  // query slices: lane covers dims 4*(lane%8) + 32*i for the score phase
+  float4 q[G][4];
+  {
+    const float* qrow = a.Q + (int64_t)r * a.dm.dim + (int64_t)kh * G * HD;
+    const int jl = lane & 7;
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float4 v = *(const float4*)(qrow + g * HD + 4 * jl + 32 * i);
+        q[g][i] = make_float4(v.x * a.scale, v.y * a.scale, v.z * a.scale, v.w * a.scale);
+      }
+  }
+  float mreg[ROUNDS], lreg[ROUNDS];  // softmax state of head (lane/8 + 4*round), replicated in its 8 lanes
+#pragma unroll
+  for (int k = 0; k < ROUNDS; k++) {
+    mreg[k] = -INFINITY;
+    lreg[k] = 0.f;
+  }
+  float4 acc[G];  // output dims 4*lane..4*lane+3 of every head
+#pragma unroll
+  for (int g = 0; g < G; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  for (int t = 0; t < ntiles; t++) {
+    __syncwarp();  // the stage about to be refilled has been consumed
+    if (t + 1 < ntiles) {
+      load_tile(t + 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncwarp();
+    const float* kt = kv + (t & 1) * 2 * MT * HD;
+    const float* vt = kt + MT * HD;
+    const int tn = min(MT, ws1 - (ws0 + t * MT));
+    // scores: 8 lanes per position, 4 positions per pass, 2 passes
+#pragma unroll
+    for (int pass = 0; pass < 2; pass++) {
+      const int s = pass * 4 + (lane >> 3);
+      float part[G];
+#pragma unroll
+      for (int g = 0; g < G; g++) part[g] = 0.f;
+      if (s < tn) {
+        const float* kr = kt + s * HD + 4 * (lane & 7);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float4 kx = *(const float4*)(kr + 32 * i);
+#pragma unroll
+          for (int g = 0; g < G; g++) {
+            part[g] = fmaf(q[g][i].x, kx.x, part[g]);
+            part[g] = fmaf(q[g][i].y, kx.y, part[g]);
+            part[g] = fmaf(q[g][i].z, kx.z, part[g]);
+            part[g] = fmaf(q[g][i].w, kx.w, part[g]);
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1)
+#pragma unroll
+        for (int g = 0; g < G; g++) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+      if ((lane & 7) == 0)
+#pragma unroll
+        for (int g = 0; g < G; g++) sc[g * MT + s] = s < tn ? part[g] : -INFINITY;
+    }
+    __syncwarp();
+    // online softmax: lane = (head lane/8 + 4*round, position lane%8)
+    float alpha[ROUNDS];
+#pragma unroll
+    for (int k = 0; k < ROUNDS; k++) {
+      const int g = (lane >> 3) + 4 * k;
+      const float v = g < G ? sc[g * MT + (lane & 7)] : -INFINITY;
+      float mt = v;
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float mo = mreg[k];
+      const float mn = fmaxf(mo, mt);
+      const float p = (v == -INFINITY) ? 0.f : __expf(v - mn);
+      float sum = p;
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      const float al = (mo == -INFINITY) ? 0.f : __expf(mo - mn);
+      lreg[k] = lreg[k] * al + sum;
+      mreg[k] = mn;
+      alpha[k] = al;
+      if (g < G) ps[(lane & 7) * GP + g] = p;
+    }
+    __syncwarp();
+    // rescale and accumulate P.V: lane owns dims 4*lane..4*lane+3
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      const float al = __shfl_sync(0xffffffffu, alpha[g / 4], (g % 4) * 8);
+      acc[g].x *= al;
+      acc[g].y *= al;
+      acc[g].z *= al;
+      acc[g].w *= al;
+    }
+    for (int s = 0; s < tn; s++) {
+      const float4 v = *(const float4*)(vt + s * HD + 4 * lane);
+      const float* pp = ps + s * GP;
+#pragma unroll
+      for (int g4 = 0; g4 < GP; g4 += 4) {
+        const float4 p4 = *(const float4*)(pp + g4);
+        const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          if (g4 + j < G) {
+            acc[g4 + j].x = fmaf(pv[j], v.x, acc[g4 + j].x);
+            acc[g4 + j].y = fmaf(pv[j], v.y, acc[g4 + j].y);
+            acc[g4 + j].z = fmaf(pv[j], v.z, acc[g4 + j].z);
+            acc[g4 + j].w = fmaf(pv[j], v.w, acc[g4 + j].w);
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+  // merge the 4 warps of the split: O_w, m_w, l_w -> (O, m, l)
+  __syncthreads();
+  float* mo = fsm;                        // [4][G][HD]
+  float* mml = fsm + 4 * G * HD;          // [4][G][2]
+#pragma unroll
+  for (int g = 0; g < G; g++) *(float4*)(mo + (warp * G + g) * HD + 4 * lane) = acc[g];
+#pragma unroll
+  for (int k = 0; k < ROUNDS; k++) {
+    const int g = (lane >> 3) + 4 * k;
+    if ((lane & 7) == 0 && g < G) {
+      mml[(warp * G + g) * 2] = mreg[k];
+      mml[(warp * G + g) * 2 + 1] = lreg[k];
+    }
+  }
+  __syncthreads();
+  float* out = fsm + 4 * G * HD + 8 * G;  // [G][HD] then [G][2]
+  for (int idx = tid; idx < G * HD; idx += kFaThreads) {
+    const int g = idx / HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; w++) M = fmaxf(M, mml[(w * G + g) * 2]);
+    float o = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+      const float mw = mml[(w * G + g) * 2];
+      const float e = (mw == -INFINITY) ? 0.f : __expf(mw - M);
+      o += e * mo[(w * G + g) * HD + (idx % HD)];
+      l += e * mml[(w * G + g) * 2 + 1];
+    }
+    out[idx] = o;
+    if (idx % HD == 0) {
+      out[G * HD + 2 * g] = M;
+      out[G * HD + 2 * g + 1] = l;
+    }
+  }
+  __syncthreads();
+  fa_write_split(a, r, kh, split, G, HD, out, out + G * HD);
+}
+
+// ====================================================== head_dim 64: per CTA
+constexpr int kFaTile = 32;
+
 template <int HD>
 __device__ __forceinline__ void fa_load_tile(const FastAttnArgs& a, float* ks, float* vs, int pbase, int kh, int t0,
                                              int tn) {
@@ -56,13 +283,11 @@ __device__ __forceinline__ void fa_load_tile(const FastAttnArgs& a, float* ks, f
 }
 
 template <int HD, int G>
-__global__ void __launch_bounds__(kFaThreads) k_attn_split(FastAttnArgs a) {
-  static_assert(HD == 64 || HD == 128, "head_dim");
-  static_assert(G >= 1 && G <= 8, "group");
-  constexpr int LPP = HD / 16;        // lanes per position in the score phase
-  constexpr int PPW = 32 / LPP;       // positions per warp per pass
-  constexpr int PPAR = kFaThreads / HD;  // position-parallel groups in the PV phase
-  constexpr int GP = (G + 3) & ~3;    // padded group (float4 p loads)
+__global__ void __launch_bounds__(kFaThreads) k_attn_tile(FastAttnArgs a) {
+  constexpr int LPP = HD / 16;
+  constexpr int PPW = 32 / LPP;
+  constexpr int PPAR = kFaThreads / HD;
+  constexpr int GP = (G + 3) & ~3;
   extern __shared__ __align__(16) float fsm[];
   float* ks = fsm;                          // [2][kFaTile][HD]
   float* vs = ks + 2 * kFaTile * HD;        // [2][kFaTile][HD]
@@ -71,7 +296,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_split(FastAttnArgs a) {
   float* alpha_s = ps + kFaTile * GP;       // [GP]
   float* m_s = alpha_s + GP;                // [GP]
   float* l_s = m_s + GP;                    // [GP]
-  float* red = l_s + GP;                    // [PPAR][G][HD] partial outputs
+  float* red = fsm;                         // reuses the tiles after the loop
 
   const int split = blockIdx.x, r = blockIdx.y, kh = blockIdx.z;
   const int L = a.meta.row_pos[r] + 1;
@@ -80,8 +305,6 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_split(FastAttnArgs a) {
   const int s1 = min(L, s0 + kFaSplit);
   const int pbase = a.meta.row_pbase[r];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  // query slices in registers: lane covers dims 4*(lane%LPP) + 4*LPP*i, i < 4
   float4 q[G][4];
   {
     const float* qrow = a.Q + (int64_t)r * a.dm.dim + (int64_t)kh * G * HD;
@@ -102,7 +325,6 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_split(FastAttnArgs a) {
   float acc[G];
 #pragma unroll
   for (int g = 0; g < G; g++) acc[g] = 0.f;
-
   const int ntiles = (s1 - s0 + kFaTile - 1) / kFaTile;
   fa_load_tile<HD>(a, ks, vs, pbase, kh, s0, min(kFaTile, s1 - s0));
   cp_async_commit();
@@ -110,7 +332,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_split(FastAttnArgs a) {
     const int t0 = s0 + t * kFaTile, tn = min(kFaTile, s1 - t0);
     float* kt = ks + (t & 1) * kFaTile * HD;
     float* vt = vs + (t & 1) * kFaTile * HD;
-    cp_async_wait_all();
+    cp_async_wait<0>();
     __syncthreads();
     if (t + 1 < ntiles) {
       const int n0 = t0 + kFaTile;
@@ -118,7 +340,6 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_split(FastAttnArgs a) {
                        min(kFaTile, s1 - n0));
     }
     cp_async_commit();
-    // scores: warp w handles positions w*PPW*k + lane/LPP
     for (int base = warp * PPW; base < kFaTile; base += 4 * PPW) {
       const int s = base + lane / LPP;
       const int jl = lane % LPP;
@@ -129,22 +350,21 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_split(FastAttnArgs a) {
         const float* kr = kt + s * HD + 4 * jl;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-          float4 kv = *(const float4*)(kr + 4 * LPP * i);
+          float4 kx = *(const float4*)(kr + 4 * LPP * i);
 #pragma unroll
           for (int g = 0; g < G; g++)
-            part[g] += q[g][i].x * kv.x + q[g][i].y * kv.y + q[g][i].z * kv.z + q[g][i].w * kv.w;
+            part[g] += q[g][i].x * kx.x + q[g][i].y * kx.y + q[g][i].z * kx.z + q[g][i].w * kx.w;
         }
       }
 #pragma unroll
       for (int off = 1; off < LPP; off <<= 1)
 #pragma unroll
         for (int g = 0; g < G; g++) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
-      if (jl == 0 && s < kFaTile)
+      if (jl == 0)
 #pragma unroll
         for (int g = 0; g < G; g++) sc[g * kFaTile + s] = s < tn ? part[g] : -INFINITY;
     }
     __syncthreads();
-    // online softmax per head: warp w handles heads w, w+4
     for (int g = warp; g < G; g += 4) {
       const float v = sc[g * kFaTile + lane];
       float mt = v;
@@ -152,20 +372,19 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_split(FastAttnArgs a) {
       for (int off = 16; off > 0; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
       const float mo = m_s[g];
       const float mn = fmaxf(mo, mt);
-      const float p = (v == -INFINITY) ? 0.f : expf(v - mn);
+      const float p = (v == -INFINITY) ? 0.f : __expf(v - mn);
       float sum = p;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
       ps[lane * GP + g] = p;
       if (lane == 0) {
-        const float al = (mo == -INFINITY) ? 0.f : expf(mo - mn);
+        const float al = (mo == -INFINITY) ? 0.f : __expf(mo - mn);
         alpha_s[g] = al;
         m_s[g] = mn;
         l_s[g] = l_s[g] * al + sum;
       }
     }
     __syncthreads();
-    // PV: thread (d, par) accumulates positions par, par+PPAR, ...
 #pragma unroll
     for (int g = 0; g < G; g++) acc[g] *= alpha_s[g];
     for (int s = par; s < tn; s += PPAR) {
@@ -175,22 +394,27 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_split(FastAttnArgs a) {
       for (int g = 0; g < G; g++) acc[g] += pp[g] * v;
     }
   }
-  // merge position-parallel partials and write this split's (O, m, l)
+  cp_async_wait<0>();
   __syncthreads();
+  float ml[2 * 8];
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    ml[2 * g] = m_s[g];
+    ml[2 * g + 1] = l_s[g];
+  }
 #pragma unroll
   for (int g = 0; g < G; g++) red[(par * G + g) * HD + d] = acc[g];
   __syncthreads();
-  const int64_t item = ((int64_t)r * a.dm.kv_heads + kh) * a.max_splits + split;
+  float* out = fsm + PPAR * G * HD;
   for (int idx = tid; idx < G * HD; idx += kFaThreads) {
     float v = 0.f;
 #pragma unroll
     for (int p = 0; p < PPAR; p++) v += red[p * G * HD + idx];
-    a.part_o[item * G * HD + idx] = v;
+    out[idx] = v;
   }
-  if (tid < G) {
-    a.part_ml[(item * G + tid) * 2] = m_s[tid];
-    a.part_ml[(item * G + tid) * 2 + 1] = l_s[tid];
-  }
+  if (tid < 2 * G) out[G * HD + tid] = ml[tid];
+  __syncthreads();
+  fa_write_split(a, r, kh, split, G, HD, out, out + G * HD);
 }
 
 // Merge the splits of each (row, query head) and write the attention output.
@@ -205,7 +429,8 @@ __global__ void __launch_bounds__(HD) k_attn_combine(FastAttnArgs a) {
   for (int s = 0; s < ns; s++) M = fmaxf(M, a.part_ml[((base + s) * G + g) * 2]);
   float den = 0.f, num = 0.f;
   for (int s = 0; s < ns; s++) {
-    const float w = expf(a.part_ml[((base + s) * G + g) * 2] - M);
+    const float ms = a.part_ml[((base + s) * G + g) * 2];
+    const float w = (ms == -INFINITY) ? 0.f : __expf(ms - M);
     den += w * a.part_ml[((base + s) * G + g) * 2 + 1];
     num += w * a.part_o[((base + s) * G + g) * HD + d];
   }
@@ -214,9 +439,15 @@ __global__ void __launch_bounds__(HD) k_attn_combine(FastAttnArgs a) {
 
 template <int HD, int G>
 inline size_t fa_smem_bytes() {
+  if (HD == 128) {
+    const size_t merge = (size_t)(4 * G * HD + 8 * G + G * HD + 2 * G);
+    return std::max((size_t)WarpSmem<G>::TOTAL, merge) * 4;
+  }
   constexpr int GP = (G + 3) & ~3;
   constexpr int PPAR = kFaThreads / HD;
-  return (size_t)(4 * kFaTile * HD + G * kFaTile + kFaTile * GP + 3 * GP + PPAR * G * HD) * 4;
+  const size_t tiles = (size_t)(4 * kFaTile * HD + G * kFaTile + kFaTile * GP + 3 * GP);
+  const size_t merge = (size_t)(PPAR * G * HD + G * HD + 2 * G);
+  return std::max(tiles, merge) * 4;
 }
 
 }  // namespace sr

@@ -211,11 +211,24 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, bool hidden_in, int n, tc::G
   a.err = t->err;
   const int mt = (W.rows + tc::kM - 1) / tc::kM, nt = (n + tc::kN - 1) / tc::kN;
   const int tiles = mt * nt;
-  int splits = 1;
-  if (tiles < 148) splits = std::min(std::max(1, a.groups / 4), (148 + tiles - 1) / tiles);
-  while (splits > 1 && (size_t)splits * n * W.rows * 4 > ((size_t)512 << 20)) splits--;
-  int kbps = (a.groups + splits - 1) / splits;
-  splits = (a.groups + kbps - 1) / kbps;
+  // Split K so the CTAs fill whole waves of 148 SMs (one CTA per SM), with at
+  // least 4 K-blocks per split; prefer fewer splits on ties.
+  int splits = 1, kbps = a.groups;
+  double best = -1.0;
+  for (int s = 1; s <= 16; s++) {
+    const int kb = (a.groups + s - 1) / s;
+    if (s > 1 && kb < 4) break;
+    const int ss = (a.groups + kb - 1) / kb;
+    if ((size_t)ss * n * W.rows * 4 > ((size_t)512 << 20)) break;
+    const int ctas = tiles * ss;
+    const int waves = (ctas + 147) / 148;
+    const double eff = (double)ctas / (waves * 148.0) - 0.02 * (ss - 1);
+    if (eff > best + 1e-9) {
+      best = eff;
+      splits = ss;
+      kbps = kb;
+    }
+  }
   a.kb_per_split = kbps;
   a.splits = splits;
   if (splits > 1) {

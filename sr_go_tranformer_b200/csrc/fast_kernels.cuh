@@ -66,8 +66,14 @@ inline void fast_rmsnorm(sr_model* m, const float* X, const int32_t* src_map, co
 template <int HD, int G>
 inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n) {
   const size_t smem = fa_smem_bytes<HD, G>();
-  cudaFuncSetAttribute(k_attn_split<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_attn_split<HD, G><<<dim3(a.max_splits, n, a.dm.kv_heads), kFaThreads, smem, m->stream>>>(a);
+  const dim3 grid(a.max_splits, n, a.dm.kv_heads);
+  if constexpr (HD == 128) {
+    cudaFuncSetAttribute(k_attn_warp128<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_attn_warp128<G><<<grid, kFaThreads, smem, m->stream>>>(a);
+  } else {
+    cudaFuncSetAttribute(k_attn_tile<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_attn_tile<HD, G><<<grid, kFaThreads, smem, m->stream>>>(a);
+  }
   k_attn_combine<HD><<<dim3(n, a.dm.heads), HD, 0, m->stream>>>(a);
   sr_count_launch(m, 2);
   return true;

@@ -11,8 +11,8 @@
 //     per-block scale (the reference's s += p*scale) is a scalar FMA on
 //     registers after each block's accumulator is read from TMEM;
 //   * TMA (SWIZZLE_128B) feeds a 4-stage mbarrier pipeline; one thread issues
-//     MMAs; TMEM holds two accumulator buffers so block b+1's MMAs overlap
-//     block b's epilogue.
+//     MMAs; TMEM holds four accumulator buffers so the MMAs of the next three
+//     blocks overlap block b's epilogue.
 // Every mbarrier wait is bounded (globaltimer); on expiry the kernel records an
 // error flag, stops waiting and finishes, and the host reports SR_ETIMEOUT.
 #pragma once
@@ -29,6 +29,7 @@ constexpr int kM = 128;          // output features per tile (MMA M)
 constexpr int kN = 128;          // step rows per tile (MMA N)
 constexpr int kKB = 64;          // K per block (one scale block, one 128-byte bf16 row)
 constexpr int kStages = 4;
+constexpr int kAcc = 4;           // TMEM accumulator buffers (kAcc * kN = 512 columns)
 constexpr int kThreads = 320;    // warp 0: TMA, warp 1: MMA, warps 2-9: epilogue
 constexpr int kEpiWarps = 8;     // two warps per TMEM lane quarter, 64 columns each
 constexpr uint32_t kTileA = kM * kKB * 2;  // 16 KiB
@@ -173,8 +174,8 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
   uint64_t* full = (uint64_t*)(gsm + kStages * kStageBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
+  uint64_t* tempty = tfull + kAcc;
+  uint32_t* tmem_slot = (uint32_t*)(tempty + kAcc);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * kM, n0 = blockIdx.x * kN, split = blockIdx.z;
@@ -187,15 +188,15 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; b++) {
+    for (int b = 0; b < kAcc; b++) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);  // one arrive per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // one warp allocates 2*kN TMEM columns
+  if (warp == 1) {  // one warp allocates kAcc*kN TMEM columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(2 * kN));
+                 "r"(kAcc * kN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -220,9 +221,9 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
     if (lane == 0) {  // MMA issuer
       const uint32_t idesc = idesc_bf16(kM, kN);
       for (int i = 0; i < nkb; i++) {
-        const int s = i % kStages, b = i & 1;
+        const int s = i % kStages, b = i % kAcc;
         if (!mbar_wait(&full[s], (i / kStages) & 1, a.err)) break;
-        if (i >= 2 && !mbar_wait(&tempty[b], ((i >> 1) - 1) & 1, a.err)) break;
+        if (i >= kAcc && !mbar_wait(&tempty[b], ((i / kAcc) - 1) & 1, a.err)) break;
         tc_fence_after();
         const uint8_t* st = gsm + s * kStageBytes;
         const uint64_t da = sw128_desc(st), dh = sw128_desc(st + kTileA), dl = sw128_desc(st + kTileA + kTileB);
@@ -244,9 +245,9 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
     for (int j = 0; j < NC; j++) acc[j] = 0.f;
     const float* srow = a.scales + (int64_t)min(o, a.out - 1) * a.groups;
     for (int i = 0; i < nkb; i++) {
-      const int b = i & 1;
+      const int b = i % kAcc;
       const float sc = srow[kb0 + i];
-      if (!mbar_wait(&tfull[b], (i >> 1) & 1, a.err)) break;
+      if (!mbar_wait(&tfull[b], (i / kAcc) & 1, a.err)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * kN + h * NC;
       uint32_t v0[32], v1[32];
@@ -282,13 +283,33 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kAcc * kN));
   }
 }
 
-// Deterministic split-K reduction (splits summed in order) + epilogue.
+// Deterministic split-K reduction (splits summed in order) + epilogue; four
+// consecutive outputs per thread when the row length allows it.
 __global__ void k_gemm_reduce(GemmArgs a) {
   const int64_t total = (int64_t)a.n * a.out;
+  if ((a.out & 3) == 0) {
+    const int64_t total4 = total >> 2;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total4; t += (int64_t)gridDim.x * blockDim.x) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s = 0; s < a.splits; s++) {
+        const float4 p = *(const float4*)(a.partial + (int64_t)s * total + 4 * t);
+        v.x += p.x;
+        v.y += p.y;
+        v.z += p.z;
+        v.w += p.w;
+      }
+      const int row = (int)((4 * t) / a.out), o = (int)((4 * t) % a.out);
+      store_out(a, row, o, v.x);
+      store_out(a, row, o + 1, v.y);
+      store_out(a, row, o + 2, v.z);
+      store_out(a, row, o + 3, v.w);
+    }
+    return;
+  }
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     const int row = (int)(t / a.out), o = (int)(t % a.out);
     float v = 0.f;
