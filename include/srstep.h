@@ -162,6 +162,20 @@ int sr_kvpool_fill_synthetic(sr_kvpool *p, uint64_t seed, float scale);
  * SR_ECANCELED (future KV rows may be written; positions are never committed
  * here: the caller commits Pos += len on SR_OK, :6452-6454). */
 int sr_step(sr_model *m, sr_kvpool *pool, const sr_batch *batch, float *logits_host, const volatile int32_t *cancel);
+/* Allocation-free variant of sr_step for callers that cannot allocate device
+ * memory while serving (for example an engine that reserved nearly all of HBM
+ * for its KV page pool up front).  No counterpart in the reference.  Same
+ * arguments, validation and outputs as sr_step (without the cancel flag); the
+ * projections and norms run in the exact order, attention runs as split-K
+ * flash-decoding whose partial results use a 16 MiB scratch array compiled into
+ * the library (resident on every GPU that loads it).  A batch needing more
+ * scratch -- rows x kv_heads x ceil(max context / 256) x group x (head_dim+2)
+ * floats -- is rejected with SR_EINVAL; head_dim must be 64 or 128 and at most
+ * 8 query heads may share a KV head (SR_EUNSUPPORTED otherwise).  The first
+ * call on each device resolves the array's address; make it before any stream
+ * capture.  Calls that overlap on one device race on the shared array.  Never
+ * calls cudaMalloc or cudaFree. */
+int sr_step_noalloc(sr_model *m, sr_kvpool *pool, const sr_batch *batch, float *logits_host);
 /* Device pointer of the last step's logits [n_sessions x vocab]. */
 int sr_step_logits(sr_model *m, const float **device_logits);
 

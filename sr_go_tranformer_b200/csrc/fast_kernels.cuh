@@ -94,14 +94,44 @@ inline bool fa_dispatch_g(sr_model* m, const FastAttnArgs& a, int n) {
   }
 }
 
+// Whether the split-K kernels cover this model shape.
+inline bool fast_attention_supported(const ModelDims& dm) {
+  return (dm.hd == 64 || dm.hd == 128) && dm.group <= 8;
+}
+inline int fa_max_splits(int max_len) { return (max_len + kFaSplit - 1) / kFaSplit; }
+// Scratch floats the split-K attention needs for n rows (partial O, then (m, l)).
+inline size_t fa_scratch_floats(const ModelDims& dm, int n, int max_len, size_t* items_out = nullptr) {
+  const size_t items = (size_t)n * dm.kv_heads * fa_max_splits(max_len);
+  if (items_out) *items_out = items;
+  return items * dm.group * (dm.hd + 2);
+}
+
+// Launch split + combine with caller-provided scratch (no allocation).
+inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, int max_len, int layer, float* part_o,
+                               float* part_ml) {
+  const ModelDims& dm = m->dm;
+  FastAttnArgs a;
+  a.Q = m->Q;
+  a.A = m->A;
+  a.pool = pool_data;
+  a.meta = m->meta;
+  a.dm = dm;
+  a.layer = layer;
+  a.scale = (float)(1.0 / std::sqrt((double)dm.hd));
+  a.max_splits = fa_max_splits(max_len);
+  a.part_o = part_o;
+  a.part_ml = part_ml;
+  return dm.hd == 128 ? fa_dispatch_g<128>(m, a, n) : fa_dispatch_g<64>(m, a, n);
+}
+
 // Returns false (exact kernel runs instead) for unsupported shapes or when the
-// split scratch would exceed its cap.
+// split scratch would exceed its cap.  The scratch grows on demand.
 inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int max_len, int layer) {
   const ModelDims& dm = m->dm;
-  if ((dm.hd != 64 && dm.hd != 128) || dm.group > 8) return false;
+  if (!fast_attention_supported(dm)) return false;
   FastState* st = fast_state(m);
-  const int max_splits = (max_len + kFaSplit - 1) / kFaSplit;
-  const size_t items = (size_t)n * dm.kv_heads * max_splits;
+  size_t items = 0;
+  fa_scratch_floats(dm, n, max_len, &items);
   const size_t o_bytes = items * dm.group * dm.hd * 4;
   if (o_bytes > ((size_t)1 << 30)) return false;
   if (items > st->items_cap) {
@@ -118,18 +148,7 @@ inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int m
     }
     st->items_cap = items;
   }
-  FastAttnArgs a;
-  a.Q = m->Q;
-  a.A = m->A;
-  a.pool = pool_data;
-  a.meta = m->meta;
-  a.dm = dm;
-  a.layer = layer;
-  a.scale = (float)(1.0 / std::sqrt((double)dm.hd));
-  a.max_splits = max_splits;
-  a.part_o = st->part_o;
-  a.part_ml = st->part_ml;
-  return dm.hd == 128 ? fa_dispatch_g<128>(m, a, n) : fa_dispatch_g<64>(m, a, n);
+  return fast_attention_run(m, pool_data, n, max_len, layer, st->part_o, st->part_ml);
 }
 
 // ------------------------------------------------------------------- linear --

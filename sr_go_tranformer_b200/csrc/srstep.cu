@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -635,7 +636,8 @@ static void launch_attention_exact(sr_model* m, sr_kvpool* pool, int n, int max_
   sr_count_launch(m);
 }
 
-int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel) {
+int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel,
+                    const StepScratch* scratch) {
   const ModelDims& dm = m->dm;
   const int n = info.rows, d = dm.dim, kd = dm.kvd, L = dm.layers;
   const double eps = m->d.norm_eps;
@@ -645,7 +647,8 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   SR_LAUNCH(m, SR_PROF_EMBED, k_embed<<<n, 256, 0, s>>>(m->params[0], m->meta.tokens, m->X, d));
   sr_count_launch(m, 2);
   const int norm_blocks = (n + kNormWarps - 1) / kNormWarps;
-  const bool fast = m->mode == SR_MODE_FAST;
+  const bool fixed_scratch = scratch && scratch->part_o;
+  const bool fast = m->mode == SR_MODE_FAST && !fixed_scratch;
   for (int l = 0; l < L; l++) {
     if (cancel && *cancel) {
       sr_prof_span_end(m);
@@ -676,7 +679,8 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
               k_rope_kv_exact<<<n, 128, 0, s>>>(m->Q, m->K, m->V, m->cos_t, m->sin_t, m->meta, pool->data, dm, l));
     sr_count_launch(m, 3);  // two norms and RoPE/KV of this layer
     SR_LAUNCH(m, SR_PROF_ATTENTION,
-              if (fast) fast_attention(m, pool, n, info.max_len, l);
+              if (fixed_scratch) fast_attention_run(m, pool->data, n, info.max_len, l, scratch->part_o, scratch->part_ml);
+              else if (fast) fast_attention(m, pool, n, info.max_len, l);
               else launch_attention_exact(m, pool, n, info.max_len, l));
     o.y = m->X; o.ldy = d; o.bias = nullptr; o.resid = m->X;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_o(m, l, n));
@@ -939,5 +943,72 @@ extern "C" int sr_profile_read(sr_model* m, double* ms, int64_t* launches, doubl
 extern "C" int sr_model_stream(sr_model* m, void** stream) {
   if (!m || !stream) return sr_fail(SR_EINVAL, "null argument");
   *stream = (void*)m->stream;
+  return SR_OK;
+}
+
+// --------------------------------------------------------- allocation-free step --
+// sr_step_noalloc serves callers that must not allocate device memory while
+// they serve: an engine that sized its KV page pool to fill nearly all of HBM
+// up front (the reference plans its page budget before admitting anything),
+// or an embedding runtime that owns every device allocation itself.  Its only
+// scratch -- the split-K attention partials (unnormalised outputs and the
+// (max, sum) pair of every row x KV head x 256-position split) -- lives in this
+// file-scope device array, which every GPU that loads the library holds until
+// the process exits.  All calls on a device share it and it keeps the last
+// call's contents; nothing in it needs to start at zero, because each call
+// writes every slot it later reads.  Calls that overlap on the GPU (other
+// streams, other threads, other models on the same device) race on it.
+constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB per device
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[256];  // device address of g_noalloc_scratch, per device ordinal
+
+// The first call on each device resolves the array's device address with that
+// device current (host code must not use the symbol itself as an address).
+static int noalloc_scratch(int device, float** out) {
+  if (device < 0 || device >= 256) return sr_fail(SR_EINVAL, "device ordinal out of range for the static scratch");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return sr_fail(SR_EDEVICE, std::string("cudaGetSymbolAddress(static attention scratch): ") +
+                                     cudaGetErrorString(e));
+    g_noalloc_ptr[device] = (float*)p;
+  }
+  *out = g_noalloc_ptr[device];
+  return SR_OK;
+}
+
+extern "C" int sr_step_noalloc(sr_model* m, sr_kvpool* pool, const sr_batch* batch, float* logits_host) {
+  if (!m || !pool || !batch) return sr_fail(SR_EINVAL, "null argument");
+  if (pool->m != m) return sr_fail(SR_EINVAL, "KV pool belongs to another model");
+  BatchInfo info;
+  int rc = sr_validate_batch(m, pool, batch, &info);
+  if (rc != SR_OK) return rc;
+  if (!fast_attention_supported(m->dm))
+    return sr_fail(SR_EUNSUPPORTED, "the allocation-free step needs head_dim 64 or 128 and at most 8 query heads per KV head");
+  size_t items = 0;
+  const size_t floats = fa_scratch_floats(m->dm, info.rows, info.max_len, &items);
+  if (floats * sizeof(float) > kNoAllocScratchBytes)
+    return sr_fail(SR_EINVAL, "batch needs " + std::to_string(floats * sizeof(float)) +
+                                  " bytes of attention scratch; the allocation-free step holds " +
+                                  std::to_string(kNoAllocScratchBytes) +
+                                  " (16 MiB): use fewer rows or shorter contexts, or sr_step");
+  CK(cudaSetDevice(m->device));
+  float* base = nullptr;
+  if ((rc = noalloc_scratch(m->device, &base)) != SR_OK) return rc;
+  StepScratch sc;
+  sc.part_o = base;
+  sc.part_ml = base + items * m->dm.group * m->dm.hd;
+  if ((rc = sr_upload_batch(m, batch, info)) != SR_OK) return rc;
+  if ((rc = sr_step_enqueue(m, pool, info, nullptr, &sc)) != SR_OK) return rc;
+  sr_prof_span_end(m);
+  if (logits_host)
+    CK(cudaMemcpyAsync(logits_host, m->logits, (size_t)info.sessions * m->dm.vocab * 4, cudaMemcpyDeviceToHost,
+                       m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  sr_prof_resolve(m);
   return SR_OK;
 }

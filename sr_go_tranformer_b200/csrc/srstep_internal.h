@@ -129,7 +129,15 @@ void sr_prof_resolve(sr_model* m);  // after a stream synchronize
 int sr_model_alloc(sr_model* m, void** p, size_t bytes);
 int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* b, BatchInfo* info);
 int sr_upload_batch(sr_model* m, const sr_batch* b, const BatchInfo& info);
-int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel);
+// Optional attention scratch supplied by the caller (the allocation-free step):
+// when part_o is set, the step runs exact-order projections and norms and the
+// split-K attention with this scratch, and allocates nothing.
+struct StepScratch {
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+};
+int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel,
+                    const StepScratch* scratch = nullptr);
 int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const int32_t* history_offsets,
                       const int32_t* history, const uint64_t* rng_state, int32_t blocked);
 int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_out);
