@@ -16,7 +16,9 @@
 //   double-buffered tiles.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <float.h>
+
 #include "common.cuh"
 
 namespace sr {
@@ -35,7 +37,16 @@ struct FastAttnArgs {
   int max_splits;
   float* part_o;   // [items][group][hd]
   float* part_ml;  // [items][group][2]
+  __nv_bfloat16* xh;  // optional: write the output as bf16 hi/lo planes (the
+  __nv_bfloat16* xl;  // next projection's tensor-core operand) instead of fp32 A
 };
+
+// x ~= hi + lo with |x - hi - lo| <= 2^-17 |x| (two bf16 terms).
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(x);
+  *hi = h;
+  *lo = __float2bfloat16_rn(x - __bfloat162float(h));
+}
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -434,7 +445,11 @@ __global__ void __launch_bounds__(HD) k_attn_combine(FastAttnArgs a) {
     den += w * a.part_ml[((base + s) * G + g) * 2 + 1];
     num += w * a.part_o[((base + s) * G + g) * HD + d];
   }
-  a.A[(int64_t)r * a.dm.dim + (int64_t)h * HD + d] = num / den;
+  const int64_t o = (int64_t)r * a.dm.dim + (int64_t)h * HD + d;
+  if (a.xh)
+    split_bf16(num / den, a.xh + o, a.xl + o);
+  else
+    a.A[o] = num / den;
 }
 
 template <int HD, int G>

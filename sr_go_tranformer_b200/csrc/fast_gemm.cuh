@@ -121,7 +121,7 @@ inline bool tc_build(sr_model* m, TcState* t, TcMatrix& dst, const std::vector<c
                       cudaMemcpyDeviceToDevice, m->stream);
     r0 += p->rows;
   }
-  return make_map(&dst.map, dst.w16, (uint64_t)cols, (uint64_t)rows, tc::kM);
+  return make_map(&dst.map, dst.w16, (uint64_t)cols, (uint64_t)rows, tc::kMC);
 }
 
 // Lazily (re)build the shadows after the weights change.  Returns false when
@@ -209,7 +209,7 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, bool hidden_in, int n, tc::G
   a.groups = (W.cols + kQBlock - 1) / kQBlock;
   a.scales = W.scales;
   a.err = t->err;
-  const int mt = (W.rows + tc::kM - 1) / tc::kM, nt = (n + tc::kN - 1) / tc::kN;
+  const int mt = (W.rows + tc::kMC - 1) / tc::kMC, nt = (n + tc::kN - 1) / tc::kN;
   const int tiles = mt * nt;
   // Split K so the CTAs fill whole waves of 148 SMs (one CTA per SM), with at
   // least 4 K-blocks per split; prefer fewer splits on ties.
@@ -270,8 +270,15 @@ inline tc::Segment seg(int rows, float* y, int ldy, const float* bias, const flo
   return s;
 }
 
-// Q|K|V in one GEMM (+ qwen2 biases).
-inline bool tc_qkv(sr_model* m, int l, int n) {
+// Whether this step's projections run on the tensor cores (and their inputs
+// are therefore produced directly as bf16 hi/lo planes).
+inline bool tc_active(sr_model* m, int n) { return n >= kTcMinRows && tc_prepare(m); }
+inline __nv_bfloat16* tc_xh(sr_model* m) { return tc_state(m)->xh; }
+inline __nv_bfloat16* tc_xl(sr_model* m) { return tc_state(m)->xl; }
+
+// Q|K|V in one GEMM (+ qwen2 biases).  presplit: the producer already wrote
+// the operand planes.
+inline bool tc_qkv(sr_model* m, int l, int n, bool presplit = false) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
   const ModelDims& dm = m->dm;
   const Param* B = m->d.qkv_bias ? &m->params[2 + 9 * dm.layers + 3 * l] : nullptr;
@@ -281,11 +288,11 @@ inline bool tc_qkv(sr_model* m, int l, int n) {
   a.seg[1] = seg(dm.kvd, m->K, dm.kvd, B ? (const float*)B[1].values : nullptr, nullptr);
   a.seg[2] = seg(dm.kvd, m->V, dm.kvd, B ? (const float*)B[2].values : nullptr, nullptr);
   a.out_map = nullptr;
-  tc_split_x(m, m->N, n, dm.dim);
+  if (!presplit) tc_split_x(m, m->N, n, dm.dim);
   return tc_gemm(m, tc_state(m)->qkv[l], false, n, a);
 }
 // gate|up in one GEMM.
-inline bool tc_gateup(sr_model* m, int l, int n) {
+inline bool tc_gateup(sr_model* m, int l, int n, bool presplit = false) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
   const ModelDims& dm = m->dm;
   tc::GemmArgs a{};
@@ -293,35 +300,35 @@ inline bool tc_gateup(sr_model* m, int l, int n) {
   a.seg[0] = seg(dm.hidden, m->G, dm.hidden, nullptr, nullptr);
   a.seg[1] = seg(dm.hidden, m->U, dm.hidden, nullptr, nullptr);
   a.out_map = nullptr;
-  tc_split_x(m, m->N, n, dm.dim);
+  if (!presplit) tc_split_x(m, m->N, n, dm.dim);
   return tc_gemm(m, tc_state(m)->gateup[l], false, n, a);
 }
 // O / down projection with the residual add (X += W x).
-inline bool tc_resid(sr_model* m, const TcMatrix& W, const float* X, int n, bool hidden_in) {
+inline bool tc_resid(sr_model* m, const TcMatrix& W, const float* X, int n, bool hidden_in, bool presplit) {
   const ModelDims& dm = m->dm;
   tc::GemmArgs a{};
   a.nseg = 1;
   a.seg[0] = seg(dm.dim, m->X, dm.dim, nullptr, m->X);
   a.out_map = nullptr;
-  tc_split_x(m, X, n, hidden_in ? dm.hidden : dm.dim);
+  if (!presplit) tc_split_x(m, X, n, hidden_in ? dm.hidden : dm.dim);
   return tc_gemm(m, W, hidden_in, n, a);
 }
-inline bool tc_o(sr_model* m, int l, int n) {
+inline bool tc_o(sr_model* m, int l, int n, bool presplit = false) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
-  return tc_resid(m, tc_state(m)->o[l], m->A, n, false);
+  return tc_resid(m, tc_state(m)->o[l], m->A, n, false, presplit);
 }
-inline bool tc_down(sr_model* m, int l, int n) {
+inline bool tc_down(sr_model* m, int l, int n, bool presplit = false) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
-  return tc_resid(m, tc_state(m)->down[l], m->H, n, true);
+  return tc_resid(m, tc_state(m)->down[l], m->H, n, true, presplit);
 }
-inline bool tc_head(sr_model* m, int heads) {
+inline bool tc_head(sr_model* m, int heads, bool presplit = false) {
   if (heads < kTcMinRows || !tc_prepare(m)) return false;
   const ModelDims& dm = m->dm;
   tc::GemmArgs a{};
   a.nseg = 1;
   a.seg[0] = seg(dm.vocab, m->logits, dm.vocab, nullptr, nullptr);
   a.out_map = m->meta.head_dst;
-  tc_split_x(m, m->N, heads, dm.dim);
+  if (!presplit) tc_split_x(m, m->N, heads, dm.dim);
   return tc_gemm(m, tc_state(m)->head, false, heads, a);
 }
 

@@ -32,34 +32,71 @@ inline int fast_init(sr_model* m) {
 }
 
 // ------------------------------------------------------------------ RMSNorm --
-// rmsInto (M:6182-6194) with a lane-parallel fp64 sum of squares (reordered).
+// rmsInto (M:6182-6194) with a block-parallel fp64 sum of squares (reordered).
+// One 128-thread block per row keeps every SM busy at decode batch sizes.
 __global__ void __launch_bounds__(128)
 k_rmsnorm_fast(const float* __restrict__ X, const int32_t* __restrict__ src_map, const float* __restrict__ w,
-               float* __restrict__ Y, int rows, int d, double eps) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * 4 + warp;
-  if (r >= rows) return;
+               float* __restrict__ Y, int rows, int d, double eps, __nv_bfloat16* __restrict__ yh,
+               __nv_bfloat16* __restrict__ yl) {
+  __shared__ double red[4];
+  const int r = blockIdx.x;
   const int srow = src_map ? src_map[r] : r;
   const float* x = X + (int64_t)srow * d;
+  const bool vec = (d & 3) == 0;
   double ss = 0.0;
-  if ((d & 3) == 0) {
-    for (int j = lane * 4; j < d; j += 128) {
-      float4 v = *(const float4*)(x + j);
+  if (vec) {
+    for (int j = threadIdx.x * 4; j < d; j += 512) {
+      const float4 v = *(const float4*)(x + j);
       ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
     }
   } else {
-    for (int j = lane; j < d; j += 32) ss += (double)x[j] * x[j];
+    for (int j = threadIdx.x; j < d; j += 128) ss += (double)x[j] * x[j];
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = red[0] + red[1] + red[2] + red[3];
   const float a = (float)(1.0 / sqrt(ss / (double)d + eps));
-  float* y = Y + (int64_t)r * d;
-  for (int j = lane; j < d; j += 32) y[j] = x[j] * a * w[j];
+  const int64_t o = (int64_t)r * d;
+  if (vec) {
+    for (int j = threadIdx.x * 4; j < d; j += 512) {
+      const float4 v = *(const float4*)(x + j);
+      const float4 g = *(const float4*)(w + j);
+      const float y0 = v.x * a * g.x, y1 = v.y * a * g.y, y2 = v.z * a * g.z, y3 = v.w * a * g.w;
+      if (yh) {
+        split_bf16(y0, yh + o + j, yl + o + j);
+        split_bf16(y1, yh + o + j + 1, yl + o + j + 1);
+        split_bf16(y2, yh + o + j + 2, yl + o + j + 2);
+        split_bf16(y3, yh + o + j + 3, yl + o + j + 3);
+      } else {
+        *(float4*)(Y + o + j) = make_float4(y0, y1, y2, y3);
+      }
+    }
+  } else {
+    for (int j = threadIdx.x; j < d; j += 128) {
+      const float y = x[j] * a * w[j];
+      if (yh)
+        split_bf16(y, yh + o + j, yl + o + j);
+      else
+        Y[o + j] = y;
+    }
+  }
 }
 
 inline void fast_rmsnorm(sr_model* m, const float* X, const int32_t* src_map, const float* w, float* Y, int rows,
-                         int d, double eps) {
-  k_rmsnorm_fast<<<(rows + 3) / 4, 128, 0, m->stream>>>(X, src_map, w, Y, rows, d, eps);
+                         int d, double eps, __nv_bfloat16* yh = nullptr, __nv_bfloat16* yl = nullptr) {
+  k_rmsnorm_fast<<<rows, 128, 0, m->stream>>>(X, src_map, w, Y, rows, d, eps, yh, yl);
+}
+
+// SwiGLU h = g/(1+exp(-g)) * u in fp32 (M:6410-6413 reordered), written as the
+// down projection's bf16 hi/lo operand planes.
+__global__ void k_swiglu_split(const float* __restrict__ G, const float* __restrict__ U,
+                               __nv_bfloat16* __restrict__ hh, __nv_bfloat16* __restrict__ hl, int64_t count) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+    const float g = G[i];
+    split_bf16(g / (1.f + __expf(-g)) * U[i], hh + i, hl + i);
+  }
 }
 
 // ---------------------------------------------------------------- attention --
@@ -106,9 +143,10 @@ inline size_t fa_scratch_floats(const ModelDims& dm, int n, int max_len, size_t*
   return items * dm.group * (dm.hd + 2);
 }
 
-// Launch split + combine with caller-provided scratch (no allocation).
+// Launch split + combine with caller-provided scratch (no allocation).  With
+// xh/xl set, the combine writes bf16 hi/lo operand planes instead of fp32 A.
 inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, int max_len, int layer, float* part_o,
-                               float* part_ml) {
+                               float* part_ml, __nv_bfloat16* xh = nullptr, __nv_bfloat16* xl = nullptr) {
   const ModelDims& dm = m->dm;
   FastAttnArgs a;
   a.Q = m->Q;
@@ -121,12 +159,15 @@ inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, int m
   a.max_splits = fa_max_splits(max_len);
   a.part_o = part_o;
   a.part_ml = part_ml;
+  a.xh = xh;
+  a.xl = xl;
   return dm.hd == 128 ? fa_dispatch_g<128>(m, a, n) : fa_dispatch_g<64>(m, a, n);
 }
 
 // Returns false (exact kernel runs instead) for unsupported shapes or when the
 // split scratch would exceed its cap.  The scratch grows on demand.
-inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int max_len, int layer) {
+inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int max_len, int layer,
+                               __nv_bfloat16* xh = nullptr, __nv_bfloat16* xl = nullptr) {
   const ModelDims& dm = m->dm;
   if (!fast_attention_supported(dm)) return false;
   FastState* st = fast_state(m);
@@ -148,7 +189,7 @@ inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int m
     }
     st->items_cap = items;
   }
-  return fast_attention_run(m, pool_data, n, max_len, layer, st->part_o, st->part_ml);
+  return fast_attention_run(m, pool_data, n, max_len, layer, st->part_o, st->part_ml, xh, xl);
 }
 
 // ------------------------------------------------------------------- linear --

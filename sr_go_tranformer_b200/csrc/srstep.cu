@@ -609,7 +609,8 @@ static void launch_linear_exact(sr_model* m, const float* X, int n, const Param&
     else k_linear_q_exact<kQ4, 64, 8><<<grid(64, 8), 256, 0, s>>>(X, n, in, out, W, O);
   }
 }
-static void fast_attention(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer);
+static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer, __nv_bfloat16* xh,
+                           __nv_bfloat16* xl);
 void sr_launch_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O, int cls = SR_PROF_LINEAR) {
   ProfScope ps(m, cls);
   if (m->mode == SR_MODE_FAST && fast_linear(m, X, n, W, O)) return;
@@ -649,6 +650,11 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   const int norm_blocks = (n + kNormWarps - 1) / kNormWarps;
   const bool fixed_scratch = scratch && scratch->part_o;
   const bool fast = m->mode == SR_MODE_FAST && !fixed_scratch;
+  // Tensor-core projections: every producer writes the next projection's bf16
+  // hi/lo operand planes directly (no fp32 round trip, no split kernel).
+  const bool tc = fast && tc_active(m, n);
+  __nv_bfloat16* xh = tc ? tc_xh(m) : nullptr;
+  __nv_bfloat16* xl = tc ? tc_xl(m) : nullptr;
   for (int l = 0; l < L; l++) {
     if (cancel && *cancel) {
       sr_prof_span_end(m);
@@ -663,10 +669,11 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     o.resid = nullptr;
     o.out_map = nullptr;
     SR_LAUNCH(m, SR_PROF_NORM,
-              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps);
+              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps, xh, xl);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps));
     bool done;
-    SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_qkv(m, l, n));
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_qkv(m, l, n, true));
+    if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) {
       o.y = m->Q; o.ldy = d; o.bias = B ? (const float*)B[0].values : nullptr;
       sr_launch_linear(m, m->N, n, P[1], o);
@@ -678,18 +685,21 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     SR_LAUNCH(m, SR_PROF_ROPE_KV,
               k_rope_kv_exact<<<n, 128, 0, s>>>(m->Q, m->K, m->V, m->cos_t, m->sin_t, m->meta, pool->data, dm, l));
     sr_count_launch(m, 3);  // two norms and RoPE/KV of this layer
+    bool a_split = false;   // attention wrote the O projection's operand planes
     SR_LAUNCH(m, SR_PROF_ATTENTION,
               if (fixed_scratch) fast_attention_run(m, pool->data, n, info.max_len, l, scratch->part_o, scratch->part_ml);
-              else if (fast) fast_attention(m, pool, n, info.max_len, l);
+              else if (fast) a_split = fast_attention(m, pool, n, info.max_len, l, xh, xl);
               else launch_attention_exact(m, pool, n, info.max_len, l));
     o.y = m->X; o.ldy = d; o.bias = nullptr; o.resid = m->X;
-    SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_o(m, l, n));
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_o(m, l, n, a_split));
+    if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->A, n, P[4], o);
     SR_LAUNCH(m, SR_PROF_NORM,
-              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps);
+              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps, xh, xl);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps));
     o.resid = nullptr;
-    SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_gateup(m, l, n));
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_gateup(m, l, n, true));
+    if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) {
       o.y = m->G; o.ldy = dm.hidden;
       sr_launch_linear(m, m->N, n, P[6], o);
@@ -697,11 +707,14 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
       sr_launch_linear(m, m->N, n, P[7], o);
     }
     int64_t cnt = (int64_t)n * dm.hidden;
+    const int sw_blocks = (int)std::min<int64_t>((cnt + 255) / 256, 148 * 16);
     SR_LAUNCH(m, SR_PROF_SWIGLU,
-              k_swiglu_exact<<<(int)std::min<int64_t>((cnt + 255) / 256, 148 * 16), 256, 0, s>>>(m->G, m->U, m->H, cnt));
+              if (tc) k_swiglu_split<<<sw_blocks, 256, 0, s>>>(m->G, m->U, xh, xl, cnt);
+              else k_swiglu_exact<<<sw_blocks, 256, 0, s>>>(m->G, m->U, m->H, cnt));
     sr_count_launch(m);
     o.y = m->X; o.ldy = d; o.resid = m->X;
-    SR_LAUNCH(m, SR_PROF_LINEAR, done = fast && tc_down(m, l, n));
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_down(m, l, n, true));
+    if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->H, n, P[8], o);
   }
   // Selected head (M:6420-6448): gather last rows, final norm, LM head into
@@ -710,9 +723,11 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   if (info.heads > 0) {
     const Param& F = m->params[1 + 9 * L];
     const int hb = (info.heads + kNormWarps - 1) / kNormWarps;
+    const bool tc_h = fast && tc_active(m, info.heads);
     sr_count_launch(m);
     SR_LAUNCH(m, SR_PROF_HEAD,
-              if (fast) fast_rmsnorm(m, m->X, m->meta.head_src, (const float*)F.values, m->N, info.heads, d, eps);
+              if (fast) fast_rmsnorm(m, m->X, m->meta.head_src, (const float*)F.values, m->N, info.heads, d, eps,
+                                     tc_h ? tc_xh(m) : nullptr, tc_h ? tc_xl(m) : nullptr);
               else k_rmsnorm_exact<<<hb, kNormWarps * 32, 0, s>>>(m->X, m->meta.head_src, (const float*)F.values, m->N, info.heads, d, eps));
     const Param& head = m->d.tied ? m->params[0] : m->params.back();
     LinearOut o;
@@ -722,7 +737,8 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     o.resid = nullptr;
     o.out_map = m->meta.head_dst;
     bool done;
-    SR_LAUNCH(m, SR_PROF_HEAD, done = fast && tc_head(m, info.heads));
+    SR_LAUNCH(m, SR_PROF_HEAD, done = tc_h && tc_head(m, info.heads, true));
+    if (tc_h && !done) return sr_fail(SR_ENOMEM, "tensor-core LM head could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->N, info.heads, head, o, SR_PROF_HEAD);
   }
   CK(cudaGetLastError());
@@ -868,9 +884,13 @@ extern "C" int sr_step_sample(sr_model* m, sr_kvpool* pool, const sr_batch* batc
   return sr_sample_finish(m, batch->n_sessions, rng_state, ids_out);
 }
 
-// Fast-mode attention: split-K kernels when the shape is covered, else exact.
-static void fast_attention(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer) {
-  if (!fast_attention_try(m, pool->data, n, max_len, layer)) launch_attention_exact(m, pool, n, max_len, layer);
+// Fast-mode attention: split-K kernels when the shape is covered (returns true
+// when they also wrote xh/xl, if given), else the exact kernel into fp32 A.
+static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer, __nv_bfloat16* xh,
+                           __nv_bfloat16* xl) {
+  if (fast_attention_try(m, pool->data, n, max_len, layer, xh, xl)) return xh != nullptr;
+  launch_attention_exact(m, pool, n, max_len, layer);
+  return false;
 }
 
 // Fast-mode projections (tensor-core GEMM) are not built yet: exact kernels run.

@@ -10,9 +10,10 @@
 //     step rows, so a thread of the epilogue owns one output feature and its
 //     per-block scale (the reference's s += p*scale) is a scalar FMA on
 //     registers after each block's accumulator is read from TMEM;
-//   * TMA (SWIZZLE_128B) feeds a 4-stage mbarrier pipeline; one thread issues
-//     MMAs; TMEM holds four accumulator buffers so the MMAs of the next three
-//     blocks overlap block b's epilogue.
+//   * a CTA owns 256 output features as two M=128 MMA halves that share each
+//     activation tile; TMA (SWIZZLE_128B) feeds a 3-stage mbarrier pipeline of
+//     64 KiB stages; one thread issues MMAs; TMEM holds two accumulator buffers
+//     so block b+1's MMAs overlap block b's epilogue.
 // Every mbarrier wait is bounded (globaltimer); on expiry the kernel records an
 // error flag, stops waiting and finishes, and the host reports SR_ETIMEOUT.
 #pragma once
@@ -25,15 +26,17 @@
 namespace sr {
 namespace tc {
 
-constexpr int kM = 128;          // output features per tile (MMA M)
+constexpr int kM = 128;          // output features per MMA (MMA M)
+constexpr int kMH = 2;           // MMA halves per CTA: a CTA owns kMC = 256 output features
+constexpr int kMC = kM * kMH;
 constexpr int kN = 128;          // step rows per tile (MMA N)
 constexpr int kKB = 64;          // K per block (one scale block, one 128-byte bf16 row)
-constexpr int kStages = 4;
-constexpr int kAcc = 4;           // TMEM accumulator buffers (kAcc * kN = 512 columns)
+constexpr int kStages = 3;
+constexpr int kAcc = 2;          // TMEM accumulator buffers, each kMH*kN columns (512 in all)
 constexpr int kThreads = 320;    // warp 0: TMA, warp 1: MMA, warps 2-9: epilogue
-constexpr int kEpiWarps = 8;     // two warps per TMEM lane quarter, 64 columns each
-constexpr uint32_t kTileA = kM * kKB * 2;  // 16 KiB
-constexpr uint32_t kTileB = kN * kKB * 2;  // 16 KiB
+constexpr int kEpiWarps = 8;     // lane quarter (warp % 4) x MMA half ((warp - 2) / 4)
+constexpr uint32_t kTileA = kMC * kKB * 2;  // 32 KiB of weight codes
+constexpr uint32_t kTileB = kN * kKB * 2;   // 16 KiB per activation plane
 constexpr uint32_t kStageBytes = kTileA + 2 * kTileB;
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait, then abort
@@ -165,7 +168,7 @@ __device__ __forceinline__ void store_out(const GemmArgs& a, int row, int o, flo
   *dst = v;
 }
 
-// grid: (ceil(n/128), ceil(out/128), splits): the row tiles of one weight tile run together (L2 reuse)
+// grid: (ceil(n/128), ceil(out/256), splits): the row tiles of one weight tile run together (L2 reuse)
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xh,
          const __grid_constant__ CUtensorMap tm_xl, GemmArgs a) {
@@ -178,7 +181,7 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
   uint32_t* tmem_slot = (uint32_t*)(tempty + kAcc);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kM, n0 = blockIdx.x * kN, split = blockIdx.z;
+  const int m0 = blockIdx.y * kMC, n0 = blockIdx.x * kN, split = blockIdx.z;
   const int kb0 = split * a.kb_per_split;
   const int kb1 = min(a.groups, kb0 + a.kb_per_split);
   const int nkb = max(0, kb1 - kb0);
@@ -194,9 +197,9 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // one warp allocates kAcc*kN TMEM columns
+  if (warp == 1) {  // one warp allocates kAcc*kMH*kN TMEM columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kAcc * kN));
+                 "r"(kAcc * kMH * kN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -226,54 +229,59 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
         if (i >= kAcc && !mbar_wait(&tempty[b], ((i / kAcc) - 1) & 1, a.err)) break;
         tc_fence_after();
         const uint8_t* st = gsm + s * kStageBytes;
-        const uint64_t da = sw128_desc(st), dh = sw128_desc(st + kTileA), dl = sw128_desc(st + kTileA + kTileB);
-        const uint32_t td = tmem + b * kN;
+        const uint64_t dh = sw128_desc(st + kTileA), dl = sw128_desc(st + kTileA + kTileB);
 #pragma unroll
-        for (int k = 0; k < kKB / 16; k++) umma_bf16(td, da + 2 * k, dh + 2 * k, idesc, k > 0 ? 1u : 0u);
+        for (int h = 0; h < kMH; h++) {
+          const uint64_t da = sw128_desc(st + h * (kTileA / kMH));
+          const uint32_t td = tmem + b * (kMH * kN) + h * kN;
 #pragma unroll
-        for (int k = 0; k < kKB / 16; k++) umma_bf16(td, da + 2 * k, dl + 2 * k, idesc, 1u);
+          for (int k = 0; k < kKB / 16; k++) umma_bf16(td, da + 2 * k, dh + 2 * k, idesc, k > 0 ? 1u : 0u);
+#pragma unroll
+          for (int k = 0; k < kKB / 16; k++) umma_bf16(td, da + 2 * k, dl + 2 * k, idesc, 1u);
+        }
         umma_commit(&empty[s]);
         umma_commit(&tfull[b]);
       }
     }
-  } else {  // epilogue warps 2..9: TMEM lane quarter = warp % 4, column half = (warp - 2) / 4
+  } else {  // epilogue warps 2..9: TMEM lane quarter = warp % 4, MMA half = (warp - 2) / 4
     const int q = warp & 3, h = (warp - 2) >> 2;
-    const int o = m0 + q * 32 + lane;
-    constexpr int NC = kN / 2;
-    float acc[NC];
+    const int o = m0 + h * kM + q * 32 + lane;
+    float acc[kN];
 #pragma unroll
-    for (int j = 0; j < NC; j++) acc[j] = 0.f;
+    for (int j = 0; j < kN; j++) acc[j] = 0.f;
     const float* srow = a.scales + (int64_t)min(o, a.out - 1) * a.groups;
     for (int i = 0; i < nkb; i++) {
       const int b = i % kAcc;
       const float sc = srow[kb0 + i];
       if (!mbar_wait(&tfull[b], (i / kAcc) & 1, a.err)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * kN + h * NC;
-      uint32_t v0[32], v1[32];
-      tmem_ld32(taddr, v0);
-      tmem_ld32(taddr + 32, v1);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * (kMH * kN) + h * kN;
 #pragma unroll
-      for (int j = 0; j < 32; j++) acc[j] = fmaf(__uint_as_float(v0[j]), sc, acc[j]);
+      for (int c = 0; c < kN; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(taddr + c, v);
+        tmem_wait_ld();
+        if (c + 32 == kN) {  // buffer fully read: hand it back before the FMAs
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[b]);
+        }
 #pragma unroll
-      for (int j = 0; j < 32; j++) acc[32 + j] = fmaf(__uint_as_float(v1[j]), sc, acc[32 + j]);
+        for (int j = 0; j < 32; j++) acc[c + j] = fmaf(__uint_as_float(v[j]), sc, acc[c + j]);
+      }
     }
     if (o < a.out) {
       if (a.splits > 1) {
         float* P = a.partial + (int64_t)split * a.n * a.out;
 #pragma unroll
-        for (int j = 0; j < NC; j++) {
-          const int row = n0 + h * NC + j;
+        for (int j = 0; j < kN; j++) {
+          const int row = n0 + j;
           if (row < a.n) P[(int64_t)row * a.out + o] = acc[j];
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < NC; j++) {
-          const int row = n0 + h * NC + j;
+        for (int j = 0; j < kN; j++) {
+          const int row = n0 + j;
           if (row < a.n) store_out(a, row, o, acc[j]);
         }
       }
@@ -283,7 +291,7 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kAcc * kN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kAcc * kMH * kN));
   }
 }
 
