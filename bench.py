@@ -20,8 +20,11 @@ output budget so contexts are ragged, as in a running server.
             from pinned host memory and the sampled ids are read back every step;
             timed with events on the same stream around the whole K steps
             (host gaps included).
-Multi-GPU: each rank runs an independent replica (weak scaling); tensor
-parallelism is not built yet.
+Multi-GPU (--gpus N under torchrun): the N ranks serve the same 256-request
+engine tensor-parallel -- each holds 1/N of the heads, FFN columns and KV pool
+and the step all-reduces after o_proj and down_proj over NCCL -- so total
+work is fixed (strong scaling).  --parallel replicas runs N independent
+engines instead (weak scaling).
 `--impl reference` times the CPU oracle (the C restatement of the reference's
 Go step, all host threads) on a bounded sample of the same workload.
 """
@@ -116,17 +119,17 @@ def traffic_per_position():
 class DecodeState:
     """256 sessions in steady decode over one device model and page pool."""
 
-    def __init__(self, cfg, device, warmup, steps, mode):
+    def __init__(self, cfg, device, warmup, steps, mode, tp=(0, 1, None), workload_rank=0):
         from sr_go_tranformer_b200 import _abi as A
         from sr_go_tranformer_b200 import step as S
         self.A, self.S, self.cfg = A, S, cfg
-        prompts, outs, offsets, rng = workload(cfg, int(os.environ.get("RANK", "0")), warmup)
+        prompts, outs, offsets, rng = workload(cfg, workload_rank, warmup)
         self.prompts, self.outs = prompts, outs
         n = cfg["sessions"]
         pt = cfg["page_tokens"]
         d = S.make_desc(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
                         cfg["context"], cfg["rope_theta"], cfg["norm_eps"], cfg["tied"], False, cfg["fmt"], pt)
-        self.model = S.Model(d, device)
+        self.model = S.Model(d, device, tp_rank=tp[0], tp_size=tp[1], nccl_id=tp[2])
         self.model.init_synthetic(cfg["seed"], 0.02)
         self.model.set_mode(mode)
         reserve = int(np.sum((prompts + outs + pt - 1) // pt))
@@ -271,6 +274,7 @@ def main():
     ap.add_argument("--cpu-sessions", type=int, default=8)
     ap.add_argument("--ref-sessions", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"])
     args = ap.parse_args()
     cfg = dict(CONFIG)
     cfg["sessions"] = args.sessions
@@ -285,11 +289,18 @@ def main():
     import torch
     torch.cuda.set_device(local)
     dist = None
+    tp = world > 1 and args.parallel == "tp"
+    tp_args = (0, 1, None)
     if world > 1:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-    st = DecodeState(cfg, local, W, K, args.mode)
+        if tp:
+            from sr_go_tranformer_b200 import step as S
+            obj = [S.tp_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            tp_args = (rank, world, obj[0])
+    st = DecodeState(cfg, local, W, K, args.mode, tp=tp_args, workload_rank=0 if tp else rank)
     for _ in range(W):
         st.step()
     ext = torch.cuda.ExternalStream(st.stream())
@@ -322,12 +333,12 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
     span_max, e2e_max = float(t[0]), float(t[1])
-    tokens = cfg["sessions"] * K * world
+    tokens = cfg["sessions"] * K * (1 if tp else world)
     value = tokens / (span_max / 1000.0)
     e2e_val = tokens / (e2e_max / 1000.0)
     if rank == 0:
         peaks, peak_kind = measured_peaks()
-        kvd = cfg["dim"] // cfg["heads"] * cfg["kv_heads"]
+        kvd = cfg["dim"] // cfg["heads"] * cfg["kv_heads"] // (world if tp else 1)  # this rank's KV width
         kv_pos_bytes = 2 * kvd * 4  # K + V row of one position, one layer
         attn_launches = launches[5]
         attn_ms = ms[5] / max(1, attn_launches)
@@ -335,19 +346,21 @@ def main():
         attn_bytes = positions * kv_pos_bytes + 2 * cfg["sessions"] * cfg["dim"] * 4
         achieved = attn_bytes / (attn_ms / 1000.0) / 1e9
         tr = traffic_per_position()
-        traffic = None if tr is None else float(tr["bytes_per_position_layer"] * positions +
+        kv_share = kvd / (cfg["dim"] // cfg["heads"] * cfg["kv_heads"])
+        traffic = None if tr is None else float(tr["bytes_per_position_layer"] * kv_share * positions +
                                                 tr.get("fixed_bytes", 0))
-        wbytes = weight_bytes(cfg)
+        wbytes = weight_bytes(cfg) / (world if tp else 1)  # this rank's share (embedding/head replicated: approx)
         step_bytes = wbytes + cfg["layers"] * (positions * kv_pos_bytes + cfg["sessions"] * kv_pos_bytes) + \
             4 * cfg["sessions"] * cfg["vocab"]
         cls_total = sum(cls_ms) or 1.0
         line = {
             "metric": METRIC, "value": value, "unit": "output tok/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": span_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": span_max / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
+            "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfg["name"], "sessions": cfg["sessions"], "layers": cfg["layers"],
                        "page_tokens": cfg["page_tokens"], "weights": "q8 (64-col blocks, fp32 scales)",
-                       "mode": args.mode, "parallelism": f"replicas{world}",
+                       "mode": args.mode, "parallelism": f"tp{world}" if tp else f"replicas{world}",
                        "kv_state": "synthetic prefilled pages (prompt + decode offset)",
                        "l2": "inputs larger than L2 (KV pool > 100 GB)",
                        "sampling": "T0.8 k40 p0.95 penalty1.1, SplitMix64"},

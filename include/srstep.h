@@ -112,6 +112,23 @@ const char *sr_version(void);
  * RoPE tables (:5034-5043) and the step workspace (decodeWorkspace,
  * :6064-6096; bounded by maxActivationElements, :50). */
 int sr_model_create(const sr_model_desc *desc, int device, sr_model **out);
+/* Tensor-parallel rank `tp_rank` of `tp_size` (SURVEY-style sharding of the
+ * reference model; the reference itself has no multi-GPU path): Q/K/V and
+ * gate/up keep a contiguous block of output rows (whole heads / FFN columns),
+ * o_proj and down_proj the matching block of input columns, the KV pool holds
+ * only this rank's KV heads, and embedding, norms and LM head are replicated.
+ * The step all-reduces (NCCL, fp32 sum) after o_proj and down_proj.  nccl_id is
+ * the 128-byte id from sr_tp_unique_id on rank 0, shared with every rank;
+ * creation blocks until all ranks have joined.  Requires heads, kv_heads and
+ * hidden divisible by tp_size (and, for quantized weights, column shards of
+ * whole 64-column blocks).  Parameters are still loaded as full tensors. */
+int sr_model_create_tp(const sr_model_desc *desc, int device, int32_t tp_rank, int32_t tp_size, const void *nccl_id,
+                       sr_model **out);
+/* 128-byte NCCL unique id for sr_model_create_tp (call on rank 0). */
+int sr_tp_unique_id(void *id_out);
+/* Host-only: rows [shard[0], shard[0]+shard[1]) and columns [shard[2],
+ * shard[2]+shard[3]) of parameter `index` that rank `rank` of `size` holds. */
+int sr_tp_shard(const sr_model_desc *desc, int32_t rank, int32_t size, int32_t index, int32_t *shard);
 int sr_model_destroy(sr_model *m);
 int sr_model_param_count(const sr_model *m, int32_t *count);
 int sr_model_param_info(const sr_model *m, int32_t index, sr_param_info *out);
@@ -126,7 +143,8 @@ int sr_model_load_param(sr_model *m, int32_t index, const void *values, size_t v
  * quantizer (readParam, :857-880; lowBitScale, :3877-3891; q8Value, :3893).
  * This is the path of loadHFModelFormatKV for f32/q8/q4/q4-mixed models. */
 int sr_model_load_param_f32(sr_model *m, int32_t index, const float *values, size_t count);
-/* Read one parameter back (same layout), for verification. */
+/* Read one parameter back (same layout; a tensor-parallel rank returns its
+ * shard, whose extent sr_tp_shard gives), for verification. */
 int sr_model_read_param(const sr_model *m, int32_t index, void *values, size_t value_bytes, float *scales,
                         size_t scale_count);
 /* Synthetic random init on the device (no reference counterpart beyond

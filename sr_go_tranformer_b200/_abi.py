@@ -24,7 +24,7 @@ EXPORTED = [
     "sr_kvpool_fill_synthetic", "sr_step", "sr_step_logits", "sr_sample", "sr_step_sample", "sr_engine_create",
     "sr_engine_destroy", "sr_engine_submit", "sr_engine_tick", "sr_engine_poll", "sr_engine_stats_get",
     "sr_engine_last_schedule", "sr_engine_session_pages", "sr_profile_set", "sr_profile_read", "sr_model_stream",
-    "sr_step_noalloc",
+    "sr_step_noalloc", "sr_model_create_tp", "sr_tp_unique_id", "sr_tp_shard",
 ]
 PROF_CLASSES = ["meta", "embed", "norm", "linear", "rope_kv", "attention", "swiglu", "head", "sample"]
 
@@ -108,6 +108,9 @@ def lib():
         "sr_step": (C.c_int, [P, P, C.POINTER(Batch), P, P]),
         "sr_step_logits": (C.c_int, [P, C.POINTER(P)]),
         "sr_step_noalloc": (C.c_int, [P, P, C.POINTER(Batch), P]),
+        "sr_model_create_tp": (C.c_int, [C.POINTER(ModelDesc), C.c_int, I32, I32, P, C.POINTER(P)]),
+        "sr_tp_unique_id": (C.c_int, [P]),
+        "sr_tp_shard": (C.c_int, [C.POINTER(ModelDesc), I32, I32, I32, P]),
         "sr_sample": (C.c_int, [P, I32, P, P, P, P, I32, P]),
         "sr_step_sample": (C.c_int, [P, P, C.POINTER(Batch), P, P, P, P, I32, P]),
         "sr_engine_create": (C.c_int, [P, C.POINTER(EngineConfig), C.POINTER(P)]),

@@ -49,8 +49,12 @@ struct StepMeta {
   int32_t* n_heads;     // [1]
 };
 
+// Per-device model dimensions.  With tensor parallelism, heads, kv_heads,
+// hidden, qd (= heads*hd, the attention width) and kvd are this rank's local
+// shares; dim (the residual width) and vocab stay whole.
 struct ModelDims {
   int32_t vocab, dim, hidden, layers, heads, kv_heads, context, hd, kvd, group, page_tokens;
+  int32_t qd, tp_rank, tp_size;
   int64_t page_elems;   // 2 * page_tokens * kvd * layers
 };
 

@@ -389,7 +389,7 @@ __global__ void k_rope_kv_exact(float* __restrict__ Q, const float* __restrict__
   const int half = dm.hd / 2;
   const float* ct = cos_t + (int64_t)pos * half;
   const float* st = sin_t + (int64_t)pos * half;
-  float* q = Q + (int64_t)r * dm.dim;
+  float* q = Q + (int64_t)r * dm.qd;
   for (int idx = threadIdx.x; idx < dm.heads * half; idx += blockDim.x) {
     int h = idx / half, j = idx % half;
     int i = h * dm.hd + j, z = i + half;
@@ -502,7 +502,7 @@ __global__ void k_attention_exact(AttnArgs a) {
   double* sum_s = (double*)(smem + lay.sum);
   double* lse_s = (double*)(smem + lay.lse);
   const int sstride = a.smem_scores ? a.ls : kAttnTile;
-  const float* qrow = a.Q + (int64_t)r * a.dm.dim + (int64_t)kh * group * hd;
+  const float* qrow = a.Q + (int64_t)r * a.dm.qd + (int64_t)kh * group * hd;
   for (int i = threadIdx.x; i < group * hd; i += blockDim.x) q_s[i] = qrow[i];
   if (threadIdx.x < group) {
     mx_s[threadIdx.x] = -FLT_MAX;
@@ -585,7 +585,7 @@ __global__ void k_attention_exact(AttnArgs a) {
     }
   }
   if (owner) {
-    float* out = a.A + (int64_t)r * a.dm.dim + (int64_t)(kh * group + pg) * hd + pj;
+    float* out = a.A + (int64_t)r * a.dm.qd + (int64_t)(kh * group + pg) * hd + pj;
     *(float4*)out = acc;
   }
 }

@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
   // query slices: lane covers dims 4*(lane%8) + 32*i for the score phase
   float4 q[G][4];
   {
-    const float* qrow = a.Q + (int64_t)r * a.dm.dim + (int64_t)kh * G * HD;
+    const float* qrow = a.Q + (int64_t)r * a.dm.qd + (int64_t)kh * G * HD;
     const int jl = lane & 7;
 #pragma unroll
     for (int g = 0; g < G; g++)
@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_tile(FastAttnArgs a) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float4 q[G][4];
   {
-    const float* qrow = a.Q + (int64_t)r * a.dm.dim + (int64_t)kh * G * HD;
+    const float* qrow = a.Q + (int64_t)r * a.dm.qd + (int64_t)kh * G * HD;
     const int jl = lane % LPP;
 #pragma unroll
     for (int g = 0; g < G; g++)
@@ -445,7 +445,7 @@ __global__ void __launch_bounds__(HD) k_attn_combine(FastAttnArgs a) {
     den += w * a.part_ml[((base + s) * G + g) * 2 + 1];
     num += w * a.part_o[((base + s) * G + g) * HD + d];
   }
-  const int64_t o = (int64_t)r * a.dm.dim + (int64_t)h * HD + d;
+  const int64_t o = (int64_t)r * a.dm.qd + (int64_t)h * HD + d;
   if (a.xh)
     split_bf16(num / den, a.xh + o, a.xl + o);
   else

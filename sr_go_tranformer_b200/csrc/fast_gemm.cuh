@@ -29,7 +29,7 @@ struct TcState {
   TcMatrix head;
   __nv_bfloat16* xh = nullptr;
   __nv_bfloat16* xl = nullptr;
-  CUtensorMap xh_d, xl_d, xh_h, xl_h;
+  CUtensorMap xh_d, xl_d, xh_h, xl_h, xh_q, xl_q;  // operand maps for in = dim, hidden, attention width
   float* partial = nullptr;
   size_t partial_cap = 0;
   int* err = nullptr;
@@ -141,7 +141,7 @@ inline bool tc_prepare(sr_model* m) {
   t->version = m->weights_version;
   t->disabled = true;
   const ModelDims& dm = m->dm;
-  if (m->d.weight_format == SR_FMT_F32 || dm.dim % 8 || dm.hidden % 8 || !encode_fn()) return false;
+  if (m->d.weight_format == SR_FMT_F32 || dm.dim % 8 || dm.hidden % 8 || dm.qd % 8 || !encode_fn()) return false;
   cudaFuncSetAttribute(tc::k_gemm_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
   const int L = dm.layers;
   t->qkv.resize(L);
@@ -161,7 +161,7 @@ inline bool tc_prepare(sr_model* m) {
     tc_free(t);
     return false;
   }
-  const int xcols = std::max(dm.dim, dm.hidden);
+  const int xcols = std::max(std::max(dm.dim, dm.hidden), dm.qd);
   if (!tc_alloc(t, (void**)&t->xh, (size_t)kMaxRows * xcols * 2) ||
       !tc_alloc(t, (void**)&t->xl, (size_t)kMaxRows * xcols * 2) || !tc_alloc(t, (void**)&t->err, 16)) {
     tc_free(t);
@@ -177,7 +177,8 @@ inline bool tc_prepare(sr_model* m) {
   }
   if (!make_map(&t->xh_d, t->xh, dm.dim, kMaxRows, tc::kN) || !make_map(&t->xl_d, t->xl, dm.dim, kMaxRows, tc::kN) ||
       !make_map(&t->xh_h, t->xh, dm.hidden, kMaxRows, tc::kN) ||
-      !make_map(&t->xl_h, t->xl, dm.hidden, kMaxRows, tc::kN)) {
+      !make_map(&t->xl_h, t->xl, dm.hidden, kMaxRows, tc::kN) || !make_map(&t->xh_q, t->xh, dm.qd, kMaxRows, tc::kN) ||
+      !make_map(&t->xl_q, t->xl, dm.qd, kMaxRows, tc::kN)) {
     tc_free(t);
     return false;
   }
@@ -201,7 +202,8 @@ inline void tc_split_x(sr_model* m, const float* X, int n, int in) {
   sr_count_launch(m);
 }
 
-inline bool tc_gemm(sr_model* m, const TcMatrix& W, bool hidden_in, int n, tc::GemmArgs a) {
+// in_kind: 0 = the residual width (dim), 1 = hidden, 2 = the attention width (qd).
+inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::GemmArgs a) {
   TcState* t = tc_state(m);
   a.n = n;
   a.out = W.rows;
@@ -247,8 +249,8 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, bool hidden_in, int n, tc::G
   } else {
     a.partial = nullptr;
   }
-  const CUtensorMap& xh = hidden_in ? t->xh_h : t->xh_d;
-  const CUtensorMap& xl = hidden_in ? t->xl_h : t->xl_d;
+  const CUtensorMap& xh = in_kind == 1 ? t->xh_h : (in_kind == 2 ? t->xh_q : t->xh_d);
+  const CUtensorMap& xl = in_kind == 1 ? t->xl_h : (in_kind == 2 ? t->xl_q : t->xl_d);
   tc::k_gemm_q<<<dim3(nt, mt, splits), tc::kThreads, tc::kSmemBytes, m->stream>>>(W.map, xh, xl, a);
   sr_count_launch(m);
   if (splits > 1) {
@@ -284,12 +286,12 @@ inline bool tc_qkv(sr_model* m, int l, int n, bool presplit = false) {
   const Param* B = m->d.qkv_bias ? &m->params[2 + 9 * dm.layers + 3 * l] : nullptr;
   tc::GemmArgs a{};
   a.nseg = 3;
-  a.seg[0] = seg(dm.dim, m->Q, dm.dim, B ? (const float*)B[0].values : nullptr, nullptr);
+  a.seg[0] = seg(dm.qd, m->Q, dm.qd, B ? (const float*)B[0].values : nullptr, nullptr);
   a.seg[1] = seg(dm.kvd, m->K, dm.kvd, B ? (const float*)B[1].values : nullptr, nullptr);
   a.seg[2] = seg(dm.kvd, m->V, dm.kvd, B ? (const float*)B[2].values : nullptr, nullptr);
   a.out_map = nullptr;
   if (!presplit) tc_split_x(m, m->N, n, dm.dim);
-  return tc_gemm(m, tc_state(m)->qkv[l], false, n, a);
+  return tc_gemm(m, tc_state(m)->qkv[l], 0, n, a);
 }
 // gate|up in one GEMM.
 inline bool tc_gateup(sr_model* m, int l, int n, bool presplit = false) {
@@ -301,25 +303,27 @@ inline bool tc_gateup(sr_model* m, int l, int n, bool presplit = false) {
   a.seg[1] = seg(dm.hidden, m->U, dm.hidden, nullptr, nullptr);
   a.out_map = nullptr;
   if (!presplit) tc_split_x(m, m->N, n, dm.dim);
-  return tc_gemm(m, tc_state(m)->gateup[l], false, n, a);
+  return tc_gemm(m, tc_state(m)->gateup[l], 0, n, a);
 }
-// O / down projection with the residual add (X += W x).
-inline bool tc_resid(sr_model* m, const TcMatrix& W, const float* X, int n, bool hidden_in, bool presplit) {
+// O / down projection into y (with the residual add y = resid + W x when
+// resid is set; tensor-parallel ranks write their partial sum instead).
+inline bool tc_proj(sr_model* m, const TcMatrix& W, const float* X, int n, int in_kind, bool presplit, float* y,
+                    const float* resid) {
   const ModelDims& dm = m->dm;
   tc::GemmArgs a{};
   a.nseg = 1;
-  a.seg[0] = seg(dm.dim, m->X, dm.dim, nullptr, m->X);
+  a.seg[0] = seg(dm.dim, y, dm.dim, nullptr, resid);
   a.out_map = nullptr;
-  if (!presplit) tc_split_x(m, X, n, hidden_in ? dm.hidden : dm.dim);
-  return tc_gemm(m, W, hidden_in, n, a);
+  if (!presplit) tc_split_x(m, X, n, in_kind == 1 ? dm.hidden : (in_kind == 2 ? dm.qd : dm.dim));
+  return tc_gemm(m, W, in_kind, n, a);
 }
-inline bool tc_o(sr_model* m, int l, int n, bool presplit = false) {
+inline bool tc_o(sr_model* m, int l, int n, bool presplit, float* y, const float* resid) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
-  return tc_resid(m, tc_state(m)->o[l], m->A, n, false, presplit);
+  return tc_proj(m, tc_state(m)->o[l], m->A, n, 2, presplit, y, resid);
 }
-inline bool tc_down(sr_model* m, int l, int n, bool presplit = false) {
+inline bool tc_down(sr_model* m, int l, int n, bool presplit, float* y, const float* resid) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
-  return tc_resid(m, tc_state(m)->down[l], m->H, n, true, presplit);
+  return tc_proj(m, tc_state(m)->down[l], m->H, n, 1, presplit, y, resid);
 }
 inline bool tc_head(sr_model* m, int heads, bool presplit = false) {
   if (heads < kTcMinRows || !tc_prepare(m)) return false;
@@ -329,7 +333,7 @@ inline bool tc_head(sr_model* m, int heads, bool presplit = false) {
   a.seg[0] = seg(dm.vocab, m->logits, dm.vocab, nullptr, nullptr);
   a.out_map = m->meta.head_dst;
   if (!presplit) tc_split_x(m, m->N, heads, dm.dim);
-  return tc_gemm(m, tc_state(m)->head, false, heads, a);
+  return tc_gemm(m, tc_state(m)->head, 0, heads, a);
 }
 
 // After the step's stream synchronize: SR_ETIMEOUT if a bounded wait expired.

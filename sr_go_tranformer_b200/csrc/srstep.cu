@@ -20,6 +20,7 @@
 #include "fast_gemm.cuh"
 #include "sampler.cuh"
 #include "srstep_internal.h"
+#include "nccl_dl.h"
 
 using namespace sr;
 
@@ -80,6 +81,7 @@ static float hf_inverse_frequency(const sr_model_desc& c, int hd, int index) {
 static void free_model(sr_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
+  if (m->nccl_comm) nccl::api().CommDestroy((nccl::Comm)m->nccl_comm);
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_stage) cudaFreeHost(m->h_stage);
   if (m->stream) cudaStreamDestroy(m->stream);
@@ -97,11 +99,9 @@ int sr_model_alloc(sr_model* m, void** p, size_t bytes) {
   return SR_OK;
 }
 
-extern "C" int sr_model_create(const sr_model_desc* desc, int device, sr_model** out) {
-  if (!desc || !out) return sr_fail(SR_EINVAL, "null argument");
-  *out = nullptr;
-  const sr_model_desc& c = *desc;
-  // Config.validateShapeLimits (M:98-118) plus this implementation's limits.
+// Validation shared by the single-GPU and tensor-parallel constructors
+// (Config.validateShapeLimits, M:98-118, plus this implementation's limits).
+static int validate_desc(const sr_model_desc& c, int tp_size) {
   if (c.vocab < 1 || c.vocab > 262144 || c.dim < 2 || c.dim > 8192 || c.hidden < 1 || c.hidden > 32768 ||
       c.layers < 1 || c.layers > 128 || c.heads < 1 || c.heads > c.dim || c.kv_heads < 1 || c.kv_heads > c.heads ||
       c.context < 1 || c.context > 32768)
@@ -118,6 +118,115 @@ extern "C" int sr_model_create(const sr_model_desc* desc, int device, sr_model**
   if (group * hd / 4 > 1024) return sr_fail(SR_EUNSUPPORTED, "query heads per KV head x head_dim exceeds 4096");
   if (c.rope_scaling && (c.rope_low_freq_factor <= 0 || c.rope_high_freq_factor <= c.rope_low_freq_factor))
     return sr_fail(SR_EINVAL, "invalid llama3 rope scaling");
+  if (tp_size < 1 || tp_size > 64) return sr_fail(SR_EINVAL, "tensor-parallel size must be 1..64");
+  if (tp_size > 1) {
+    if (c.heads % tp_size || c.kv_heads % tp_size || c.hidden % tp_size)
+      return sr_fail(SR_EUNSUPPORTED, "tensor parallelism needs heads, kv_heads and hidden divisible by the rank count");
+    if (c.weight_format != SR_FMT_F32 && ((c.heads / tp_size * hd) % kQBlock || (c.hidden / tp_size) % kQBlock))
+      return sr_fail(SR_EUNSUPPORTED, "tensor-parallel column shards of quantized matrices must hold whole 64-column blocks");
+  }
+  return SR_OK;
+}
+
+// Parameter table in hfProfileSpecs order (M:407-442) for rank `rank` of
+// `size`: Q/K/V/gate/up keep a contiguous block of rows, O/down and the qkv
+// biases a contiguous block of columns; everything else is replicated.
+int sr_param_table(const sr_model_desc& c, int rank, int size, std::vector<Param>* params,
+                   std::vector<Shard>* shards) {
+  params->clear();
+  shards->clear();
+  const int hd = c.dim / c.heads, kd = hd * c.kv_heads;
+  auto add = [&](int rows, int cols, bool matrix, bool eh, int kind) {
+    Shard sh{rows, cols, 0, 0};
+    Param p;
+    p.rows = rows;
+    p.cols = cols;
+    if (kind == 1) {
+      p.rows = rows / size;
+      sh.row0 = rank * p.rows;
+    } else if (kind == 2) {
+      p.cols = cols / size;
+      sh.col0 = rank * p.cols;
+    }
+    p.format = matrix ? matrix_format(c.weight_format, eh) : kF32;
+    p.values = nullptr;
+    p.scales = nullptr;
+    params->push_back(p);
+    shards->push_back(sh);
+  };
+  const int L = c.layers, d = c.dim, h = c.hidden;
+  add(c.vocab, d, true, true, 0);
+  for (int l = 0; l < L; l++) {
+    add(1, d, false, false, 0);
+    add(d, d, true, false, 1);
+    add(kd, d, true, false, 1);
+    add(kd, d, true, false, 1);
+    add(d, d, true, false, 2);
+    add(1, d, false, false, 0);
+    add(h, d, true, false, 1);
+    add(h, d, true, false, 1);
+    add(d, h, true, false, 2);
+  }
+  add(1, d, false, false, 0);
+  if (c.qkv_bias)
+    for (int l = 0; l < L; l++) {
+      add(1, d, false, false, 2);
+      add(1, kd, false, false, 2);
+      add(1, kd, false, false, 2);
+    }
+  if (!c.tied) add(c.vocab, d, true, true, 0);
+  return SR_OK;
+}
+
+extern "C" int sr_tp_shard(const sr_model_desc* desc, int32_t rank, int32_t size, int32_t index, int32_t* shard) {
+  if (!desc || !shard) return sr_fail(SR_EINVAL, "null argument");
+  int rc = validate_desc(*desc, size);
+  if (rc != SR_OK) return rc;
+  if (rank < 0 || rank >= size) return sr_fail(SR_EINVAL, "rank out of range");
+  std::vector<Param> ps;
+  std::vector<Shard> sh;
+  sr_param_table(*desc, rank, size, &ps, &sh);
+  if (index < 0 || index >= (int32_t)ps.size()) return sr_fail(SR_EINVAL, "parameter index out of range");
+  shard[0] = sh[index].row0;
+  shard[1] = ps[index].rows;
+  shard[2] = sh[index].col0;
+  shard[3] = ps[index].cols;
+  return SR_OK;
+}
+
+static int model_create(const sr_model_desc* desc, int device, int tp_rank, int tp_size, const void* nccl_id,
+                        sr_model** out);
+
+extern "C" int sr_model_create(const sr_model_desc* desc, int device, sr_model** out) {
+  return model_create(desc, device, 0, 1, nullptr, out);
+}
+
+extern "C" int sr_tp_unique_id(void* id_out) {
+  if (!id_out) return sr_fail(SR_EINVAL, "null argument");
+  nccl::Api& api = nccl::api();
+  if (!api.ok) return sr_fail(SR_EUNSUPPORTED, api.error);
+  nccl::UniqueId id;
+  int r = api.GetUniqueId(&id);
+  if (r != nccl::kSuccess) return sr_fail(SR_EDEVICE, std::string("ncclGetUniqueId: ") + api.GetErrorString(r));
+  memcpy(id_out, &id, sizeof(id));
+  return SR_OK;
+}
+
+extern "C" int sr_model_create_tp(const sr_model_desc* desc, int device, int32_t tp_rank, int32_t tp_size,
+                                  const void* nccl_id, sr_model** out) {
+  if (tp_size > 1 && !nccl_id) return sr_fail(SR_EINVAL, "tensor parallelism needs the rank-0 NCCL id");
+  if (tp_rank < 0 || tp_rank >= tp_size) return sr_fail(SR_EINVAL, "rank out of range");
+  return model_create(desc, device, tp_rank, tp_size, nccl_id, out);
+}
+
+static int model_create(const sr_model_desc* desc, int device, int tp_rank, int tp_size, const void* nccl_id,
+                        sr_model** out) {
+  if (!desc || !out) return sr_fail(SR_EINVAL, "null argument");
+  *out = nullptr;
+  const sr_model_desc& c = *desc;
+  int rc = validate_desc(c, tp_size);
+  if (rc != SR_OK) return rc;
+  const int hd = c.dim / c.heads, group = c.heads / c.kv_heads;
   int ndev = 0;
   CK(cudaGetDeviceCount(&ndev));
   if (device < 0 || device >= ndev) return sr_fail(SR_EINVAL, "invalid device ordinal");
@@ -130,50 +239,38 @@ extern "C" int sr_model_create(const sr_model_desc* desc, int device, sr_model**
   ModelDims& dm = m->dm;
   dm.vocab = c.vocab;
   dm.dim = c.dim;
-  dm.hidden = c.hidden;
+  dm.hidden = c.hidden / tp_size;
   dm.layers = c.layers;
-  dm.heads = c.heads;
-  dm.kv_heads = c.kv_heads;
+  dm.heads = c.heads / tp_size;
+  dm.kv_heads = c.kv_heads / tp_size;
   dm.context = c.context;
   dm.hd = hd;
-  dm.kvd = hd * c.kv_heads;
+  dm.kvd = hd * dm.kv_heads;
+  dm.qd = hd * dm.heads;
   dm.group = group;
+  dm.tp_rank = tp_rank;
+  dm.tp_size = tp_size;
   dm.page_tokens = c.page_tokens;
   dm.page_elems = 2LL * c.page_tokens * dm.kvd * c.layers;
-
-  // Parameter table in hfProfileSpecs order (M:407-442).
-  auto add = [&](int rows, int cols, bool matrix, bool eh) {
-    Param p;
-    p.rows = rows;
-    p.cols = cols;
-    p.format = matrix ? matrix_format(c.weight_format, eh) : kF32;
-    p.values = nullptr;
-    p.scales = nullptr;
-    m->params.push_back(p);
-  };
-  const int L = c.layers, d = c.dim, kd = dm.kvd, h = c.hidden;
-  add(c.vocab, d, true, true);
-  for (int l = 0; l < L; l++) {
-    add(1, d, false, false);
-    add(d, d, true, false);
-    add(kd, d, true, false);
-    add(kd, d, true, false);
-    add(d, d, true, false);
-    add(1, d, false, false);
-    add(h, d, true, false);
-    add(h, d, true, false);
-    add(d, h, true, false);
-  }
-  add(1, d, false, false);
-  if (c.qkv_bias)
-    for (int l = 0; l < L; l++) {
-      add(1, d, false, false);
-      add(1, kd, false, false);
-      add(1, kd, false, false);
+  sr_param_table(c, tp_rank, tp_size, &m->params, &m->shards);
+  const int L = c.layers, d = c.dim, kd = dm.kvd, h = dm.hidden;
+  if (tp_size > 1) {
+    nccl::Api& api = nccl::api();
+    if (!api.ok) {
+      delete m;
+      return sr_fail(SR_EUNSUPPORTED, api.error);
     }
-  if (!c.tied) add(c.vocab, d, true, true);
+    nccl::UniqueId id;
+    memcpy(&id, nccl_id, sizeof(id));
+    nccl::Comm comm = nullptr;
+    int r = api.CommInitRank(&comm, tp_size, id, tp_rank);
+    if (r != nccl::kSuccess) {
+      delete m;
+      return sr_fail(SR_EDEVICE, std::string("ncclCommInitRank: ") + api.GetErrorString(r));
+    }
+    m->nccl_comm = comm;
+  }
 
-  int rc;
   for (auto& p : m->params) {
     int64_t vb = param_value_bytes(p.rows, p.cols, p.format);
     int64_t sc = param_scale_count(p.rows, p.cols, p.format);
@@ -282,25 +379,52 @@ extern "C" int sr_model_param_info(const sr_model* m, int32_t index, sr_param_in
   if (!m || !out) return sr_fail(SR_EINVAL, "null argument");
   if (index < 0 || index >= (int32_t)m->params.size()) return sr_fail(SR_EINVAL, "parameter index out of range");
   const Param& p = m->params[index];
-  out->rows = p.rows;
-  out->cols = p.cols;
+  const Shard& sh = m->shards[index];
+  out->rows = sh.full_rows;
+  out->cols = sh.full_cols;
   out->format = p.format;
   out->reserved = 0;
-  out->value_bytes = param_value_bytes(p.rows, p.cols, p.format);
-  out->scale_count = param_scale_count(p.rows, p.cols, p.format);
+  out->value_bytes = param_value_bytes(sh.full_rows, sh.full_cols, p.format);
+  out->scale_count = param_scale_count(sh.full_rows, sh.full_cols, p.format);
   return SR_OK;
+}
+
+// Copy this rank's shard (rows [row0, row0+rows), columns [col0, col0+cols))
+// out of a full host tensor in the reference layout.  Column shards start on
+// 64-column blocks, so Q4 bytes and scale blocks split cleanly.
+static void extract_shard(const Param& p, const Shard& sh, const void* full_values, const float* full_scales,
+                          std::vector<uint8_t>* values, std::vector<float>* scales) {
+  const int64_t vb = param_value_bytes(p.rows, p.cols, p.format), sc = param_scale_count(p.rows, p.cols, p.format);
+  values->resize((size_t)vb);
+  scales->resize((size_t)sc);
+  const int64_t full_row_bytes = param_value_bytes(1, sh.full_cols, p.format);
+  const int64_t row_bytes = param_value_bytes(1, p.cols, p.format);
+  const int64_t col_byte0 = param_value_bytes(1, sh.col0, p.format);
+  const int64_t full_groups = (sh.full_cols + kQBlock - 1) / kQBlock, groups = (p.cols + kQBlock - 1) / kQBlock;
+  for (int64_t r = 0; r < p.rows; r++) {
+    const uint8_t* src = (const uint8_t*)full_values + (sh.row0 + r) * full_row_bytes + col_byte0;
+    memcpy(values->data() + r * row_bytes, src, (size_t)row_bytes);
+    if (sc)
+      memcpy(scales->data() + r * groups, full_scales + (sh.row0 + r) * full_groups + sh.col0 / kQBlock,
+             (size_t)groups * 4);
+  }
 }
 extern "C" int sr_model_load_param(sr_model* m, int32_t index, const void* values, size_t value_bytes,
                                    const float* scales, size_t scale_count) {
   if (!m || !values) return sr_fail(SR_EINVAL, "null argument");
   if (index < 0 || index >= (int32_t)m->params.size()) return sr_fail(SR_EINVAL, "parameter index out of range");
   Param& p = m->params[index];
-  int64_t vb = param_value_bytes(p.rows, p.cols, p.format), sc = param_scale_count(p.rows, p.cols, p.format);
-  if ((int64_t)value_bytes != vb) return sr_fail(SR_EINVAL, "value byte count does not match the parameter layout");
-  if ((int64_t)scale_count != sc || (sc && !scales)) return sr_fail(SR_EINVAL, "scale count does not match the parameter layout");
+  const Shard& sh = m->shards[index];
+  const int64_t fvb = param_value_bytes(sh.full_rows, sh.full_cols, p.format);
+  const int64_t fsc = param_scale_count(sh.full_rows, sh.full_cols, p.format);
+  if ((int64_t)value_bytes != fvb) return sr_fail(SR_EINVAL, "value byte count does not match the parameter layout");
+  if ((int64_t)scale_count != fsc || (fsc && !scales)) return sr_fail(SR_EINVAL, "scale count does not match the parameter layout");
   CK(cudaSetDevice(m->device));
-  CK(cudaMemcpy(p.values, values, (size_t)vb, cudaMemcpyHostToDevice));
-  if (sc) CK(cudaMemcpy(p.scales, scales, (size_t)sc * 4, cudaMemcpyHostToDevice));
+  std::vector<uint8_t> v;
+  std::vector<float> sv;
+  extract_shard(p, sh, values, scales, &v, &sv);
+  CK(cudaMemcpy(p.values, v.data(), v.size(), cudaMemcpyHostToDevice));
+  if (!sv.empty()) CK(cudaMemcpy(p.scales, sv.data(), sv.size() * 4, cudaMemcpyHostToDevice));
   m->weights_version++;
   return SR_OK;
 }
@@ -336,7 +460,10 @@ __device__ __forceinline__ float synth_value(uint64_t seed, uint64_t e, double s
 }
 // One thread per (row, 64-column block): generate, then quantize with the
 // reference's block quantizer (readParam M:857-880, lowBitScale M:3877-3891).
-__global__ void k_init_param(Param p, uint64_t seed, uint64_t e0, double scale, int norm, const float* src) {
+// (row0, col0, full_cols) place the local shard in the full tensor, so every
+// rank generates exactly its part of the same model.
+__global__ void k_init_param(Param p, uint64_t seed, uint64_t e0, double scale, int norm, const float* src, int row0,
+                             int col0, int full_cols) {
   const int64_t groups = (p.cols + kQBlock - 1) / kQBlock;
   const int64_t total = (int64_t)p.rows * groups;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
@@ -345,7 +472,9 @@ __global__ void k_init_param(Param p, uint64_t seed, uint64_t e0, double scale, 
     float v[kQBlock];
     float amax = 0.f;
     for (int j = j0; j < j1; j++) {
-      float x = src ? src[row * p.cols + j] : (norm ? 1.0f : synth_value(seed, e0 + (uint64_t)(row * p.cols + j), scale));
+      float x = src ? src[row * p.cols + j]
+                    : (norm ? 1.0f
+                            : synth_value(seed, e0 + (uint64_t)((row0 + row) * (int64_t)full_cols + col0 + j), scale));
       v[j - j0] = x;
       amax = fmaxf(amax, fabsf(x));
     }
@@ -390,9 +519,11 @@ extern "C" int sr_model_init_synthetic(sr_model* m, uint64_t seed, double scale)
     if (p.format == kQ4) CK(cudaMemsetAsync(p.values, 0, (size_t)param_value_bytes(p.rows, p.cols, p.format), m->stream));
     int64_t work = (int64_t)p.rows * ((p.cols + kQBlock - 1) / kQBlock);
     int blocks = (int)std::min<int64_t>((work + 255) / 256, 148 * 32);
-    k_init_param<<<blocks, 256, 0, m->stream>>>(p, seed, e0, scale, norm ? 1 : 0, nullptr);
+    const Shard& sh = m->shards[i];
+    k_init_param<<<blocks, 256, 0, m->stream>>>(p, seed, e0, scale, norm ? 1 : 0, nullptr, sh.row0, sh.col0,
+                                                 sh.full_cols);
     CK(cudaGetLastError());
-    if (!norm) e0 += (uint64_t)p.rows * p.cols;
+    if (!norm) e0 += (uint64_t)sh.full_rows * sh.full_cols;
   }
   CK(cudaStreamSynchronize(m->stream));
   m->weights_version++;
@@ -403,21 +534,30 @@ extern "C" int sr_model_load_param_f32(sr_model* m, int32_t index, const float* 
   if (!m || !values) return sr_fail(SR_EINVAL, "null argument");
   if (index < 0 || index >= (int32_t)m->params.size()) return sr_fail(SR_EINVAL, "parameter index out of range");
   Param& p = m->params[index];
-  if ((int64_t)count != (int64_t)p.rows * p.cols) return sr_fail(SR_EINVAL, "value count does not match rows*cols");
+  const Shard& sh = m->shards[index];
+  if ((int64_t)count != (int64_t)sh.full_rows * sh.full_cols)
+    return sr_fail(SR_EINVAL, "value count does not match rows*cols");
   CK(cudaSetDevice(m->device));
+  // this rank's rows/columns of the full fp32 tensor
+  Param fp = p;
+  fp.format = kF32;
+  std::vector<uint8_t> local;
+  std::vector<float> unused;
+  extract_shard(fp, sh, values, nullptr, &local, &unused);
+  const size_t lcount = (size_t)p.rows * p.cols;
   float* tmp = nullptr;
-  cudaError_t e = cudaMalloc((void**)&tmp, count * 4);
+  cudaError_t e = cudaMalloc((void**)&tmp, lcount * 4);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return sr_fail(SR_ENOMEM, "staging allocation for a parameter failed");
   }
-  e = cudaMemcpy(tmp, values, count * 4, cudaMemcpyHostToDevice);
+  e = cudaMemcpy(tmp, local.data(), lcount * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess && p.format == kQ4)
     e = cudaMemset(p.values, 0, (size_t)param_value_bytes(p.rows, p.cols, p.format));
   if (e == cudaSuccess) {
     int64_t work = (int64_t)p.rows * ((p.cols + kQBlock - 1) / kQBlock);
     int blocks = (int)std::min<int64_t>((work + 255) / 256, 148 * 32);
-    k_init_param<<<blocks, 256, 0, 0>>>(p, 0, 0, 0.0, 0, tmp);
+    k_init_param<<<blocks, 256, 0, 0>>>(p, 0, 0, 0.0, 0, tmp, 0, 0, p.cols);
     e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
   }
@@ -637,6 +777,23 @@ static void launch_attention_exact(sr_model* m, sr_kvpool* pool, int n, int max_
   sr_count_launch(m);
 }
 
+// X += T after summing every rank's partial T over NCCL (the exchange after
+// o_proj and down_proj of the tensor-parallel step).
+__global__ void k_add_inplace(float* __restrict__ X, const float* __restrict__ T, int64_t count) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
+    X[i] += T[i];
+}
+static int tp_allreduce_add(sr_model* m, int n) {
+  nccl::Api& api = nccl::api();
+  const int64_t count = (int64_t)n * m->dm.dim;
+  const int r = api.AllReduce(m->T, m->T, (size_t)count, nccl::kFloat32, nccl::kSum, (nccl::Comm)m->nccl_comm,
+                              m->stream);
+  if (r != nccl::kSuccess) return sr_fail(SR_EDEVICE, std::string("ncclAllReduce: ") + api.GetErrorString(r));
+  k_add_inplace<<<(int)std::min<int64_t>((count + 255) / 256, 148 * 8), 256, 0, m->stream>>>(m->X, m->T, count);
+  sr_count_launch(m);
+  return SR_OK;
+}
+
 int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel,
                     const StepScratch* scratch) {
   const ModelDims& dm = m->dm;
@@ -653,6 +810,8 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   // Tensor-core projections: every producer writes the next projection's bf16
   // hi/lo operand planes directly (no fp32 round trip, no split kernel).
   const bool tc = fast && tc_active(m, n);
+  const bool tp = dm.tp_size > 1;
+  int rc = SR_OK;
   __nv_bfloat16* xh = tc ? tc_xh(m) : nullptr;
   __nv_bfloat16* xl = tc ? tc_xl(m) : nullptr;
   for (int l = 0; l < L; l++) {
@@ -675,7 +834,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_qkv(m, l, n, true));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) {
-      o.y = m->Q; o.ldy = d; o.bias = B ? (const float*)B[0].values : nullptr;
+      o.y = m->Q; o.ldy = dm.qd; o.bias = B ? (const float*)B[0].values : nullptr;
       sr_launch_linear(m, m->N, n, P[1], o);
       o.y = m->K; o.ldy = kd; o.bias = B ? (const float*)B[1].values : nullptr;
       sr_launch_linear(m, m->N, n, P[2], o);
@@ -690,10 +849,15 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
               if (fixed_scratch) fast_attention_run(m, pool->data, n, info.max_len, l, scratch->part_o, scratch->part_ml);
               else if (fast) a_split = fast_attention(m, pool, n, info.max_len, l, xh, xl);
               else launch_attention_exact(m, pool, n, info.max_len, l));
-    o.y = m->X; o.ldy = d; o.bias = nullptr; o.resid = m->X;
-    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_o(m, l, n, a_split));
+    // O projection: X += O(a); a tensor-parallel rank writes its partial sum to
+    // T, which the ranks all-reduce before the residual add.
+    float* oy = tp ? m->T : m->X;
+    const float* ores = tp ? nullptr : m->X;
+    o.y = oy; o.ldy = d; o.bias = nullptr; o.resid = ores;
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_o(m, l, n, a_split, oy, ores));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->A, n, P[4], o);
+    if (tp && (rc = tp_allreduce_add(m, n)) != SR_OK) return rc;
     SR_LAUNCH(m, SR_PROF_NORM,
               if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps, xh, xl);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps));
@@ -712,10 +876,11 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
               if (tc) k_swiglu_split<<<sw_blocks, 256, 0, s>>>(m->G, m->U, xh, xl, cnt);
               else k_swiglu_exact<<<sw_blocks, 256, 0, s>>>(m->G, m->U, m->H, cnt));
     sr_count_launch(m);
-    o.y = m->X; o.ldy = d; o.resid = m->X;
-    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_down(m, l, n, true));
+    o.y = oy; o.ldy = d; o.resid = ores;
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_down(m, l, n, true, oy, ores));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->H, n, P[8], o);
+    if (tp && (rc = tp_allreduce_add(m, n)) != SR_OK) return rc;
   }
   // Selected head (M:6420-6448): gather last rows, final norm, LM head into
   // the session's logits row; unselected rows are zero.
@@ -1009,6 +1174,8 @@ extern "C" int sr_step_noalloc(sr_model* m, sr_kvpool* pool, const sr_batch* bat
   if (rc != SR_OK) return rc;
   if (!fast_attention_supported(m->dm))
     return sr_fail(SR_EUNSUPPORTED, "the allocation-free step needs head_dim 64 or 128 and at most 8 query heads per KV head");
+  if (m->dm.tp_size > 1)
+    return sr_fail(SR_EUNSUPPORTED, "the allocation-free step runs on single-GPU models (NCCL may allocate)");
   size_t items = 0;
   const size_t floats = fa_scratch_floats(m->dm, info.rows, info.max_len, &items);
   if (floats * sizeof(float) > kNoAllocScratchBytes)

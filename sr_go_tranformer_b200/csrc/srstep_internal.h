@@ -52,8 +52,16 @@ struct Profiler {
   int64_t steps = 0;
 };
 
+// Where this device's copy of a parameter sits in the full tensor (tensor
+// parallelism shards Q/K/V/gate/up by rows and O/down/qkv-bias by columns).
+struct Shard {
+  int32_t full_rows, full_cols, row0, col0;
+};
+
 struct sr_model {
   sr_model_desc d;
+  std::vector<Shard> shards;  // parallel to params
+  void* nccl_comm = nullptr;
   int device = 0;
   int mode = SR_MODE_EXACT;
   sr::ModelDims dm;
@@ -86,6 +94,9 @@ struct sr_kvpool {
 };
 
 int sr_fail(int code, const std::string& msg);
+// Parameter table (hfProfileSpecs order) of one tensor-parallel rank.
+int sr_param_table(const sr_model_desc& c, int rank, int size, std::vector<sr::Param>* params,
+                   std::vector<Shard>* shards);
 
 // Every kernel launch of a step increments this counter (the benchmark's
 // gpu_launches); class scopes below may cover several launches.

@@ -58,13 +58,33 @@ def make_desc(vocab, dim, hidden, layers, heads, kv_heads, context, rope_theta=1
     return d
 
 
-class Model:
-    """A device model (weights, RoPE tables, workspace) on one GPU."""
+def tp_unique_id():
+    """128-byte NCCL id (rank 0) for Model(..., tp_rank, tp_size, nccl_id)."""
+    buf = (C.c_char * 128)()
+    A.check(A.lib().sr_tp_unique_id(buf))
+    return bytes(buf)
 
-    def __init__(self, desc, device=0):
+
+def tp_shard(desc, rank, size, index):
+    """(row0, rows, col0, cols) of parameter `index` held by rank `rank` of `size`."""
+    out = np.zeros(4, dtype=np.int32)
+    A.check(A.lib().sr_tp_shard(C.byref(desc), rank, size, index, _p(out)))
+    return tuple(int(x) for x in out)
+
+
+class Model:
+    """A device model (weights, RoPE tables, workspace) on one GPU, or one
+    tensor-parallel rank of it (tp_size > 1, nccl_id from tp_unique_id)."""
+
+    def __init__(self, desc, device=0, tp_rank=0, tp_size=1, nccl_id=None):
         self.desc = desc
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         h = C.c_void_p()
-        A.check(A.lib().sr_model_create(C.byref(desc), device, C.byref(h)))
+        if tp_size > 1:
+            idbuf = C.create_string_buffer(bytes(nccl_id), 128)
+            A.check(A.lib().sr_model_create_tp(C.byref(desc), device, tp_rank, tp_size, idbuf, C.byref(h)))
+        else:
+            A.check(A.lib().sr_model_create(C.byref(desc), device, C.byref(h)))
         self.h = h
         n = C.c_int32()
         A.check(A.lib().sr_model_param_count(self.h, C.byref(n)))
@@ -91,7 +111,8 @@ class Model:
 
     @property
     def kv_dim(self):
-        return self.desc.dim // self.desc.heads * self.desc.kv_heads
+        """KV width held on this device (this rank's KV heads)."""
+        return self.desc.dim // self.desc.heads * (self.desc.kv_heads // self.tp_size)
 
     @property
     def page_elements(self):
