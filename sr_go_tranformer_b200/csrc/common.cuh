@@ -9,6 +9,7 @@ namespace sr {
 constexpr int kQBlock = 64;          // q8Block: 64 columns per scale (monolith.go:3793)
 constexpr int kMaxRows = 1024;       // rows per step (monolith.go:6275)
 constexpr int kMaxSessions = 256;    // sessions per step (monolith.go:6248)
+constexpr int kAttnSplit = 256;      // positions per split-K attention item (fast mode)
 
 enum ParamFormat { kF32 = 0, kQ8 = 1, kQ4 = 2 };
 
@@ -47,6 +48,8 @@ struct StepMeta {
   int32_t* head_src;    // [sessions] compact head row -> step row
   int32_t* head_dst;    // [sessions] compact head row -> session index
   int32_t* n_heads;     // [1]
+  int32_t* row_item0;   // [rows] first attention item of the row
+  int32_t* item_rs;     // [items] attention item -> (row << 16) | split
 };
 
 // Per-device model dimensions.  With tensor parallelism, heads, kv_heads,

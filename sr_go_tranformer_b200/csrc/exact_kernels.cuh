@@ -15,16 +15,48 @@ namespace sr {
 
 // ---------------------------------------------------------------- metadata --
 // Ragged-batch metadata (M:6361-6375, 6420-6427): per row the session position
-// and page-table base; per selected session its last row (compacted head).
-__global__ void k_meta(StepMeta m, int sessions, int rows) {
-  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+// and page-table base; per selected session its last row (compacted head); and
+// the compact list of (row, 256-position split) items that the fast-mode
+// attention launches one CTA per KV head for.
+__global__ void __launch_bounds__(1024) k_meta(StepMeta m, int sessions, int rows) {
+  __shared__ int warp_sum[32];
+  const int r = threadIdx.x;  // rows <= 1024 = blockDim.x: one row per thread
+  int ns = 0;
+  if (r < rows) {
     int lo = 0, hi = sessions - 1;
     while (lo < hi) {
       int mid = (lo + hi + 1) >> 1;
       if (m.tok_off[mid] <= r) lo = mid; else hi = mid - 1;
     }
-    m.row_pos[r] = m.sess_pos[lo] + (r - m.tok_off[lo]);
+    const int pos = m.sess_pos[lo] + (r - m.tok_off[lo]);
+    m.row_pos[r] = pos;
     m.row_pbase[r] = m.page_off[lo];
+    ns = (pos + 1 + kAttnSplit - 1) / kAttnSplit;
+  }
+  // exclusive scan of the rows' attention item counts
+  const int lane = r & 31, warp = r >> 5;
+  int incl = ns;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += v;
+  }
+  if (lane == 31) warp_sum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_sum[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += v;
+    }
+    warp_sum[lane] = w;  // inclusive totals of warps 0..lane
+  }
+  __syncthreads();
+  const int base = incl - ns + (warp > 0 ? warp_sum[warp - 1] : 0);
+  if (r < rows) {
+    m.row_item0[r] = base;
+    for (int s = 0; s < ns; s++) m.item_rs[base + s] = (r << 16) | s;
   }
   if (threadIdx.x == 0) {
     int h = 0;

@@ -2,7 +2,8 @@
 //
 // Same mathematics as attend (cmd/monolith/monolith.go:5293-5352), reordered
 // for the B200.  Every (row, KV head) context is cut into splits of kFaSplit
-// positions, one CTA per split; the `group` query heads that share a KV head
+// positions, one CTA per split (grid: the step's compact (row, split) item list
+// built by k_meta x KV heads, so no CTA is launched past a row's context); the `group` query heads that share a KV head
 // read each K/V element once (GQA), keep an online softmax (running max,
 // rescaled sum and output) and write the split's (O, m, l); a combine kernel
 // merges the splits with their log-sum-exp weights.  Results match the exact
@@ -24,7 +25,7 @@
 namespace sr {
 
 constexpr int kFaThreads = 128;
-constexpr int kFaSplit = 256;  // positions per CTA
+constexpr int kFaSplit = kAttnSplit;  // positions per CTA
 
 struct FastAttnArgs {
   const float* Q;
@@ -34,9 +35,8 @@ struct FastAttnArgs {
   ModelDims dm;
   int layer;
   float scale;
-  int max_splits;
-  float* part_o;   // [items][group][hd]
-  float* part_ml;  // [items][group][2]
+  float* part_o;   // [items][kv_heads][group][hd]
+  float* part_ml;  // [items][kv_heads][group][2]
   __nv_bfloat16* xh;  // optional: write the output as bf16 hi/lo planes (the
   __nv_bfloat16* xl;  // next projection's tensor-core operand) instead of fp32 A
 };
@@ -58,9 +58,9 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
-__device__ __forceinline__ void fa_write_split(const FastAttnArgs& a, int r, int kh, int split, int G, int HD,
+__device__ __forceinline__ void fa_write_split(const FastAttnArgs& a, int item_idx, int kh, int G, int HD,
                                                const float* o_smem, const float* ml_smem) {
-  const int64_t item = ((int64_t)r * a.dm.kv_heads + kh) * a.max_splits + split;
+  const int64_t item = (int64_t)item_idx * a.dm.kv_heads + kh;
   for (int idx = threadIdx.x; idx < G * HD; idx += kFaThreads) a.part_o[item * G * HD + idx] = o_smem[idx];
   if (threadIdx.x < 2 * G) a.part_ml[item * G * 2 + threadIdx.x] = ml_smem[threadIdx.x];
 }
@@ -85,7 +85,8 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
   constexpr int HD = 128, MT = kWpMT, GP = WarpSmem<G>::GP;
   constexpr int ROUNDS = (G + 3) / 4;  // softmax passes: 4 heads x 8 positions per pass
   extern __shared__ __align__(16) float fsm[];
-  const int split = blockIdx.x, r = blockIdx.y, kh = blockIdx.z;
+  const int rs = a.meta.item_rs[blockIdx.x], kh = blockIdx.y;
+  const int r = rs >> 16, split = rs & 0xffff;
   const int L = a.meta.row_pos[r] + 1;
   const int s0 = split * kFaSplit;
   if (s0 >= L) return;
@@ -104,16 +105,26 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
   const int nw = max(0, ws1 - ws0);
   const int ntiles = (nw + MT - 1) / MT;
 
+  // The warp's page ids, one per lane (when its sub-split spans <= 32 pages),
+  // so the tile loader never waits on a dependent global load.
+  const int pg0 = ws0 / pt;
+  const int npg = nw > 0 ? (ws1 - 1) / pt - pg0 + 1 : 0;
+  const bool page_regs = npg <= 32;
+  const int my_page = (page_regs && lane < npg) ? a.meta.page_ids[pbase + pg0 + lane] : 0;
   // lane copies 16-byte chunk `lane` of each K and V row of a tile
   auto load_tile = [&](int t) {
     float* dst = kv + (t & 1) * 2 * MT * HD;
     const int t0 = ws0 + t * MT, tn = min(MT, ws1 - t0);
+    int pi = t0 / pt, po = t0 - pi * pt;  // page index and offset of position t0
     for (int s = 0; s < tn; s++) {
-      const int pos = t0 + s;
-      const int64_t page = a.meta.page_ids[pbase + pos / pt];
-      const float* krow = a.pool + page * a.dm.page_elems + lay + (int64_t)(pos % pt) * a.dm.kvd + 4 * lane;
+      const int64_t page = page_regs ? __shfl_sync(0xffffffffu, my_page, pi - pg0) : a.meta.page_ids[pbase + pi];
+      const float* krow = a.pool + page * a.dm.page_elems + lay + (int64_t)po * a.dm.kvd + 4 * lane;
       cp_async16(dst + s * HD + 4 * lane, krow);
       cp_async16(dst + (MT + s) * HD + 4 * lane, krow + vofs);
+      if (++po == pt) {
+        po = 0;
+        pi++;
+      }
     }
   };
   if (ntiles > 0) load_tile(0);
@@ -272,7 +283,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
     }
   }
   __syncthreads();
-  fa_write_split(a, r, kh, split, G, HD, out, out + G * HD);
+  fa_write_split(a, blockIdx.x, kh, G, HD, out, out + G * HD);
 }
 
 // ====================================================== head_dim 64: per CTA
@@ -309,7 +320,8 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_tile(FastAttnArgs a) {
   float* l_s = m_s + GP;                    // [GP]
   float* red = fsm;                         // reuses the tiles after the loop
 
-  const int split = blockIdx.x, r = blockIdx.y, kh = blockIdx.z;
+  const int rs = a.meta.item_rs[blockIdx.x], kh = blockIdx.y;
+  const int r = rs >> 16, split = rs & 0xffff;
   const int L = a.meta.row_pos[r] + 1;
   const int s0 = split * kFaSplit;
   if (s0 >= L) return;
@@ -425,7 +437,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_tile(FastAttnArgs a) {
   }
   if (tid < 2 * G) out[G * HD + tid] = ml[tid];
   __syncthreads();
-  fa_write_split(a, r, kh, split, G, HD, out, out + G * HD);
+  fa_write_split(a, blockIdx.x, kh, G, HD, out, out + G * HD);
 }
 
 // Merge the splits of each (row, query head) and write the attention output.
@@ -435,15 +447,17 @@ __global__ void __launch_bounds__(HD) k_attn_combine(FastAttnArgs a) {
   const int G = a.dm.group, kh = h / G, g = h % G;
   const int L = a.meta.row_pos[r] + 1;
   const int ns = (L + kFaSplit - 1) / kFaSplit;
-  const int64_t base = ((int64_t)r * a.dm.kv_heads + kh) * a.max_splits;
+  const int KVH = a.dm.kv_heads;
+  const int64_t base = (int64_t)a.meta.row_item0[r] * KVH + kh;  // split s is unit base + s*KVH
   float M = -INFINITY;
-  for (int s = 0; s < ns; s++) M = fmaxf(M, a.part_ml[((base + s) * G + g) * 2]);
+  for (int s = 0; s < ns; s++) M = fmaxf(M, a.part_ml[((base + (int64_t)s * KVH) * G + g) * 2]);
   float den = 0.f, num = 0.f;
   for (int s = 0; s < ns; s++) {
-    const float ms = a.part_ml[((base + s) * G + g) * 2];
+    const int64_t u = base + (int64_t)s * KVH;
+    const float ms = a.part_ml[(u * G + g) * 2];
     const float w = (ms == -INFINITY) ? 0.f : __expf(ms - M);
-    den += w * a.part_ml[((base + s) * G + g) * 2 + 1];
-    num += w * a.part_o[((base + s) * G + g) * HD + d];
+    den += w * a.part_ml[(u * G + g) * 2 + 1];
+    num += w * a.part_o[(u * G + g) * HD + d];
   }
   const int64_t o = (int64_t)r * a.dm.qd + (int64_t)h * HD + d;
   if (a.xh)

@@ -1,6 +1,6 @@
 // fast_gemm.cuh -- host side of the tensor-core projections (tc_gemm.cuh):
 // bf16 code shadows of every Q8/Q4 matrix (Q|K|V and gate|up fused row-wise),
-// TMA descriptors, split-K selection and the per-layer entry points.
+// TMA descriptors, the stream-K schedule and the per-layer entry points.
 #pragma once
 
 #include <cuda.h>
@@ -30,8 +30,8 @@ struct TcState {
   __nv_bfloat16* xh = nullptr;
   __nv_bfloat16* xl = nullptr;
   CUtensorMap xh_d, xl_d, xh_h, xl_h, xh_q, xl_q;  // operand maps for in = dim, hidden, attention width
-  float* partial = nullptr;
-  size_t partial_cap = 0;
+  float* partial = nullptr;   // [sms][2][kN][kMC] stream-K partial tiles
+  int sms = 148;
   int* err = nullptr;
   int* h_err = nullptr;
   bool ran = false;
@@ -80,7 +80,6 @@ inline void tc_free(TcState* t) {
   t->gateup.clear();
   t->down.clear();
   t->partial = nullptr;
-  t->partial_cap = 0;
 }
 
 inline bool tc_alloc(TcState* t, void** p, size_t bytes) {
@@ -162,8 +161,17 @@ inline bool tc_prepare(sr_model* m) {
     return false;
   }
   const int xcols = std::max(std::max(dm.dim, dm.hidden), dm.qd);
+  {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device) != cudaSuccess || sms < 1) {
+      cudaGetLastError();
+      sms = 148;
+    }
+    t->sms = sms;
+  }
   if (!tc_alloc(t, (void**)&t->xh, (size_t)kMaxRows * xcols * 2) ||
-      !tc_alloc(t, (void**)&t->xl, (size_t)kMaxRows * xcols * 2) || !tc_alloc(t, (void**)&t->err, 16)) {
+      !tc_alloc(t, (void**)&t->xl, (size_t)kMaxRows * xcols * 2) || !tc_alloc(t, (void**)&t->err, 16) ||
+      !tc_alloc(t, (void**)&t->partial, (size_t)t->sms * 2 * tc::kN * tc::kMC * 4)) {
     tc_free(t);
     return false;
   }
@@ -203,6 +211,9 @@ inline void tc_split_x(sr_model* m, const float* X, int n, int in) {
 }
 
 // in_kind: 0 = the residual width (dim), 1 = hidden, 2 = the attention width (qd).
+// Stream-K schedule: groups of nt CTAs (one per 128-row tile) fill the SMs,
+// each group taking at least kSkMinUnits (tile, block) units.
+constexpr int kSkMinUnits = 4;
 inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::GemmArgs a) {
   TcState* t = tc_state(m);
   a.n = n;
@@ -211,51 +222,23 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::Gemm
   a.groups = (W.cols + kQBlock - 1) / kQBlock;
   a.scales = W.scales;
   a.err = t->err;
-  const int mt = (W.rows + tc::kMC - 1) / tc::kMC, nt = (n + tc::kN - 1) / tc::kN;
-  const int tiles = mt * nt;
-  // Split K so the CTAs fill whole waves of 148 SMs (one CTA per SM), with at
-  // least 4 K-blocks per split; prefer fewer splits on ties.
-  int splits = 1, kbps = a.groups;
-  double best = -1.0;
-  for (int s = 1; s <= 16; s++) {
-    const int kb = (a.groups + s - 1) / s;
-    if (s > 1 && kb < 4) break;
-    const int ss = (a.groups + kb - 1) / kb;
-    if ((size_t)ss * n * W.rows * 4 > ((size_t)512 << 20)) break;
-    const int ctas = tiles * ss;
-    const int waves = (ctas + 147) / 148;
-    const double eff = (double)ctas / (waves * 148.0) - 0.02 * (ss - 1);
-    if (eff > best + 1e-9) {
-      best = eff;
-      splits = ss;
-      kbps = kb;
-    }
-  }
-  a.kb_per_split = kbps;
-  a.splits = splits;
-  if (splits > 1) {
-    const size_t need = (size_t)splits * n * W.rows * 4;
-    if (need > t->partial_cap) {
-      if (t->partial) {
-        cudaFree(t->partial);
-        t->allocs.erase(std::find(t->allocs.begin(), t->allocs.end(), (void*)t->partial));
-      }
-      t->partial = nullptr;
-      t->partial_cap = 0;
-      if (!tc_alloc(t, (void**)&t->partial, need)) return false;
-      t->partial_cap = need;
-    }
-    a.partial = t->partial;
-  } else {
-    a.partial = nullptr;
-  }
+  a.mt = (W.rows + tc::kMC - 1) / tc::kMC;
+  a.nt = (n + tc::kN - 1) / tc::kN;
+  if (a.nt > t->sms) return false;
+  const int64_t units = (int64_t)a.mt * a.groups;
+  a.ngroups = (int)std::max<int64_t>(1, std::min<int64_t>(t->sms / a.nt, (units + kSkMinUnits - 1) / kSkMinUnits));
+  a.partial = t->partial;
   const CUtensorMap& xh = in_kind == 1 ? t->xh_h : (in_kind == 2 ? t->xh_q : t->xh_d);
   const CUtensorMap& xl = in_kind == 1 ? t->xl_h : (in_kind == 2 ? t->xl_q : t->xl_d);
-  tc::k_gemm_q<<<dim3(nt, mt, splits), tc::kThreads, tc::kSmemBytes, m->stream>>>(W.map, xh, xl, a);
+  tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, m->stream>>>(W.map, xh, xl, a);
   sr_count_launch(m);
-  if (splits > 1) {
-    const int64_t total = (int64_t)n * W.rows;
-    tc::k_gemm_reduce<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, m->stream>>>(a);
+  bool split = a.out_map != nullptr;  // tiles left in partial slots?
+  for (int sg = 0; sg < a.nseg; sg++) split = split || a.seg[sg].resid != nullptr;
+  for (int mi = 0; mi < a.mt && !split; mi++)
+    split = tc::sk_group_of(mi * a.groups, (int)units, a.ngroups) !=
+            tc::sk_group_of(mi * a.groups + a.groups - 1, (int)units, a.ngroups);
+  if (split) {
+    tc::k_sk_reduce<<<dim3(a.mt * a.nt, tc::kN / 32), tc::kMC, 0, m->stream>>>(a);
     sr_count_launch(m);
   }
   t->ran = true;

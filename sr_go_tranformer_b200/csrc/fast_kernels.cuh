@@ -101,9 +101,9 @@ __global__ void k_swiglu_split(const float* __restrict__ G, const float* __restr
 
 // ---------------------------------------------------------------- attention --
 template <int HD, int G>
-inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n) {
+inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n, int items) {
   const size_t smem = fa_smem_bytes<HD, G>();
-  const dim3 grid(a.max_splits, n, a.dm.kv_heads);
+  const dim3 grid(items, a.dm.kv_heads);
   if constexpr (HD == 128) {
     cudaFuncSetAttribute(k_attn_warp128<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k_attn_warp128<G><<<grid, kFaThreads, smem, m->stream>>>(a);
@@ -117,16 +117,16 @@ inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n) {
 }
 
 template <int HD>
-inline bool fa_dispatch_g(sr_model* m, const FastAttnArgs& a, int n) {
+inline bool fa_dispatch_g(sr_model* m, const FastAttnArgs& a, int n, int items) {
   switch (a.dm.group) {
-    case 1: return fa_launch<HD, 1>(m, a, n);
-    case 2: return fa_launch<HD, 2>(m, a, n);
-    case 3: return fa_launch<HD, 3>(m, a, n);
-    case 4: return fa_launch<HD, 4>(m, a, n);
-    case 5: return fa_launch<HD, 5>(m, a, n);
-    case 6: return fa_launch<HD, 6>(m, a, n);
-    case 7: return fa_launch<HD, 7>(m, a, n);
-    case 8: return fa_launch<HD, 8>(m, a, n);
+    case 1: return fa_launch<HD, 1>(m, a, n, items);
+    case 2: return fa_launch<HD, 2>(m, a, n, items);
+    case 3: return fa_launch<HD, 3>(m, a, n, items);
+    case 4: return fa_launch<HD, 4>(m, a, n, items);
+    case 5: return fa_launch<HD, 5>(m, a, n, items);
+    case 6: return fa_launch<HD, 6>(m, a, n, items);
+    case 7: return fa_launch<HD, 7>(m, a, n, items);
+    case 8: return fa_launch<HD, 8>(m, a, n, items);
     default: return false;
   }
 }
@@ -135,17 +135,17 @@ inline bool fa_dispatch_g(sr_model* m, const FastAttnArgs& a, int n) {
 inline bool fast_attention_supported(const ModelDims& dm) {
   return (dm.hd == 64 || dm.hd == 128) && dm.group <= 8;
 }
-inline int fa_max_splits(int max_len) { return (max_len + kFaSplit - 1) / kFaSplit; }
-// Scratch floats the split-K attention needs for n rows (partial O, then (m, l)).
-inline size_t fa_scratch_floats(const ModelDims& dm, int n, int max_len, size_t* items_out = nullptr) {
-  const size_t items = (size_t)n * dm.kv_heads * fa_max_splits(max_len);
-  if (items_out) *items_out = items;
-  return items * dm.group * (dm.hd + 2);
+// Scratch floats the split-K attention needs for a step's (row, split) items
+// (partial O, then (m, l)); *units_out = items x KV heads.
+inline size_t fa_scratch_floats(const ModelDims& dm, int items, size_t* units_out = nullptr) {
+  const size_t units = (size_t)items * dm.kv_heads;
+  if (units_out) *units_out = units;
+  return units * dm.group * (dm.hd + 2);
 }
 
 // Launch split + combine with caller-provided scratch (no allocation).  With
 // xh/xl set, the combine writes bf16 hi/lo operand planes instead of fp32 A.
-inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, int max_len, int layer, float* part_o,
+inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, int items, int layer, float* part_o,
                                float* part_ml, __nv_bfloat16* xh = nullptr, __nv_bfloat16* xl = nullptr) {
   const ModelDims& dm = m->dm;
   FastAttnArgs a;
@@ -156,23 +156,22 @@ inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, int m
   a.dm = dm;
   a.layer = layer;
   a.scale = (float)(1.0 / std::sqrt((double)dm.hd));
-  a.max_splits = fa_max_splits(max_len);
   a.part_o = part_o;
   a.part_ml = part_ml;
   a.xh = xh;
   a.xl = xl;
-  return dm.hd == 128 ? fa_dispatch_g<128>(m, a, n) : fa_dispatch_g<64>(m, a, n);
+  return dm.hd == 128 ? fa_dispatch_g<128>(m, a, n, items) : fa_dispatch_g<64>(m, a, n, items);
 }
 
 // Returns false (exact kernel runs instead) for unsupported shapes or when the
 // split scratch would exceed its cap.  The scratch grows on demand.
-inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int max_len, int layer,
+inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int row_items, int layer,
                                __nv_bfloat16* xh = nullptr, __nv_bfloat16* xl = nullptr) {
   const ModelDims& dm = m->dm;
   if (!fast_attention_supported(dm)) return false;
   FastState* st = fast_state(m);
   size_t items = 0;
-  fa_scratch_floats(dm, n, max_len, &items);
+  fa_scratch_floats(dm, row_items, &items);
   const size_t o_bytes = items * dm.group * dm.hd * 4;
   if (o_bytes > ((size_t)1 << 30)) return false;
   if (items > st->items_cap) {
@@ -189,7 +188,7 @@ inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int m
     }
     st->items_cap = items;
   }
-  return fast_attention_run(m, pool_data, n, max_len, layer, st->part_o, st->part_ml, xh, xl);
+  return fast_attention_run(m, pool_data, n, row_items, layer, st->part_o, st->part_ml, xh, xl);
 }
 
 // ------------------------------------------------------------------- linear --

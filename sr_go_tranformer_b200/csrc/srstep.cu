@@ -320,7 +320,10 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
   m->max_pages_per_session = (c.context + c.page_tokens - 1) / c.page_tokens;
   m->page_cap = (int64_t)kMaxSessions * m->max_pages_per_session;
   m->upload_ints = kMetaHeader + m->page_cap;
-  const int64_t meta_ints = m->upload_ints + kMetaComputed;
+  // computed region: per-row data, head maps, then the attention item table
+  // (at most ceil(context / 256) items for each of the 1024 rows)
+  const int64_t item_cap = (int64_t)kMaxRows * ((c.context + kAttnSplit - 1) / kAttnSplit);
+  const int64_t meta_ints = m->upload_ints + kMetaComputed + kMaxRows + item_cap;
   if ((rc = sr_model_alloc(m, (void**)&m->meta_dev, (size_t)meta_ints * 4)) != SR_OK) { free_model(m); return rc; }
   if (cudaMallocHost(&m->h_stage, (size_t)(m->upload_ints * 4 + kSampleStageBytes)) != cudaSuccess) {
     cudaGetLastError();
@@ -342,6 +345,8 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
     s.head_src = cbase + 2 * kMaxRows;
     s.head_dst = cbase + 2 * kMaxRows + kMaxSessions;
     s.n_heads = cbase + 2 * kMaxRows + 2 * kMaxSessions;
+    s.row_item0 = cbase + kMetaComputed;
+    s.item_rs = cbase + kMetaComputed + kMaxRows;
   }
   // Sampler device buffers.
   {
@@ -650,7 +655,7 @@ int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* 
     return sr_fail(SR_EINVAL, "null batch array");
   if (b->token_offsets[0] != 0 || b->page_offsets[0] != 0) return sr_fail(SR_EINVAL, "offsets must start at 0");
   const int pt = c.page_tokens;
-  int64_t n = 0, max_end = 0, heads = 0;
+  int64_t n = 0, max_end = 0, heads = 0, items = 0;
   for (int i = 0; i < S; i++) {
     int64_t len = (int64_t)b->token_offsets[i + 1] - b->token_offsets[i];
     if (len < 1 || len > kMaxRows - n)
@@ -665,6 +670,7 @@ int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* 
     if (np < need || np > m->max_pages_per_session) return sr_fail(SR_EINVAL, "invalid KV page coverage");
     for (int64_t j = b->page_offsets[i]; j < b->page_offsets[i + 1]; j++)
       if (b->page_ids[j] < 0 || b->page_ids[j] >= pool->num_pages) return sr_fail(SR_EINVAL, "invalid KV page id");
+    for (int64_t L = pos + 1; L <= pos + len; L++) items += (L + kAttnSplit - 1) / kAttnSplit;
     n += len;
     max_end = std::max(max_end, pos + len);
     heads += (!b->want_logits || b->want_logits[i]) ? 1 : 0;
@@ -707,6 +713,7 @@ int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* 
   info->max_len = (int)max_end;
   info->heads = (int)heads;
   info->pages = b->page_offsets[S];
+  info->attn_items = (int)items;
   return SR_OK;
 }
 
@@ -749,8 +756,8 @@ static void launch_linear_exact(sr_model* m, const float* X, int n, const Param&
     else k_linear_q_exact<kQ4, 64, 8><<<grid(64, 8), 256, 0, s>>>(X, n, in, out, W, O);
   }
 }
-static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer, __nv_bfloat16* xh,
-                           __nv_bfloat16* xl);
+static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, const BatchInfo& info, int layer,
+                           __nv_bfloat16* xh, __nv_bfloat16* xl);
 void sr_launch_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O, int cls = SR_PROF_LINEAR) {
   ProfScope ps(m, cls);
   if (m->mode == SR_MODE_FAST && fast_linear(m, X, n, W, O)) return;
@@ -846,8 +853,8 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     sr_count_launch(m, 3);  // two norms and RoPE/KV of this layer
     bool a_split = false;   // attention wrote the O projection's operand planes
     SR_LAUNCH(m, SR_PROF_ATTENTION,
-              if (fixed_scratch) fast_attention_run(m, pool->data, n, info.max_len, l, scratch->part_o, scratch->part_ml);
-              else if (fast) a_split = fast_attention(m, pool, n, info.max_len, l, xh, xl);
+              if (fixed_scratch) fast_attention_run(m, pool->data, n, info.attn_items, l, scratch->part_o, scratch->part_ml);
+              else if (fast) a_split = fast_attention(m, pool, n, info, l, xh, xl);
               else launch_attention_exact(m, pool, n, info.max_len, l));
     // O projection: X += O(a); a tensor-parallel rank writes its partial sum to
     // T, which the ranks all-reduce before the residual add.
@@ -1051,14 +1058,15 @@ extern "C" int sr_step_sample(sr_model* m, sr_kvpool* pool, const sr_batch* batc
 
 // Fast-mode attention: split-K kernels when the shape is covered (returns true
 // when they also wrote xh/xl, if given), else the exact kernel into fp32 A.
-static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, int max_len, int layer, __nv_bfloat16* xh,
-                           __nv_bfloat16* xl) {
-  if (fast_attention_try(m, pool->data, n, max_len, layer, xh, xl)) return xh != nullptr;
-  launch_attention_exact(m, pool, n, max_len, layer);
+static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, const BatchInfo& info, int layer,
+                           __nv_bfloat16* xh, __nv_bfloat16* xl) {
+  if (fast_attention_try(m, pool->data, n, info.attn_items, layer, xh, xl)) return xh != nullptr;
+  launch_attention_exact(m, pool, n, info.max_len, layer);
   return false;
 }
 
-// Fast-mode projections (tensor-core GEMM) are not built yet: exact kernels run.
+// Per-call fast projection hook.  The step's fast projections go through the
+// tensor-core path (fast_gemm.cuh) directly; other callers use the exact kernels.
 bool sr::fast_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O) {
   (void)m, (void)X, (void)n, (void)W, (void)O;
   return false;
@@ -1177,7 +1185,7 @@ extern "C" int sr_step_noalloc(sr_model* m, sr_kvpool* pool, const sr_batch* bat
   if (m->dm.tp_size > 1)
     return sr_fail(SR_EUNSUPPORTED, "the allocation-free step runs on single-GPU models (NCCL may allocate)");
   size_t items = 0;
-  const size_t floats = fa_scratch_floats(m->dm, info.rows, info.max_len, &items);
+  const size_t floats = fa_scratch_floats(m->dm, info.attn_items, &items);
   if (floats * sizeof(float) > kNoAllocScratchBytes)
     return sr_fail(SR_EINVAL, "batch needs " + std::to_string(floats * sizeof(float)) +
                                   " bytes of attention scratch; the allocation-free step holds " +

@@ -10,10 +10,18 @@
 //     step rows, so a thread of the epilogue owns one output feature and its
 //     per-block scale (the reference's s += p*scale) is a scalar FMA on
 //     registers after each block's accumulator is read from TMEM;
-//   * a CTA owns 256 output features as two M=128 MMA halves that share each
-//     activation tile; TMA (SWIZZLE_128B) feeds a 3-stage mbarrier pipeline of
-//     64 KiB stages; one thread issues MMAs; TMEM holds two accumulator buffers
-//     so block b+1's MMAs overlap block b's epilogue.
+//   * a CTA computes 256 output features (two M=128 MMA halves sharing each
+//     activation tile) for one 128-row tile of the step; TMA (SWIZZLE_128B)
+//     feeds a 3-stage mbarrier pipeline of 64 KiB stages; one thread issues
+//     MMAs; TMEM holds two accumulator buffers so block b+1's MMAs overlap
+//     block b's epilogue;
+//   * persistent stream-K schedule: the (256-feature tile, 64-column block)
+//     units of the matrix are cut into one contiguous range per group of CTAs
+//     (a group holds one CTA per 128-row tile, so the CTAs that read the same
+//     weight tile run together and share it in L2); the pipeline runs through
+//     tile boundaries without refilling.  A tile whose blocks span several
+//     groups leaves one partial sum per group, and k_sk_reduce adds them in
+//     block order (deterministic) and applies the epilogue.
 // Every mbarrier wait is bounded (globaltimer); on expiry the kernel records an
 // error flag, stops waiting and finishes, and the host reports SR_ETIMEOUT.
 #pragma once
@@ -33,12 +41,14 @@ constexpr int kN = 128;          // step rows per tile (MMA N)
 constexpr int kKB = 64;          // K per block (one scale block, one 128-byte bf16 row)
 constexpr int kStages = 3;
 constexpr int kAcc = 2;          // TMEM accumulator buffers, each kMH*kN columns (512 in all)
+static_assert(kAcc == 2, "the epilogue indexes TMEM buffers as i & 1");
 constexpr int kThreads = 320;    // warp 0: TMA, warp 1: MMA, warps 2-9: epilogue
 constexpr int kEpiWarps = 8;     // lane quarter (warp % 4) x MMA half ((warp - 2) / 4)
+constexpr int kEpiWarp0 = 2;
 constexpr uint32_t kTileA = kMC * kKB * 2;  // 32 KiB of weight codes
 constexpr uint32_t kTileB = kN * kKB * 2;   // 16 KiB per activation plane
 constexpr uint32_t kStageBytes = kTileA + 2 * kTileB;
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers, flags*/;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait, then abort
 
 struct Segment {
@@ -54,15 +64,26 @@ struct GemmArgs {
   int out;           // total output features (sum of segment rows)
   int in;            // K
   int groups;        // ceil(in/64) scale blocks per output row
-  int kb_per_split;  // K-blocks per split
-  int splits;
+  int mt, nt;        // 256-feature tiles, 128-row tiles
+  int ngroups;       // stream-K groups (nt CTAs each); grid = ngroups * nt
   const float* scales;   // [out][groups] (concatenated for fused segments)
-  float* partial;        // [splits][n][out] when splits > 1
-  const int32_t* out_map;  // compacted head rows -> destination row
+  float* partial;        // [ngroups*nt][2][kN][kMC] partial tiles (first / last segment of a CTA)
+  const int32_t* out_map;  // compacted head rows -> destination row (never combined with a residual)
   Segment seg[3];
   int nseg;
   int* err;
 };
+
+// Stream-K range of group g over the mt*groups (tile, block) units.
+__host__ __device__ inline int sk_begin(int g, int units, int ngroups) {
+  return (int)((int64_t)g * units / ngroups);
+}
+__host__ __device__ inline int sk_group_of(int u, int units, int ngroups) {
+  int g = (int)((int64_t)u * ngroups / units);
+  while (g + 1 < ngroups && sk_begin(g + 1, units, ngroups) <= u) g++;
+  while (g > 0 && sk_begin(g, units, ngroups) > u) g--;
+  return g;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -151,24 +172,40 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ void store_out(const GemmArgs& a, int row, int o, float v) {
-  int s = 0, base = 0;
-  while (s + 1 < a.nseg && o >= base + a.seg[s].rows) {
-    base += a.seg[s].rows;
-    s++;
-  }
-  const Segment& g = a.seg[s];
-  const int ol = o - base;
-  const int orow = a.out_map ? a.out_map[row] : row;
-  float* dst = g.y + (int64_t)orow * g.ldy + ol;
-  if (g.bias) v += g.bias[ol];
-  if (g.resid) v = g.resid[(int64_t)orow * g.ldy + ol] + v;
-  *dst = v;
+// Output column of feature o: its segment's destination, stride, bias and
+// residual, resolved once per thread.
+struct OutCol {
+  float* y;
+  const float* resid;
+  float bias;
+  int ldy;
+  bool has_bias;
+};
+__device__ __forceinline__ OutCol out_col(const GemmArgs& a, int o) {
+  // constant indices into a.seg (a dynamic index would copy it to local memory)
+  const int r0 = a.seg[0].rows, r1 = a.seg[1].rows;
+  const int s = (a.nseg > 1 && o >= r0) ? ((a.nseg > 2 && o >= r0 + r1) ? 2 : 1) : 0;
+  const Segment& g = s == 0 ? a.seg[0] : (s == 1 ? a.seg[1] : a.seg[2]);
+  const int ol = o - (s == 0 ? 0 : (s == 1 ? r0 : r0 + r1));
+  OutCol c;
+  c.y = g.y + ol;
+  c.resid = g.resid ? g.resid + ol : nullptr;
+  c.has_bias = g.bias != nullptr;
+  c.bias = g.bias ? g.bias[ol] : 0.f;
+  c.ldy = g.ldy;
+  return c;
 }
 
-// grid: (ceil(n/128), ceil(out/256), splits): the row tiles of one weight tile run together (L2 reuse)
+// grid: ngroups * nt CTAs, one per SM (197 KiB of shared memory each).
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xh,
          const __grid_constant__ CUtensorMap tm_xl, GemmArgs a) {
@@ -181,10 +218,13 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
   uint32_t* tmem_slot = (uint32_t*)(tempty + kAcc);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kMC, n0 = blockIdx.x * kN, split = blockIdx.z;
-  const int kb0 = split * a.kb_per_split;
-  const int kb1 = min(a.groups, kb0 + a.kb_per_split);
-  const int nkb = max(0, kb1 - kb0);
+  const int g = blockIdx.x / a.nt, j = blockIdx.x % a.nt;  // stream-K group, row tile
+  const int K = a.groups;
+  const int units = a.mt * K;
+  const int ub = sk_begin(g, units, a.ngroups), ue = sk_begin(g + 1, units, a.ngroups);
+  const int nu = ue - ub;
+  const int m_first = ub / K, kb_first = ub - m_first * K;
+  const int n0 = j * kN;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
@@ -209,21 +249,21 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
-      for (int i = 0; i < nkb; i++) {
+      int m = m_first, kb = kb_first;
+      for (int i = 0; i < nu; i++, kb = (kb + 1 == K) ? 0 : kb + 1, m += (kb == 0) ? 1 : 0) {
         const int s = i % kStages, use = i / kStages;
         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, a.err)) break;
         uint8_t* st = gsm + s * kStageBytes;
         mbar_expect_tx(&full[s], kStageBytes);
-        const int k = (kb0 + i) * kKB;
-        tma_load_2d(st, &tm_w, &full[s], k, m0);
-        tma_load_2d(st + kTileA, &tm_xh, &full[s], k, n0);
-        tma_load_2d(st + kTileA + kTileB, &tm_xl, &full[s], k, n0);
+        tma_load_2d(st, &tm_w, &full[s], kb * kKB, m * kMC);
+        tma_load_2d(st + kTileA, &tm_xh, &full[s], kb * kKB, n0);
+        tma_load_2d(st + kTileA + kTileB, &tm_xl, &full[s], kb * kKB, n0);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
       const uint32_t idesc = idesc_bf16(kM, kN);
-      for (int i = 0; i < nkb; i++) {
+      for (int i = 0; i < nu; i++) {
         const int s = i % kStages, b = i % kAcc;
         if (!mbar_wait(&full[s], (i / kStages) & 1, a.err)) break;
         if (i >= kAcc && !mbar_wait(&tempty[b], ((i / kAcc) - 1) & 1, a.err)) break;
@@ -244,46 +284,76 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
       }
     }
   } else {  // epilogue warps 2..9: TMEM lane quarter = warp % 4, MMA half = (warp - 2) / 4
-    const int q = warp & 3, h = (warp - 2) >> 2;
-    const int o = m0 + h * kM + q * 32 + lane;
+    // After an expired wait the warp only skips the TMEM reads.  The loops
+    // keep little state besides acc[] so that it stays in registers.
+    const int q = warp & 3, h = (warp - kEpiWarp0) >> 2;
+    const int f = h * kM + q * 32 + lane;  // feature within the tile
+    bool ok = true;
     float acc[kN];
 #pragma unroll
-    for (int j = 0; j < kN; j++) acc[j] = 0.f;
-    const float* srow = a.scales + (int64_t)min(o, a.out - 1) * a.groups;
-    for (int i = 0; i < nkb; i++) {
-      const int b = i % kAcc;
-      const float sc = srow[kb0 + i];
-      if (!mbar_wait(&tfull[b], (i / kAcc) & 1, a.err)) break;
-      tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * (kMH * kN) + h * kN;
+    for (int jj = 0; jj < kN; jj++) acc[jj] = 0.f;
+    int kb_s = kb_first;
+    int m = m_first, kb = kb_first;
+    for (int i = 0; i < nu; i++, kb = (kb + 1 == K) ? 0 : kb + 1, m += (kb == 0) ? 1 : 0) {
+      const int b = i & 1;
+      const int o = m * kMC + f;
+      if (kb == 0) kb_s = 0;
+      const float sc = a.scales[(int64_t)min(o, a.out - 1) * K + kb];
+      ok = ok && mbar_wait(&tfull[b], (i >> 1) & 1, a.err);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * (kMH * kN) + h * kN;
 #pragma unroll
-      for (int c = 0; c < kN; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(taddr + c, v);
-        tmem_wait_ld();
-        if (c + 32 == kN) {  // buffer fully read: hand it back before the FMAs
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[b]);
+        for (int c = 0; c < kN; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(taddr + c, v);
+          tmem_wait_ld();
+          if (c + 16 == kN) {  // buffer fully read: hand it back before the FMAs
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+          }
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++) acc[c + jj] = fmaf(__uint_as_float(v[jj]), sc, acc[c + jj]);
         }
-#pragma unroll
-        for (int j = 0; j < 32; j++) acc[c + j] = fmaf(__uint_as_float(v[j]), sc, acc[c + j]);
       }
-    }
-    if (o < a.out) {
-      if (a.splits > 1) {
-        float* P = a.partial + (int64_t)split * a.n * a.out;
-#pragma unroll
-        for (int j = 0; j < kN; j++) {
-          const int row = n0 + j;
-          if (row < a.n) P[(int64_t)row * a.out + o] = acc[j];
+      if (kb != K - 1 && i != nu - 1) continue;
+      const int kb_e = kb;
+      // ---- the group's segment of tile (m, j) ends here.  A whole tile that
+      // needs only a bias goes straight to the output; every other segment
+      // goes to this CTA's partial slot (first segment: 0, later ones: 1) for
+      // k_sk_reduce.  (This store shape keeps acc[] in registers: a per-element
+      // select of the bias, or a dynamic row bound inside the loop, did not.)
+      const bool whole = (kb_s == 0 && kb_e == K - 1);
+      bool direct = false;
+      float* dst;
+      int ld;
+      bool hb = false;
+      float bias = 0.f;
+      if (whole && o < a.out) {
+        const OutCol oc = out_col(a, o);
+        direct = !oc.resid && !a.out_map;
+        if (direct) {
+          dst = oc.y + (int64_t)n0 * oc.ldy;
+          ld = oc.ldy;
+          hb = oc.has_bias;
+          bias = oc.bias;
         }
-      } else {
+      }
+      if (!direct) {
+        dst = a.partial + ((int)blockIdx.x * 2 + ((m == m_first) ? 0 : 1)) * kN * kMC + f;
+        ld = kMC;
+      }
+      const bool write = direct || !whole || o < a.out;
+      const int nr = write ? min(kN, a.n - n0) : 0;
+      if (hb) {
 #pragma unroll
-        for (int j = 0; j < kN; j++) {
-          const int row = n0 + j;
-          if (row < a.n) store_out(a, row, o, acc[j]);
-        }
+        for (int jj = 0; jj < kN; jj++) acc[jj] += bias;
+      }
+#pragma unroll
+      for (int jj = 0; jj < kN; jj++) {
+        if (jj < nr) dst[jj * ld] = acc[jj];
+        acc[jj] = 0.f;
       }
     }
   }
@@ -295,34 +365,48 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
   }
 }
 
-// Deterministic split-K reduction (splits summed in order) + epilogue; four
-// consecutive outputs per thread when the row length allows it.
-__global__ void k_gemm_reduce(GemmArgs a) {
-  const int64_t total = (int64_t)a.n * a.out;
-  if ((a.out & 3) == 0) {
-    const int64_t total4 = total >> 2;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total4; t += (int64_t)gridDim.x * blockDim.x) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int s = 0; s < a.splits; s++) {
-        const float4 p = *(const float4*)(a.partial + (int64_t)s * total + 4 * t);
-        v.x += p.x;
-        v.y += p.y;
-        v.z += p.z;
-        v.w += p.w;
-      }
-      const int row = (int)((4 * t) / a.out), o = (int)((4 * t) % a.out);
-      store_out(a, row, o, v.x);
-      store_out(a, row, o + 1, v.y);
-      store_out(a, row, o + 2, v.z);
-      store_out(a, row, o + 3, v.w);
-    }
-    return;
+// Tiles a stream-K launch left in partial slots (split tiles, and whole tiles
+// that need the residual or the head row map): out[row][o] = the groups'
+// partials added in block order, then bias / residual / head row map.  grid (mt*nt, kN/32),
+// block kMC threads (one output feature each, 32 rows).
+__global__ void __launch_bounds__(kMC) k_sk_reduce(GemmArgs a) {
+  const int t = blockIdx.x, m = t / a.nt, j = t % a.nt;
+  const int K = a.groups, units = a.mt * K;
+  const int gf = sk_group_of(m * K, units, a.ngroups), gl = sk_group_of(m * K + K - 1, units, a.ngroups);
+  const int f = threadIdx.x, o = m * kMC + f;
+  const int r0 = blockIdx.y * 32, n0 = j * kN;
+  if (o >= a.out || n0 + r0 >= a.n) return;
+  const OutCol oc = out_col(a, o);
+  if (gf == gl && !oc.resid && !a.out_map) return;  // the GEMM stored this tile
+  float v[32];
+#pragma unroll
+  for (int jj = 0; jj < 32; jj++) v[jj] = 0.f;
+  for (int gs = gf; gs <= gl; gs++) {
+    const int sl = (sk_begin(gs, units, a.ngroups) / K == m) ? 0 : 1;
+    const float* P = a.partial + ((int64_t)(gs * a.nt + j) * 2 + sl) * kN * kMC + (int64_t)r0 * kMC + f;
+#pragma unroll
+    for (int jj = 0; jj < 32; jj++) v[jj] += __ldcg(P + jj * kMC);
   }
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-    const int row = (int)(t / a.out), o = (int)(t % a.out);
-    float v = 0.f;
-    for (int s = 0; s < a.splits; s++) v += a.partial[(int64_t)s * total + t];
-    store_out(a, row, o, v);
+  float pre[32];
+#pragma unroll
+  for (int jj = 0; jj < 32; jj++) {
+    const int row = n0 + r0 + jj;
+    pre[jj] = 0.f;
+    if (row < a.n) {
+      if (a.out_map) pre[jj] = __int_as_float(a.out_map[row]);
+      else if (oc.resid) pre[jj] = oc.resid[(int64_t)row * oc.ldy];
+    }
+  }
+#pragma unroll
+  for (int jj = 0; jj < 32; jj++) {
+    const int row = n0 + r0 + jj;
+    if (row < a.n) {
+      const int64_t orow = a.out_map ? (int64_t)__float_as_int(pre[jj]) : (int64_t)row;
+      float x = v[jj];
+      if (oc.has_bias) x += oc.bias;
+      if (oc.resid) x = pre[jj] + x;
+      oc.y[orow * oc.ldy] = x;
+    }
   }
 }
 
