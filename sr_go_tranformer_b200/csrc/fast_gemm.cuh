@@ -224,7 +224,7 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::Gemm
   a.err = t->err;
   a.mt = (W.rows + tc::kMC - 1) / tc::kMC;
   a.nt = (n + tc::kN - 1) / tc::kN;
-  if (a.nt > t->sms) return false;
+  if (a.nt > t->sms || (int64_t)a.mt * a.groups * t->sms >= ((int64_t)1 << 31)) return false;  // 32-bit schedule math
   const int64_t units = (int64_t)a.mt * a.groups;
   a.ngroups = (int)std::max<int64_t>(1, std::min<int64_t>(t->sms / a.nt, (units + kSkMinUnits - 1) / kSkMinUnits));
   a.partial = t->partial;
@@ -232,13 +232,15 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::Gemm
   const CUtensorMap& xl = in_kind == 1 ? t->xl_h : (in_kind == 2 ? t->xl_q : t->xl_d);
   tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, m->stream>>>(W.map, xh, xl, a);
   sr_count_launch(m);
-  bool split = a.out_map != nullptr;  // tiles left in partial slots?
-  for (int sg = 0; sg < a.nseg; sg++) split = split || a.seg[sg].resid != nullptr;
-  for (int mi = 0; mi < a.mt && !split; mi++)
-    split = tc::sk_group_of(mi * a.groups, (int)units, a.ngroups) !=
-            tc::sk_group_of(mi * a.groups + a.groups - 1, (int)units, a.ngroups);
-  if (split) {
-    tc::k_sk_reduce<<<dim3(a.mt * a.nt, tc::kN / 32), tc::kMC, 0, m->stream>>>(a);
+  // Tiles left in partial slots: every tile when the epilogue needs the
+  // residual or the head row map, otherwise only tiles cut by a group boundary.
+  bool all = a.out_map != nullptr;
+  for (int sg = 0; sg < a.nseg; sg++) all = all || a.seg[sg].resid != nullptr;
+  if (all) {
+    tc::k_sk_reduce<<<dim3(a.mt * a.nt, tc::kN / tc::kRedBlockRows), tc::kMC, 0, m->stream>>>(a, 0);
+    sr_count_launch(m);
+  } else if (a.ngroups > 1) {
+    tc::k_sk_reduce<<<dim3((a.ngroups - 1) * a.nt, tc::kN / tc::kRedBlockRows), tc::kMC, 0, m->stream>>>(a, 1);
     sr_count_launch(m);
   }
   t->ran = true;

@@ -175,18 +175,23 @@ inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int r
   const size_t o_bytes = items * dm.group * dm.hd * 4;
   if (o_bytes > ((size_t)1 << 30)) return false;
   if (items > st->items_cap) {
+    // Grow by half again (within the 1 GiB cap): the item count creeps up as
+    // contexts cross 256-position boundaries, and every reallocation
+    // synchronises the device.
+    const size_t unit_o = (size_t)dm.group * dm.hd * 4;
+    const size_t cap = std::max(items, std::min(st->items_cap + st->items_cap / 2, ((size_t)1 << 30) / unit_o));
     if (st->part_o) cudaFree(st->part_o);
     if (st->part_ml) cudaFree(st->part_ml);
     st->part_o = st->part_ml = nullptr;
     st->items_cap = 0;
-    if (cudaMalloc((void**)&st->part_o, o_bytes) != cudaSuccess ||
-        cudaMalloc((void**)&st->part_ml, items * dm.group * 2 * 4) != cudaSuccess) {
+    if (cudaMalloc((void**)&st->part_o, cap * unit_o) != cudaSuccess ||
+        cudaMalloc((void**)&st->part_ml, cap * dm.group * 2 * 4) != cudaSuccess) {
       cudaGetLastError();
       if (st->part_o) cudaFree(st->part_o);
       st->part_o = nullptr;
       return false;
     }
-    st->items_cap = items;
+    st->items_cap = cap;
   }
   return fast_attention_run(m, pool_data, n, row_items, layer, st->part_o, st->part_ml, xh, xl);
 }

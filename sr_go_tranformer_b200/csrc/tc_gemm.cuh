@@ -74,12 +74,13 @@ struct GemmArgs {
   int* err;
 };
 
-// Stream-K range of group g over the mt*groups (tile, block) units.
+// Stream-K range of group g over the mt*groups (tile, block) units.  32-bit
+// arithmetic: g, ngroups <= 148 and units < 2^24 (checked on the host).
 __host__ __device__ inline int sk_begin(int g, int units, int ngroups) {
-  return (int)((int64_t)g * units / ngroups);
+  return (int)((unsigned)(g * units) / (unsigned)ngroups);
 }
 __host__ __device__ inline int sk_group_of(int u, int units, int ngroups) {
-  int g = (int)((int64_t)u * ngroups / units);
+  int g = (int)((unsigned)(u * ngroups) / (unsigned)units);
   while (g + 1 < ngroups && sk_begin(g + 1, units, ngroups) <= u) g++;
   while (g > 0 && sk_begin(g, units, ngroups) > u) g--;
   return g;
@@ -133,6 +134,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
+// Bring [p, p + bytes) into L2 (a hint: no shared memory, no barrier).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+// The per-block scales of 256-feature tile m (contiguous: rows m*256.. of a
+// [out][groups] array), so that the epilogue's scale loads hit L2.
+__device__ __forceinline__ void prefetch_tile_scales(const GemmArgs& a, int m) {
+  if (m >= a.mt) return;
+  const int rows = min(kMC, a.out - m * kMC);
+  const uint32_t bytes = ((uint32_t)rows * a.groups * 4u) & ~15u;  // bulk sizes are multiples of 16
+  if (bytes) prefetch_l2(a.scales + (int64_t)m * kMC * a.groups, bytes);
+}
 // K-major, SWIZZLE_128B shared-memory matrix descriptor (rows of 128 bytes,
 // 8-row groups 1024 bytes apart).
 __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
@@ -178,6 +191,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
+}
+// Wait for this thread's outstanding TMEM loads.  The registers of the load
+// being waited for are in/out operands, so no use of them can be scheduled
+// before the wait.
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -249,8 +272,12 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
+      // The epilogue reads one scale per unit right before its FMAs: bring
+      // each tile's scales (and the next tile's) into L2 when the tile starts.
+      if (nu > 0) prefetch_tile_scales(a, m_first);
       int m = m_first, kb = kb_first;
       for (int i = 0; i < nu; i++, kb = (kb + 1 == K) ? 0 : kb + 1, m += (kb == 0) ? 1 : 0) {
+        if (i == 0 || kb == 0) prefetch_tile_scales(a, m + 1);
         const int s = i % kStages, use = i / kStages;
         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, a.err)) break;
         uint8_t* st = gsm + s * kStageBytes;
@@ -303,18 +330,27 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
       if (ok) {
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * (kMH * kN) + h * kN;
+        // Two 16-column register sets: the load of the next set is in flight
+        // while the FMAs consume the current one.
+        uint32_t va[16], vb[16];
+        tmem_ld16(taddr, va);
+        tmem_wait_ld16(va);
 #pragma unroll
-        for (int c = 0; c < kN; c += 16) {
-          uint32_t v[16];
-          tmem_ld16(taddr + c, v);
-          tmem_wait_ld();
-          if (c + 16 == kN) {  // buffer fully read: hand it back before the FMAs
+        for (int c = 0; c < kN; c += 32) {
+          tmem_ld16(taddr + c + 16, vb);
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++) acc[c + jj] = fmaf(__uint_as_float(va[jj]), sc, acc[c + jj]);
+          tmem_wait_ld16(vb);
+          if (c + 32 < kN) {
+            tmem_ld16(taddr + c + 32, va);
+          } else {  // buffer fully read: hand it back before the last FMAs
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[b]);
           }
 #pragma unroll
-          for (int jj = 0; jj < 16; jj++) acc[c + jj] = fmaf(__uint_as_float(v[jj]), sc, acc[c + jj]);
+          for (int jj = 0; jj < 16; jj++) acc[c + 16 + jj] = fmaf(__uint_as_float(vb[jj]), sc, acc[c + 16 + jj]);
+          if (c + 32 < kN) tmem_wait_ld16(va);
         }
       }
       if (kb != K - 1 && i != nu - 1) continue;
@@ -367,45 +403,83 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
 
 // Tiles a stream-K launch left in partial slots (split tiles, and whole tiles
 // that need the residual or the head row map): out[row][o] = the groups'
-// partials added in block order, then bias / residual / head row map.  grid (mt*nt, kN/32),
-// block kMC threads (one output feature each, 32 rows).
-__global__ void __launch_bounds__(kMC) k_sk_reduce(GemmArgs a) {
-  const int t = blockIdx.x, m = t / a.nt, j = t % a.nt;
+// partials added in block order, then bias / residual / head row map.
+// grid (tiles*nt, kN/kRedBlockRows), block kMC threads (one output feature
+// each) over kRedBlockRows rows in chunks of kRedRows.
+// by_boundary: blockIdx.x / nt is a group boundary b (1..ngroups-1) and the
+// block finishes the tile it cuts (once per tile: at its first inner
+// boundary); otherwise blockIdx.x / nt is the tile.  The partials of up to 8
+// groups for a chunk are loaded before any add.
+constexpr int kRedRows = 8;
+constexpr int kRedBlockRows = 32;
+__global__ void __launch_bounds__(kMC, 2) k_sk_reduce(GemmArgs a, int by_boundary) {
   const int K = a.groups, units = a.mt * K;
+  const int j = blockIdx.x % a.nt;
+  int m = blockIdx.x / a.nt;
+  if (by_boundary) {
+    const int bnd = m + 1, u = sk_begin(bnd, units, a.ngroups);
+    m = u / K;
+    if (u == m * K) return;                                              // boundary on a tile edge
+    if (bnd > 1 && sk_begin(bnd - 1, units, a.ngroups) > m * K) return;  // tile owned by an earlier boundary
+  }
   const int gf = sk_group_of(m * K, units, a.ngroups), gl = sk_group_of(m * K + K - 1, units, a.ngroups);
   const int f = threadIdx.x, o = m * kMC + f;
-  const int r0 = blockIdx.y * 32, n0 = j * kN;
-  if (o >= a.out || n0 + r0 >= a.n) return;
+  const int n0 = j * kN;
+  if (o >= a.out) return;
   const OutCol oc = out_col(a, o);
   if (gf == gl && !oc.resid && !a.out_map) return;  // the GEMM stored this tile
-  float v[32];
+  const int ns = gl - gf + 1;
+  int off[8];  // partial slot of each group (first segment of a group: slot 0)
 #pragma unroll
-  for (int jj = 0; jj < 32; jj++) v[jj] = 0.f;
-  for (int gs = gf; gs <= gl; gs++) {
+  for (int q = 0; q < 8; q++) {
+    const int gs = min(gf + q, gl);
     const int sl = (sk_begin(gs, units, a.ngroups) / K == m) ? 0 : 1;
-    const float* P = a.partial + ((int64_t)(gs * a.nt + j) * 2 + sl) * kN * kMC + (int64_t)r0 * kMC + f;
-#pragma unroll
-    for (int jj = 0; jj < 32; jj++) v[jj] += __ldcg(P + jj * kMC);
+    off[q] = ((gs * a.nt + j) * 2 + sl) * kN * kMC + f;
   }
-  float pre[32];
+  for (int r0 = blockIdx.y * kRedBlockRows; r0 < (int)(blockIdx.y + 1) * kRedBlockRows && n0 + r0 < a.n;
+       r0 += kRedRows) {
+    float v[kRedRows];
 #pragma unroll
-  for (int jj = 0; jj < 32; jj++) {
-    const int row = n0 + r0 + jj;
-    pre[jj] = 0.f;
-    if (row < a.n) {
-      if (a.out_map) pre[jj] = __int_as_float(a.out_map[row]);
-      else if (oc.resid) pre[jj] = oc.resid[(int64_t)row * oc.ldy];
+    for (int jj = 0; jj < kRedRows; jj++) v[jj] = 0.f;
+    if (ns <= 8) {
+      float p[8][kRedRows];
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+#pragma unroll
+        for (int jj = 0; jj < kRedRows; jj++) p[q][jj] = (q < ns) ? __ldcg(a.partial + off[q] + (r0 + jj) * kMC) : 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+#pragma unroll
+        for (int jj = 0; jj < kRedRows; jj++)
+          if (q < ns) v[jj] += p[q][jj];
+    } else {
+      for (int gs = gf; gs <= gl; gs++) {
+        const int sl = (sk_begin(gs, units, a.ngroups) / K == m) ? 0 : 1;
+        const float* P = a.partial + ((gs * a.nt + j) * 2 + sl) * kN * kMC + r0 * kMC + f;
+#pragma unroll
+        for (int jj = 0; jj < kRedRows; jj++) v[jj] += __ldcg(P + jj * kMC);
+      }
     }
-  }
+    float pre[kRedRows];
 #pragma unroll
-  for (int jj = 0; jj < 32; jj++) {
-    const int row = n0 + r0 + jj;
-    if (row < a.n) {
-      const int64_t orow = a.out_map ? (int64_t)__float_as_int(pre[jj]) : (int64_t)row;
-      float x = v[jj];
-      if (oc.has_bias) x += oc.bias;
-      if (oc.resid) x = pre[jj] + x;
-      oc.y[orow * oc.ldy] = x;
+    for (int jj = 0; jj < kRedRows; jj++) {
+      const int row = n0 + r0 + jj;
+      pre[jj] = 0.f;
+      if (row < a.n) {
+        if (a.out_map) pre[jj] = __int_as_float(a.out_map[row]);
+        else if (oc.resid) pre[jj] = oc.resid[(int64_t)row * oc.ldy];
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < kRedRows; jj++) {
+      const int row = n0 + r0 + jj;
+      if (row < a.n) {
+        const int64_t orow = a.out_map ? (int64_t)__float_as_int(pre[jj]) : (int64_t)row;
+        float x = v[jj];
+        if (oc.has_bias) x += oc.bias;
+        if (oc.resid) x = pre[jj] + x;
+        oc.y[orow * oc.ldy] = x;
+      }
     }
   }
 }
