@@ -15,11 +15,10 @@
 namespace sr {
 
 struct TcMatrix {
-  __nv_bfloat16* w16 = nullptr;
+  uint8_t* wt = nullptr;  // bf16 codes in 32 KiB swizzled (256-feature, 64-column) tiles
   float* scales = nullptr;
   bool own_scales = false;
   int rows = 0, cols = 0;
-  CUtensorMap map;
 };
 
 struct TcState {
@@ -100,9 +99,12 @@ inline bool tc_build(sr_model* m, TcState* t, TcMatrix& dst, const std::vector<c
     rows += p->rows;
   }
   const int groups = (cols + kQBlock - 1) / kQBlock;
+  const int mt = (rows + tc::kMC - 1) / tc::kMC;
   dst.rows = rows;
   dst.cols = cols;
-  if (!tc_alloc(t, (void**)&dst.w16, (size_t)rows * cols * 2)) return false;
+  const size_t bytes = (size_t)mt * groups * tc::kTileA;
+  if (!tc_alloc(t, (void**)&dst.wt, bytes)) return false;
+  cudaMemsetAsync(dst.wt, 0, bytes, m->stream);  // padding rows of the last tile
   if (parts.size() == 1) {
     dst.scales = parts[0]->scales;
     dst.own_scales = false;
@@ -112,15 +114,15 @@ inline bool tc_build(sr_model* m, TcState* t, TcMatrix& dst, const std::vector<c
   }
   int r0 = 0;
   for (const Param* p : parts) {
-    const int64_t total = (int64_t)p->rows * cols;
-    tc::k_codes_bf16<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 64), 256, 0, m->stream>>>(
-        p->values, p->format, p->rows, cols, dst.w16 + (int64_t)r0 * cols);
+    const int64_t chunks = (int64_t)p->rows * groups * 8;
+    tc::k_codes_tiled<<<(int)std::min<int64_t>((chunks + 255) / 256, 148 * 64), 256, 0, m->stream>>>(
+        p->values, p->format, p->rows, cols, r0, groups, dst.wt);
     if (dst.own_scales)
       cudaMemcpyAsync(dst.scales + (int64_t)r0 * groups, p->scales, (size_t)p->rows * groups * 4,
                       cudaMemcpyDeviceToDevice, m->stream);
     r0 += p->rows;
   }
-  return make_map(&dst.map, dst.w16, (uint64_t)cols, (uint64_t)rows, tc::kMC);
+  return true;
 }
 
 // Lazily (re)build the shadows after the weights change.  Returns false when
@@ -230,7 +232,8 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::Gemm
   a.partial = t->partial;
   const CUtensorMap& xh = in_kind == 1 ? t->xh_h : (in_kind == 2 ? t->xh_q : t->xh_d);
   const CUtensorMap& xl = in_kind == 1 ? t->xl_h : (in_kind == 2 ? t->xl_q : t->xl_d);
-  tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, m->stream>>>(W.map, xh, xl, a);
+  a.wt = W.wt;
+  tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, m->stream>>>(xh, xl, a);
   sr_count_launch(m);
   // Tiles left in partial slots: every tile when the epilogue needs the
   // residual or the head row map, otherwise only tiles cut by a group boundary.

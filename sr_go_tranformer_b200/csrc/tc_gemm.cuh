@@ -2,7 +2,10 @@
 //
 // Y[n, out] = X[n, in] W[out, in]^T for Q8/Q4 weights (linearQ8Into / linearQ4Into,
 // cmd/monolith/monolith.go:4074-4511) restated for tcgen05:
-//   * W's integer codes are held as bf16 (exact: |q| <= 127) in a shadow copy;
+//   * W's integer codes are held as bf16 (exact: |q| <= 127) in a shadow copy
+//     laid out as contiguous 32 KiB (256-feature, 64-column) tiles that are
+//     already in the MMA's 128-byte-swizzled shared-memory order, so each
+//     weight tile is one bulk copy (a few DRAM pages, not 256 strided rows);
 //     the fp32 activations are split into bf16 hi + lo planes, so each 64-column
 //     block's partial sum  sum_j x_j q_j  is formed by two MMA passes with fp32
 //     accumulation in TMEM (relative error ~2^-16 per term);
@@ -60,6 +63,7 @@ struct Segment {
 };
 
 struct GemmArgs {
+  const uint8_t* wt;  // tiled weight codes: tile (m, kb) at (m * groups + kb) * kTileA bytes
   int n;             // step rows
   int out;           // total output features (sum of segment rows)
   int in;            // K
@@ -126,6 +130,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
       }
     }
   }
+}
+// Contiguous global -> shared bulk copy completing on an mbarrier (16-byte
+// aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
@@ -230,8 +242,7 @@ __device__ __forceinline__ OutCol out_col(const GemmArgs& a, int o) {
 
 // grid: ngroups * nt CTAs, one per SM (197 KiB of shared memory each).
 __global__ void __launch_bounds__(kThreads, 1)
-k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xh,
-         const __grid_constant__ CUtensorMap tm_xl, GemmArgs a) {
+k_gemm_q(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl, GemmArgs a) {
   extern __shared__ __align__(1024) uint8_t gsm_raw[];
   uint8_t* gsm = (uint8_t*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(gsm + kStages * kStageBytes);
@@ -282,7 +293,7 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUten
         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, a.err)) break;
         uint8_t* st = gsm + s * kStageBytes;
         mbar_expect_tx(&full[s], kStageBytes);
-        tma_load_2d(st, &tm_w, &full[s], kb * kKB, m * kMC);
+        bulk_load(st, a.wt + ((int64_t)m * K + kb) * kTileA, kTileA, &full[s]);
         tma_load_2d(st + kTileA, &tm_xh, &full[s], kb * kKB, n0);
         tma_load_2d(st + kTileA + kTileB, &tm_xl, &full[s], kb * kKB, n0);
       }
@@ -496,20 +507,35 @@ __global__ void k_split_bf16(const float* __restrict__ X, int n, int in, __nv_bf
   }
 }
 
-// Integer codes of a Q8/Q4 matrix as bf16 (exact), rows [0, rows) written at dst_row0.
-__global__ void k_codes_bf16(const void* __restrict__ values, int fmt, int rows, int cols,
-                             __nv_bfloat16* __restrict__ dst) {
-  const int64_t total = (int64_t)rows * cols;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = t / cols, c = t % cols;
-    float q;
-    if (fmt == kQ8) {
-      q = (float)((const int8_t*)values)[t];
-    } else {
-      const uint32_t b = ((const uint8_t*)values)[r * ((cols + 1) / 2) + c / 2];
-      q = (c & 1) ? q4_hi(b) : q4_lo(b);
+// Integer codes of a Q8/Q4 matrix as bf16 (exact) in the tiled, swizzled
+// shadow layout: row r (of a fused matrix, this part starting at row0) and
+// 16-byte chunk c (columns 8c..8c+7 of block kb) of tile m = r / 256 go to
+// byte ((m * groups + kb) * 256 + r % 256) * 128 + ((c ^ (r % 8)) * 16).
+// Columns past cols are written as zero; the caller zeroes rows past the end.
+__global__ void k_codes_tiled(const void* __restrict__ values, int fmt, int rows, int cols, int row0, int groups,
+                              uint8_t* __restrict__ dst) {
+  const int64_t chunks = (int64_t)rows * groups * 8;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < chunks; t += (int64_t)gridDim.x * blockDim.x) {
+    const int rl = (int)(t / (groups * 8)), cc = (int)(t % (groups * 8));
+    const int kb = cc >> 3, c = cc & 7;
+    const int r = row0 + rl, m = r / kMC, rr = r % kMC;
+    __align__(16) __nv_bfloat16 v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int col = kb * kKB + c * 8 + e;
+      float q = 0.f;
+      if (col < cols) {
+        if (fmt == kQ8) {
+          q = (float)((const int8_t*)values)[(int64_t)rl * cols + col];
+        } else {
+          const uint32_t b = ((const uint8_t*)values)[(int64_t)rl * ((cols + 1) / 2) + col / 2];
+          q = (col & 1) ? q4_hi(b) : q4_lo(b);
+        }
+      }
+      v[e] = __float2bfloat16_rn(q);
     }
-    dst[t] = __float2bfloat16_rn(q);
+    const int64_t off = (((int64_t)m * groups + kb) * kMC + rr) * 128 + (int64_t)((c ^ (rr & 7)) * 16);
+    *(uint4*)(dst + off) = *(const uint4*)v;
   }
 }
 
