@@ -10,9 +10,11 @@
 // path within fp32 rounding (tolerance-checked), not bit for bit.
 //
 // head_dim 128 (Mistral, Qwen): k_attn_warp128 -- each of the 4 warps streams
-//   its own 64-position sub-split through a private 2-stage cp.async ring of
-//   8-position tiles and keeps its own softmax state, synchronising with
-//   __syncwarp only; the warps merge once at the end of the split.
+//   its own 64-position sub-split through a private 2-stage ring of
+//   8-position tiles (one 512-byte bulk copy per K or V row, issued by the
+//   row's lane, completing on the warp's mbarrier) and keeps its own softmax
+//   state, synchronising with __syncwarp only; the warps merge once at the
+//   end of the split.
 // head_dim 64 (SmolLM, Llama-1B): k_attn_tile -- the CTA shares 32-position
 //   double-buffered tiles.
 #pragma once
@@ -21,6 +23,7 @@
 #include <float.h>
 
 #include "common.cuh"
+#include "tc_gemm.cuh"  // mbarrier and bulk-copy helpers
 
 namespace sr {
 
@@ -39,6 +42,7 @@ struct FastAttnArgs {
   float* part_ml;  // [items][kv_heads][group][2]
   __nv_bfloat16* xh;  // optional: write the output as bf16 hi/lo planes (the
   __nv_bfloat16* xl;  // next projection's tensor-core operand) instead of fp32 A
+  int* err;           // raised when a bounded wait for a tile expires
 };
 
 // x ~= hi + lo with |x - hi - lo| <= 2^-17 |x| (two bf16 terms).
@@ -77,7 +81,8 @@ struct WarpSmem {
   static constexpr int SC = G * kWpMT;            // scores [G][MT]
   static constexpr int PS = kWpMT * GP;           // probabilities [MT][GP]
   static constexpr int PER_WARP = KV + SC + PS;
-  static constexpr int TOTAL = 4 * PER_WARP;      // floats
+  static constexpr int TOTAL = 4 * PER_WARP;      // floats, then 4 x 2 mbarriers
+  static constexpr size_t BYTES = (size_t)TOTAL * 4 + 4 * 2 * 8;
 };
 
 template <int G>
@@ -96,6 +101,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
   float* kv = wsm;                                 // [2][2][MT][HD]
   float* sc = wsm + WarpSmem<G>::KV;               // [G][MT]
   float* ps = sc + WarpSmem<G>::SC;                // [MT][GP]
+  uint64_t* bar = (uint64_t*)(fsm + WarpSmem<G>::TOTAL) + warp * 2;  // past the merge area
   const int pbase = a.meta.row_pbase[r];
   const int pt = a.dm.page_tokens;
   const int64_t lay = (int64_t)a.layer * 2 * pt * a.dm.kvd + (int64_t)kh * HD;
@@ -111,24 +117,31 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
   const int npg = nw > 0 ? (ws1 - 1) / pt - pg0 + 1 : 0;
   const bool page_regs = npg <= 32;
   const int my_page = (page_regs && lane < npg) ? a.meta.page_ids[pbase + pg0 + lane] : 0;
-  // lane copies 16-byte chunk `lane` of each K and V row of a tile
+  if (lane == 0) {
+    tc::mbar_init(&bar[0], 1);
+    tc::mbar_init(&bar[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  // Tile t -> stage t & 1: lane s copies the K and V rows of position t0 + s.
   auto load_tile = [&](int t) {
-    float* dst = kv + (t & 1) * 2 * MT * HD;
+    const int st = t & 1;
+    float* dst = kv + st * 2 * MT * HD;
     const int t0 = ws0 + t * MT, tn = min(MT, ws1 - t0);
-    int pi = t0 / pt, po = t0 - pi * pt;  // page index and offset of position t0
-    for (int s = 0; s < tn; s++) {
-      const int64_t page = page_regs ? __shfl_sync(0xffffffffu, my_page, pi - pg0) : a.meta.page_ids[pbase + pi];
-      const float* krow = a.pool + page * a.dm.page_elems + lay + (int64_t)po * a.dm.kvd + 4 * lane;
-      cp_async16(dst + s * HD + 4 * lane, krow);
-      cp_async16(dst + (MT + s) * HD + 4 * lane, krow + vofs);
-      if (++po == pt) {
-        po = 0;
-        pi++;
-      }
+    if (lane == 0) tc::mbar_expect_tx(&bar[st], (uint32_t)tn * 2 * HD * 4);
+    __syncwarp();
+    const int pos = t0 + min(lane, tn - 1);
+    const int pi = pos / pt;
+    const int pg = __shfl_sync(0xffffffffu, my_page, (pi - pg0) & 31);
+    if (lane < tn) {
+      const int64_t page = page_regs ? pg : a.meta.page_ids[pbase + pi];
+      const float* krow = a.pool + page * a.dm.page_elems + lay + (int64_t)(pos - pi * pt) * a.dm.kvd;
+      tc::bulk_load(dst + lane * HD, krow, HD * 4, &bar[st]);
+      tc::bulk_load(dst + (MT + lane) * HD, krow + vofs, HD * 4, &bar[st]);
     }
   };
   if (ntiles > 0) load_tile(0);
-  cp_async_commit();
+  bool ok = true;
 
   // query slices: lane covers dims 4*(lane%8) + 32*i for the score phase
   float4 q[G][4];
@@ -155,14 +168,8 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
 
   for (int t = 0; t < ntiles; t++) {
     __syncwarp();  // the stage about to be refilled has been consumed
-    if (t + 1 < ntiles) {
-      load_tile(t + 1);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncwarp();
+    if (t + 1 < ntiles) load_tile(t + 1);
+    ok = ok && tc::mbar_wait(&bar[t & 1], (t >> 1) & 1, a.err);  // on expiry: error raised, garbage computed
     const float* kt = kv + (t & 1) * 2 * MT * HD;
     const float* vt = kt + MT * HD;
     const int tn = min(MT, ws1 - (ws0 + t * MT));
@@ -187,13 +194,27 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
           }
         }
       }
+      if constexpr (G == 4) {
+        // reduce-scatter over the 8 lanes of the position: after the three
+        // exchanges lane bits (b0, b1) hold head 2*b0 + b1 (4 shuffles, not 12)
+        const bool b0 = lane & 1, b1 = lane & 2;
+        float k0 = b0 ? part[2] : part[0], k1 = b0 ? part[3] : part[1];
+        const float x0 = b0 ? part[0] : part[2], x1 = b0 ? part[1] : part[3];
+        k0 += __shfl_xor_sync(0xffffffffu, x0, 1);
+        k1 += __shfl_xor_sync(0xffffffffu, x1, 1);
+        float kk = b1 ? k1 : k0;
+        kk += __shfl_xor_sync(0xffffffffu, b1 ? k0 : k1, 2);
+        kk += __shfl_xor_sync(0xffffffffu, kk, 4);
+        if ((lane & 4) == 0) sc[(2 * (int)b0 + (int)b1) * MT + s] = s < tn ? kk : -INFINITY;
+      } else {
 #pragma unroll
-      for (int off = 1; off < 8; off <<= 1)
+        for (int off = 1; off < 8; off <<= 1)
 #pragma unroll
-        for (int g = 0; g < G; g++) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
-      if ((lane & 7) == 0)
+          for (int g = 0; g < G; g++) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+        if ((lane & 7) == 0)
 #pragma unroll
-        for (int g = 0; g < G; g++) sc[g * MT + s] = s < tn ? part[g] : -INFINITY;
+          for (int g = 0; g < G; g++) sc[g * MT + s] = s < tn ? part[g] : -INFINITY;
+      }
     }
     __syncwarp();
     // online softmax: lane = (head lane/8 + 4*round, position lane%8)
@@ -246,7 +267,6 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
       }
     }
   }
-  cp_async_wait<0>();
   // merge the 4 warps of the split: O_w, m_w, l_w -> (O, m, l)
   __syncthreads();
   float* mo = fsm;                        // [4][G][HD]
@@ -470,7 +490,8 @@ template <int HD, int G>
 inline size_t fa_smem_bytes() {
   if (HD == 128) {
     const size_t merge = (size_t)(4 * G * HD + 8 * G + G * HD + 2 * G);
-    return std::max((size_t)WarpSmem<G>::TOTAL, merge) * 4;
+    static_assert((4 * G * HD + 8 * G + G * HD + 2 * G) <= WarpSmem<G>::TOTAL, "merge area overlaps the mbarriers");
+    return WarpSmem<G>::BYTES + 0 * merge;
   }
   constexpr int GP = (G + 3) & ~3;
   constexpr int PPAR = kFaThreads / HD;

@@ -16,6 +16,9 @@ struct FastState {
   float* part_o = nullptr;
   float* part_ml = nullptr;
   size_t items_cap = 0;
+  int* err = nullptr;    // device flag raised by an expired bounded wait
+  int* h_err = nullptr;  // pinned host copy
+  bool ran = false;      // a kernel that can raise the flag ran since the last check
 };
 
 inline FastState* fast_state(sr_model* m) { return (FastState*)m->fast; }
@@ -26,8 +29,31 @@ inline int fast_init(sr_model* m) {
   m->fast_free.push_back([st]() {
     if (st->part_o) cudaFree(st->part_o);
     if (st->part_ml) cudaFree(st->part_ml);
+    if (st->err) cudaFree(st->err);
+    if (st->h_err) cudaFreeHost(st->h_err);
     delete st;
   });
+  if (cudaMalloc((void**)&st->err, 16) != cudaSuccess || cudaMallocHost((void**)&st->h_err, 16) != cudaSuccess ||
+      cudaMemset(st->err, 0, 16) != cudaSuccess) {
+    cudaGetLastError();
+    return sr_fail(SR_ENOMEM, "allocating the attention error flag failed");
+  }
+  return SR_OK;
+}
+
+// After the step's stream synchronize: SR_ETIMEOUT if an attention wait expired.
+inline int fast_check(sr_model* m) {
+  FastState* st = fast_state(m);
+  if (!st || !st->err || !st->ran) return SR_OK;
+  st->ran = false;
+  if (cudaMemcpy(st->h_err, st->err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return sr_fail(SR_EDEVICE, "reading the attention error flag failed");
+  }
+  if (*st->h_err) {
+    cudaMemset(st->err, 0, 4);
+    return sr_fail(SR_ETIMEOUT, "an attention tile wait expired; results of this step are invalid");
+  }
   return SR_OK;
 }
 
@@ -160,6 +186,8 @@ inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, int i
   a.part_ml = part_ml;
   a.xh = xh;
   a.xl = xl;
+  a.err = fast_state(m)->err;
+  fast_state(m)->ran = true;
   return dm.hd == 128 ? fa_dispatch_g<128>(m, a, n, items) : fa_dispatch_g<64>(m, a, n, items);
 }
 

@@ -934,6 +934,7 @@ extern "C" int sr_step(sr_model* m, sr_kvpool* pool, const sr_batch* batch, floa
                        m->stream));
   CK(cudaStreamSynchronize(m->stream));
   sr_prof_resolve(m);
+  if (int rc = fast_check(m)) return rc;
   return tc_check(m);
 }
 
@@ -1009,6 +1010,7 @@ int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const
 int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_out) {
   CK(cudaStreamSynchronize(m->stream));
   sr_prof_resolve(m);
+  if (int rc = fast_check(m)) return rc;
   if (int rc = tc_check(m)) return rc;
   uint8_t* h = (uint8_t*)m->h_stage + m->upload_ints * 4;
   const size_t off_hoff = kSampOffHistOff, off_hist = kSampOffHist, off_rng = kSampOffRng, off_ids = kSampOffIds,
@@ -1205,5 +1207,5 @@ extern "C" int sr_step_noalloc(sr_model* m, sr_kvpool* pool, const sr_batch* bat
                        m->stream));
   CK(cudaStreamSynchronize(m->stream));
   sr_prof_resolve(m);
-  return SR_OK;
+  return fast_check(m);
 }
