@@ -469,15 +469,31 @@ __global__ void __launch_bounds__(HD) k_attn_combine(FastAttnArgs a) {
   const int ns = (L + kFaSplit - 1) / kFaSplit;
   const int KVH = a.dm.kv_heads;
   const int64_t base = (int64_t)a.meta.row_item0[r] * KVH + kh;  // split s is unit base + s*KVH
-  float M = -INFINITY;
-  for (int s = 0; s < ns; s++) M = fmaxf(M, a.part_ml[((base + (int64_t)s * KVH) * G + g) * 2]);
-  float den = 0.f, num = 0.f;
-  for (int s = 0; s < ns; s++) {
-    const int64_t u = base + (int64_t)s * KVH;
-    const float ms = a.part_ml[(u * G + g) * 2];
-    const float w = (ms == -INFINITY) ? 0.f : __expf(ms - M);
-    den += w * a.part_ml[(u * G + g) * 2 + 1];
-    num += w * a.part_o[(u * G + g) * HD + d];
+  // one online pass over the splits in order; the loads of 8 splits are issued together
+  float M = -INFINITY, den = 0.f, num = 0.f;
+  for (int c = 0; c < ns; c += 8) {
+    float m8[8], l8[8], o8[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const bool v = c + k < ns;
+      const int64_t u = base + (int64_t)(c + k) * KVH;
+      m8[k] = v ? a.part_ml[(u * G + g) * 2] : -INFINITY;
+      l8[k] = v ? a.part_ml[(u * G + g) * 2 + 1] : 0.f;
+      o8[k] = v ? a.part_o[(u * G + g) * HD + d] : 0.f;
+    }
+    float Mc = M;
+#pragma unroll
+    for (int k = 0; k < 8; k++) Mc = fmaxf(Mc, m8[k]);
+    const float rs = (M == -INFINITY) ? 0.f : __expf(M - Mc);
+    den *= rs;
+    num *= rs;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const float w = (m8[k] == -INFINITY) ? 0.f : __expf(m8[k] - Mc);
+      den += w * l8[k];
+      num += w * o8[k];
+    }
+    M = Mc;
   }
   const int64_t o = (int64_t)r * a.dm.qd + (int64_t)h * HD + d;
   if (a.xh)
