@@ -25,6 +25,14 @@ engine tensor-parallel -- each holds 1/N of the heads, FFN columns and KV pool
 and the step all-reduces after o_proj and down_proj over NCCL -- so total
 work is fixed (strong scaling).  --parallel replicas runs N independent
 engines instead (weak scaling).
+`ttft_p50_ms` comes from a serving run before the decode measurement: the
+            same 256 requests (prompt ids uniform over the vocabulary) are
+            submitted at once to the C++ restatement of the reference engine
+            (admission, scheduleTokens, steps, sampling) on an empty KV pool,
+            with prefill chunks of 1024 tokens (also while sessions decode)
+            and a 1024-row token budget, and it ticks until every request has
+            its first token; TTFT is submit -> first sampled token, host clock
+            after the step's synchronising sample call (M:8441-8447).
 `--impl reference` times the CPU oracle (the C restatement of the reference's
 Go step, all host threads) on a bounded sample of the same workload.
 """
@@ -119,7 +127,7 @@ def traffic_per_position():
 class DecodeState:
     """256 sessions in steady decode over one device model and page pool."""
 
-    def __init__(self, cfg, device, warmup, steps, mode, tp=(0, 1, None), workload_rank=0):
+    def __init__(self, cfg, model, warmup, workload_rank=0):
         from sr_go_tranformer_b200 import _abi as A
         from sr_go_tranformer_b200 import step as S
         self.A, self.S, self.cfg = A, S, cfg
@@ -127,11 +135,7 @@ class DecodeState:
         self.prompts, self.outs = prompts, outs
         n = cfg["sessions"]
         pt = cfg["page_tokens"]
-        d = S.make_desc(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
-                        cfg["context"], cfg["rope_theta"], cfg["norm_eps"], cfg["tied"], False, cfg["fmt"], pt)
-        self.model = S.Model(d, device, tp_rank=tp[0], tp_size=tp[1], nccl_id=tp[2])
-        self.model.init_synthetic(cfg["seed"], 0.02)
-        self.model.set_mode(mode)
+        self.model = model
         reserve = int(np.sum((prompts + outs + pt - 1) // pt))
         self.pool = S.PagePool(self.model, reserve)
         self.pool.fill_synthetic(cfg["seed"] + 1, 0.5)
@@ -198,6 +202,44 @@ class DecodeState:
         s = C.c_void_p()
         self.A.check(self.A.lib().sr_model_stream(self.model.h, C.byref(s)))
         return s.value
+
+
+def make_model(cfg, device, mode, tp=(0, 1, None)):
+    from sr_go_tranformer_b200 import step as S
+    d = S.make_desc(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
+                    cfg["context"], cfg["rope_theta"], cfg["norm_eps"], cfg["tied"], False, cfg["fmt"],
+                    cfg["page_tokens"])
+    model = S.Model(d, device, tp_rank=tp[0], tp_size=tp[1], nccl_id=tp[2])
+    model.init_synthetic(cfg["seed"], 0.02)
+    model.set_mode(mode)
+    return model
+
+
+def ttft_phase(cfg, model, workload_rank=0, max_ticks=4000):
+    """Serve the workload's requests from an empty pool until each has its first token."""
+    from sr_go_tranformer_b200.engine import Engine
+    prompts, outs, _, _ = workload(cfg, workload_rank, 0)
+    n, pt, V = cfg["sessions"], cfg["page_tokens"], cfg["vocab"]
+    pages = int(np.sum((prompts + outs + pt - 1) // pt))
+    eng = Engine(model, max_batch=n, token_budget=1024, prefill_chunk=1024, mixed_prefill_chunk=1024,
+                 cache_bytes=pages * model.page_elements * 4)
+    ids_rng = np.random.default_rng(cfg["seed"] + 17)
+    t, k, p, pen = cfg["sampling"]
+    for i in range(n):
+        eng.submit(ids_rng.integers(0, V, size=int(prompts[i])), int(outs[i]), t, k, p, pen, seed=cfg["seed"] + i)
+    t0 = time.time()
+    ticks = rows = 0
+    lat = eng.latency()
+    while lat["first_tokens"] < n and ticks < max_ticks:
+        rows += eng.tick()
+        ticks += 1
+        lat = eng.latency()
+    wall = time.time() - t0
+    st = eng.stats()
+    eng.close()
+    return {"ttft_p50_ms": lat["ttft_p50_ms"], "first_tokens": lat["first_tokens"], "ticks": ticks,
+            "wall_s": wall, "prompt_tokens": int(np.sum(prompts)), "input_tok_s": st["input_tokens"] / wall,
+            "rows": rows, "settings": "prefill chunk 1024 (also while decoding), token budget 1024, max batch 256"}
 
 
 def weight_bytes(cfg):
@@ -275,6 +317,7 @@ def main():
     ap.add_argument("--ref-sessions", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"])
+    ap.add_argument("--no-ttft", action="store_true", help="skip the serving run that measures TTFT")
     args = ap.parse_args()
     cfg = dict(CONFIG)
     cfg["sessions"] = args.sessions
@@ -300,7 +343,8 @@ def main():
             obj = [S.tp_unique_id() if rank == 0 else None]
             dist.broadcast_object_list(obj, src=0)
             tp_args = (rank, world, obj[0])
-    st = DecodeState(cfg, local, W, K, args.mode, tp=tp_args, workload_rank=0 if tp else rank)
+    model = make_model(cfg, local, args.mode, tp=tp_args)
+    st = DecodeState(cfg, model, W, workload_rank=0 if tp else rank)
     for _ in range(W):
         st.step()
     ext = torch.cuda.ExternalStream(st.stream())
@@ -321,6 +365,7 @@ def main():
     torch.cuda.synchronize()
     clocks = clocks_stop(clk, tmp)
     e2e_ms = e0.elapsed_time(e1)
+    ctx_trace, h2d, d2h = list(st.ctx_trace), st.h2d_bytes, st.d2h_bytes  # the timed steps only
     ms, launches, span_ms, nsteps, total_launches = st.profile(reset=True)
     st.set_profile(0)
     # Per-class breakdown from a separately profiled step (not timed).
@@ -328,6 +373,10 @@ def main():
     st.step()
     cls_ms, cls_launch, _, _, _ = st.profile(reset=True)
     st.set_profile(0)
+    # The serving run for TTFT comes after the decode measurement (its prefill
+    # steps heat the GPU) and needs the memory of the decode state's KV pool.
+    st.pool.close()
+    ttft = None if args.no_ttft else ttft_phase(cfg, model, workload_rank=0 if tp else rank)
     t = torch.tensor([span_ms, e2e_ms], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -342,7 +391,7 @@ def main():
         kv_pos_bytes = 2 * kvd * 4  # K + V row of one position, one layer
         attn_launches = launches[5]
         attn_ms = ms[5] / max(1, attn_launches)
-        positions = float(np.mean(st.ctx_trace))  # sum over sessions of (pos+1) per step
+        positions = float(np.mean(ctx_trace))  # sum over sessions of (pos+1) per step
         attn_bytes = positions * kv_pos_bytes + 2 * cfg["sessions"] * cfg["dim"] * 4
         achieved = attn_bytes / (attn_ms / 1000.0) / 1e9
         tr = traffic_per_position()
@@ -364,11 +413,11 @@ def main():
                        "kv_state": "synthetic prefilled pages (prompt + decode offset)",
                        "l2": "inputs larger than L2 (KV pool > 100 GB)",
                        "sampling": "T0.8 k40 p0.95 penalty1.1, SplitMix64"},
-            "itl_p50_ms": span_max / K, "ttft_p50_ms": None,
+            "itl_p50_ms": span_max / K, "ttft_p50_ms": ttft["ttft_p50_ms"] if ttft else None,
             "hbm_gbs_step": step_bytes / (span_max / K / 1000.0) / 1e9,
             "algorithmic_bytes_per_step": step_bytes,
             "e2e": {"value": e2e_val, "unit": "output tok/s",
-                    "h2d_bytes_per_step": st.h2d_bytes // max(1, K), "d2h_bytes_per_step": st.d2h_bytes // max(1, K)},
+                    "h2d_bytes_per_step": h2d // max(1, K), "d2h_bytes_per_step": d2h // max(1, K)},
             "gpu_launches": int(total_launches),
             "roofline": {"kernel": "attention", "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
@@ -377,6 +426,8 @@ def main():
                         for i, n in enumerate(st.A.PROF_CLASSES)},
             "clocks": clocks,
         }
+        if ttft:
+            line["ttft"] = ttft
         if world == 1 and not args.no_cpu_baseline:
             try:
                 cb = cpu_baseline(cfg, args.cpu_sessions, os.cpu_count() or 1)

@@ -273,6 +273,11 @@ int sr_engine_tick(sr_engine *e, int32_t *rows);
 int sr_engine_poll(sr_engine *e, int64_t *request_id, int32_t *out_ids, int32_t cap, int32_t *n_out,
                    int32_t *reason);
 int sr_engine_stats_get(const sr_engine *e, sr_engine_stats *s);
+/* Medians (ms) of the time to first token (submit to first sampled token) and
+ * of the gaps between a request's consecutive tokens, over everything this
+ * engine has produced so far: firstTokenLatency / tokenGap (:8441-8447). */
+int sr_engine_latency(const sr_engine *e, double *ttft_p50_ms, double *itl_p50_ms, int64_t *n_ttft,
+                      int64_t *n_itl);
 /* Last tick's schedule: counts[i] rows for session i (up to cap), pages owned. */
 int sr_engine_last_schedule(const sr_engine *e, int32_t *counts, int32_t cap, int32_t *n_sessions);
 /* Page table of active session i in admission order (up to cap ids). */

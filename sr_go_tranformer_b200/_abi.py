@@ -24,7 +24,7 @@ EXPORTED = [
     "sr_kvpool_fill_synthetic", "sr_step", "sr_step_logits", "sr_sample", "sr_step_sample", "sr_engine_create",
     "sr_engine_destroy", "sr_engine_submit", "sr_engine_tick", "sr_engine_poll", "sr_engine_stats_get",
     "sr_engine_last_schedule", "sr_engine_session_pages", "sr_profile_set", "sr_profile_read", "sr_model_stream",
-    "sr_step_noalloc", "sr_model_create_tp", "sr_tp_unique_id", "sr_tp_shard",
+    "sr_step_noalloc", "sr_model_create_tp", "sr_tp_unique_id", "sr_tp_shard", "sr_engine_latency",
 ]
 PROF_CLASSES = ["meta", "embed", "norm", "linear", "rope_kv", "attention", "swiglu", "head", "sample"]
 
@@ -119,6 +119,8 @@ def lib():
         "sr_engine_tick": (C.c_int, [P, C.POINTER(I32)]),
         "sr_engine_poll": (C.c_int, [P, C.POINTER(I64), P, I32, C.POINTER(I32), C.POINTER(I32)]),
         "sr_engine_stats_get": (C.c_int, [P, C.POINTER(EngineStats)]),
+        "sr_engine_latency": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(I64),
+                                        C.POINTER(I64)]),
         "sr_engine_last_schedule": (C.c_int, [P, P, I32, C.POINTER(I32)]),
         "sr_engine_session_pages": (C.c_int, [P, I32, P, I32, C.POINTER(I32)]),
         "sr_profile_set": (C.c_int, [P, C.c_uint32]),

@@ -7,6 +7,7 @@
 // have no Go runtime (tests, benchmarks).  HTTP, SSE streaming, tokenisation,
 // prefix caching and cancellation watchers are outside this restatement.
 #include <algorithm>
+#include <chrono>
 #include <deque>
 #include <string>
 #include <vector>
@@ -16,12 +17,15 @@
 
 namespace {
 
+using Clock = std::chrono::steady_clock;
+
 struct EngRequest {
   int64_t id;
   std::vector<int32_t> ids;
   int32_t max_tokens;
   sr_sampling s;
   uint64_t seed;
+  Clock::time_point started;  // Request.Started (submit time)
 };
 
 struct EngSession {
@@ -32,6 +36,8 @@ struct EngSession {
   int32_t cursor = 0;          // engineSession.Cursor
   std::vector<int32_t> output, history;
   uint64_t rng = 0;            // engineSession.RNG
+  Clock::time_point last_token;  // engineSession.LastToken
+  bool has_token = false;
 };
 
 struct Finished {
@@ -56,6 +62,8 @@ struct sr_engine {
   std::deque<Finished> finished;
   sr_engine_stats st{};
   std::vector<int32_t> last_counts;
+  // firstTokenLatency / tokenGap observations (M:8441-8447), in seconds
+  std::vector<double> ttft, itl;
   // per-tick scratch
   std::vector<int32_t> pos, toff, tokens, poff, pids, counts, hoff, hist, ids_out;
   std::vector<uint8_t> want;
@@ -170,6 +178,7 @@ extern "C" int sr_engine_submit(sr_engine* e, const sr_request* r, int64_t* requ
   q.max_tokens = r->max_tokens;
   q.s = r->sampling;
   q.seed = r->seed;
+  q.started = Clock::now();
   e->queue.push_back(std::move(q));
   e->st.submitted++;
   *request_id = e->next_id - 1;
@@ -278,6 +287,11 @@ extern "C" int sr_engine_tick(sr_engine* e, int32_t* rows) {
     }
     const int32_t id = e->ids_out[i];
     s.rng = e->rng[i];
+    const Clock::time_point now = Clock::now();  // after the step's synchronising sample call
+    if (!s.has_token) e->ttft.push_back(std::chrono::duration<double>(now - s.req.started).count());
+    else e->itl.push_back(std::chrono::duration<double>(now - s.last_token).count());
+    s.last_token = now;
+    s.has_token = true;
     e->st.generated_tokens++;
     s.output.push_back(id);
     s.history.push_back(id);
@@ -308,6 +322,25 @@ extern "C" int sr_engine_poll(sr_engine* e, int64_t* request_id, int32_t* out_id
   *reason = f.reason;
   *n_out = (int32_t)f.out.size();
   if (out_ids) std::copy(f.out.begin(), f.out.begin() + std::min<size_t>(f.out.size(), (size_t)std::max(cap, 0)), out_ids);
+  return SR_OK;
+}
+
+static double median_ms(std::vector<double> v) {
+  if (v.empty()) return 0.0;
+  const size_t k = v.size() / 2;
+  std::nth_element(v.begin(), v.begin() + k, v.end());
+  double x = v[k];
+  if (v.size() % 2 == 0) x = 0.5 * (x + *std::max_element(v.begin(), v.begin() + k));
+  return 1000.0 * x;
+}
+
+extern "C" int sr_engine_latency(const sr_engine* e, double* ttft_p50_ms, double* itl_p50_ms, int64_t* n_ttft,
+                                 int64_t* n_itl) {
+  if (!e || !ttft_p50_ms || !itl_p50_ms || !n_ttft || !n_itl) return sr_fail(SR_EINVAL, "null argument");
+  *ttft_p50_ms = median_ms(e->ttft);
+  *itl_p50_ms = median_ms(e->itl);
+  *n_ttft = (int64_t)e->ttft.size();
+  *n_itl = (int64_t)e->itl.size();
   return SR_OK;
 }
 

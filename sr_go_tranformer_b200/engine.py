@@ -61,6 +61,12 @@ class Engine:
         A.check(A.lib().sr_engine_stats_get(self.h, C.byref(s)))
         return {k: getattr(s, k) for k, _ in A.EngineStats._fields_}
 
+    def latency(self):
+        """p50 time to first token and p50 inter-token gap (ms) so far, with sample counts."""
+        t, g, nt, ng = C.c_double(), C.c_double(), C.c_int64(), C.c_int64()
+        A.check(A.lib().sr_engine_latency(self.h, C.byref(t), C.byref(g), C.byref(nt), C.byref(ng)))
+        return {"ttft_p50_ms": t.value, "itl_p50_ms": g.value, "first_tokens": nt.value, "gaps": ng.value}
+
     def last_schedule(self, cap=256):
         out = np.zeros(cap, dtype=np.int32)
         n = C.c_int32()

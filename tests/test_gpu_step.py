@@ -309,3 +309,10 @@ def test_engine_matches_oracle_simulation(oracle, srlib):
         assert done[k][1] == want[k][1]
     st = eng.stats()
     assert st["active"] == 0 and st["pool_reserved"] == 0
+    # firstTokenLatency / tokenGap observations (M:8441-8447): one first token per
+    # request that produced any token, one gap for every later token
+    lat = eng.latency()
+    produced = [k for k in want if len(want[k][0]) > 0]
+    assert lat["first_tokens"] == len(produced)
+    assert lat["gaps"] == st["generated_tokens"] - len(produced)
+    assert lat["ttft_p50_ms"] > 0 and lat["itl_p50_ms"] > 0
