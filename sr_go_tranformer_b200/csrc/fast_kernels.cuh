@@ -60,15 +60,22 @@ inline int fast_check(sr_model* m) {
 // ------------------------------------------------------------------ RMSNorm --
 // rmsInto (M:6182-6194) with a block-parallel fp64 sum of squares (reordered).
 // One 128-thread block per row keeps every SM busy at decode batch sizes.
+// With T set (tensor parallel, rows not remapped), the row first takes the
+// all-reduced projection: X += T (addInPlace, M:6405/6418), written back.
 __global__ void __launch_bounds__(128)
-k_rmsnorm_fast(const float* __restrict__ X, const int32_t* __restrict__ src_map, const float* __restrict__ w,
+k_rmsnorm_fast(float* __restrict__ X, const int32_t* __restrict__ src_map, const float* __restrict__ w,
                float* __restrict__ Y, int rows, int d, double eps, __nv_bfloat16* __restrict__ yh,
-               __nv_bfloat16* __restrict__ yl) {
+               __nv_bfloat16* __restrict__ yl, const float* __restrict__ T) {
   __shared__ double red[4];
   const int r = blockIdx.x;
   const int srow = src_map ? src_map[r] : r;
-  const float* x = X + (int64_t)srow * d;
+  float* x = X + (int64_t)srow * d;
   const bool vec = (d & 3) == 0;
+  if (T) {
+    const float* t = T + (int64_t)srow * d;
+    for (int j = threadIdx.x; j < d; j += 128) x[j] += t[j];
+    __syncthreads();
+  }
   double ss = 0.0;
   if (vec) {
     for (int j = threadIdx.x * 4; j < d; j += 512) {
@@ -110,9 +117,10 @@ k_rmsnorm_fast(const float* __restrict__ X, const int32_t* __restrict__ src_map,
   }
 }
 
-inline void fast_rmsnorm(sr_model* m, const float* X, const int32_t* src_map, const float* w, float* Y, int rows,
-                         int d, double eps, __nv_bfloat16* yh = nullptr, __nv_bfloat16* yl = nullptr) {
-  k_rmsnorm_fast<<<rows, 128, 0, m->stream>>>(X, src_map, w, Y, rows, d, eps, yh, yl);
+inline void fast_rmsnorm(sr_model* m, float* X, const int32_t* src_map, const float* w, float* Y, int rows, int d,
+                         double eps, __nv_bfloat16* yh = nullptr, __nv_bfloat16* yl = nullptr,
+                         const float* T = nullptr) {
+  k_rmsnorm_fast<<<rows, 128, 0, m->stream>>>(X, src_map, w, Y, rows, d, eps, yh, yl, T);
 }
 
 // SwiGLU h = g/(1+exp(-g)) * u in fp32 (M:6410-6413 reordered), written as the

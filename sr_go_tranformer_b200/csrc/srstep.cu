@@ -784,21 +784,26 @@ static void launch_attention_exact(sr_model* m, sr_kvpool* pool, int n, int max_
   sr_count_launch(m);
 }
 
-// X += T after summing every rank's partial T over NCCL (the exchange after
-// o_proj and down_proj of the tensor-parallel step).
+// The exchange after o_proj and down_proj of the tensor-parallel step: every
+// rank's partial T is summed in place over NCCL.  The residual add X += T is
+// then folded into the next fast-mode RMSNorm (k_rmsnorm_fast with T), or done
+// by k_add_inplace where no norm follows directly.
 __global__ void k_add_inplace(float* __restrict__ X, const float* __restrict__ T, int64_t count) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
     X[i] += T[i];
 }
-static int tp_allreduce_add(sr_model* m, int n) {
+static int tp_allreduce(sr_model* m, int n) {
   nccl::Api& api = nccl::api();
   const int64_t count = (int64_t)n * m->dm.dim;
   const int r = api.AllReduce(m->T, m->T, (size_t)count, nccl::kFloat32, nccl::kSum, (nccl::Comm)m->nccl_comm,
                               m->stream);
   if (r != nccl::kSuccess) return sr_fail(SR_EDEVICE, std::string("ncclAllReduce: ") + api.GetErrorString(r));
+  return SR_OK;
+}
+static void tp_add(sr_model* m, int n) {
+  const int64_t count = (int64_t)n * m->dm.dim;
   k_add_inplace<<<(int)std::min<int64_t>((count + 255) / 256, 148 * 8), 256, 0, m->stream>>>(m->X, m->T, count);
   sr_count_launch(m);
-  return SR_OK;
 }
 
 int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel,
@@ -821,6 +826,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   int rc = SR_OK;
   __nv_bfloat16* xh = tc ? tc_xh(m) : nullptr;
   __nv_bfloat16* xl = tc ? tc_xl(m) : nullptr;
+  bool pending = false;  // tensor parallel: the all-reduced T is still to be added to X
   for (int l = 0; l < L; l++) {
     if (cancel && *cancel) {
       sr_prof_span_end(m);
@@ -834,9 +840,12 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     o.ldy = 0;
     o.resid = nullptr;
     o.out_map = nullptr;
+    if (pending && !fast) tp_add(m, n);
     SR_LAUNCH(m, SR_PROF_NORM,
-              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps, xh, xl);
+              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps, xh, xl,
+                                     pending ? m->T : nullptr);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps));
+    pending = false;
     bool done;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_qkv(m, l, n, true));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
@@ -864,9 +873,13 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_o(m, l, n, a_split, oy, ores));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->A, n, P[4], o);
-    if (tp && (rc = tp_allreduce_add(m, n)) != SR_OK) return rc;
+    if (tp) {
+      if ((rc = tp_allreduce(m, n)) != SR_OK) return rc;
+      if (!fast) tp_add(m, n);
+    }
     SR_LAUNCH(m, SR_PROF_NORM,
-              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps, xh, xl);
+              if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps, xh, xl,
+                                     tp ? m->T : nullptr);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps));
     o.resid = nullptr;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_gateup(m, l, n, true));
@@ -887,8 +900,12 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_down(m, l, n, true, oy, ores));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->H, n, P[8], o);
-    if (tp && (rc = tp_allreduce_add(m, n)) != SR_OK) return rc;
+    if (tp) {
+      if ((rc = tp_allreduce(m, n)) != SR_OK) return rc;
+      pending = true;
+    }
   }
+  if (pending) tp_add(m, n);  // the final norm below gathers the head rows: a plain add
   // Selected head (M:6420-6448): gather last rows, final norm, LM head into
   // the session's logits row; unselected rows are zero.
   CK(cudaMemsetAsync(m->logits, 0, (size_t)info.sessions * dm.vocab * 4, s));

@@ -1,4 +1,4 @@
-"""Tensor-parallel step on 2 GPUs against the single-GPU step (needs 2 GPUs).
+"""Tensor-parallel step on 2 (and 4) GPUs against the single-GPU step.
 
 Each rank holds its shard of the same synthetic model (the counter-based init
 generates every rank's part of one full model) and the step all-reduces the
@@ -71,14 +71,17 @@ def _single_logits(mode):
     return r[1]
 
 
-@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("size", [2, 4])
 @pytest.mark.parametrize("mode", ["exact", "fast"])
-def test_tp2_matches_single_gpu(mode):
-    tp = _tp_logits(2, mode)
+def test_tp_matches_single_gpu(mode, size):
+    if _gpus() < size:
+        pytest.skip(f"needs {size} GPUs")
+    tp = _tp_logits(size, mode)
     single = _single_logits(mode)
     for step in range(len(single)):
-        a0, a1, b = tp[0][step], tp[1][step], single[step]
-        assert np.array_equal(a0, a1), "ranks disagree"  # replicated head on the same reduced residual
-        err = float(np.abs(a0 - b).max())
-        assert err <= ATOL, f"{mode} step {step}: TP2 logits differ from 1 GPU by {err:.3g}"
-        assert (np.argmax(a0, 1) == np.argmax(b, 1)).mean() >= 0.75
+        b = single[step]
+        for r in range(1, size):
+            assert np.array_equal(tp[0][step], tp[r][step]), "ranks disagree"  # replicated head, same residual
+        err = float(np.abs(tp[0][step] - b).max())
+        assert err <= ATOL, f"{mode} step {step}: TP{size} logits differ from 1 GPU by {err:.3g}"
+        assert (np.argmax(tp[0][step], 1) == np.argmax(b, 1)).mean() >= 0.75
