@@ -148,7 +148,10 @@ class DecodeState:
                 self.pages[i].append(self.pool.acquire())
         self.page_arr = [np.asarray(p, dtype=np.int32) for p in self.pages]
         V = cfg["vocab"]
-        self.hist = [rng.integers(0, V, size=int(self.pos[i])).astype(np.int32) for i in range(n)]
+        hist = [rng.integers(0, V, size=int(self.pos[i])).astype(np.int32) for i in range(n)]
+        self.hist = np.concatenate(hist)  # every session's history, back to back
+        self.hoff = np.zeros(n + 1, dtype=np.int32)
+        self.hoff[1:] = np.cumsum([len(h) for h in hist])
         self.last = rng.integers(0, V, size=n).astype(np.int32)
         self.rng_state = np.array([cfg["seed"] + i for i in range(n)], dtype=np.uint64)
         t, k, p, pen = cfg["sampling"]
@@ -169,9 +172,7 @@ class DecodeState:
         poff = np.zeros(n + 1, dtype=np.int32)
         poff[1:] = np.cumsum([len(p) for p in self.pages])
         pids = np.concatenate(self.page_arr)
-        hoff = np.zeros(n + 1, dtype=np.int32)
-        hoff[1:] = np.cumsum([len(h) for h in self.hist])
-        hist = np.concatenate(self.hist)
+        hoff, hist = self.hoff, self.hist
         b = A.Batch(n, self.pos.ctypes.data, self.toff.ctypes.data, self.last.ctypes.data, poff.ctypes.data,
                     pids.ctypes.data, None)
         self.ctx_trace.append(int(np.sum(self.pos.astype(np.int64) + 1)))
@@ -181,8 +182,8 @@ class DecodeState:
         # bytes crossing the host boundary this step (sr_upload_batch + sampler staging)
         self.h2d_bytes += 4 * (1864 + pids.size) + n * 32 + 4 * (n + 1) + 4 * hist.size + 8 * n
         self.d2h_bytes += 8 * n + 4 * n + 4 * n
-        for i in range(n):
-            self.hist[i] = np.append(self.hist[i], self.ids[i])
+        self.hist = np.insert(hist, hoff[1:], self.ids)  # append each session's new id
+        self.hoff = hoff + np.arange(n + 1, dtype=np.int32)
         self.pos += 1
         self.last[:] = self.ids
 

@@ -10,7 +10,6 @@
 #include <cstring>
 #include <mutex>
 #include <string>
-#include <unordered_map>
 #include <vector>
 
 #include "../../include/srstep.h"
@@ -677,27 +676,30 @@ int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* 
   }
   // A page this step writes must belong to exactly one session (the reference
   // rejects duplicate caches, M:6264-6266; shared prefix pages are read-only).
+  // pool->owner is indexed by page id (ids were range-checked above).
   {
-    std::unordered_map<int32_t, int> owner;
-    owner.reserve((size_t)b->page_offsets[S] * 2);
+    std::vector<int32_t>& owner = const_cast<sr_kvpool*>(pool)->owner;
+    if ((int64_t)owner.size() != pool->num_pages) owner.assign((size_t)pool->num_pages, -2);
+    const int64_t np_all = b->page_offsets[S];
     for (int i = 0; i < S; i++)
       for (int64_t j = b->page_offsets[i]; j < b->page_offsets[i + 1]; j++) {
-        auto it = owner.find(b->page_ids[j]);
-        if (it == owner.end())
-          owner.emplace(b->page_ids[j], i);
-        else if (it->second != i)
-          it->second = -1;  // listed by several sessions
+        int32_t& o = owner[b->page_ids[j]];
+        if (o == -2) o = i;
+        else if (o != i) o = -1;  // listed by several sessions
       }
-    for (int i = 0; i < S; i++) {
+    const char* err = nullptr;
+    for (int i = 0; i < S && !err; i++) {
       int64_t len = (int64_t)b->token_offsets[i + 1] - b->token_offsets[i];
       int64_t first = b->pos[i] / pt, last = (b->pos[i] + len - 1) / pt;
-      for (int64_t pg = first; pg <= last; pg++) {
+      for (int64_t pg = first; pg <= last && !err; pg++) {
         int32_t id = b->page_ids[b->page_offsets[i] + pg];
-        if (owner[id] != i) return sr_fail(SR_EINVAL, "a written KV page is shared with another session");
-        for (int64_t q = b->page_offsets[i]; q < b->page_offsets[i] + pg; q++)
-          if (b->page_ids[q] == id) return sr_fail(SR_EINVAL, "duplicate page in one session's page table");
+        if (owner[id] != i) err = "a written KV page is shared with another session";
+        for (int64_t q = b->page_offsets[i]; q < b->page_offsets[i] + pg && !err; q++)
+          if (b->page_ids[q] == id) err = "duplicate page in one session's page table";
       }
     }
+    for (int64_t j = 0; j < np_all; j++) owner[b->page_ids[j]] = -2;  // leave the scratch clear
+    if (err) return sr_fail(SR_EINVAL, err);
   }
   // resizeInferenceArrays bound (M:6149-6174) with maxActivationElements (M:50),
   // counting one attention lane.

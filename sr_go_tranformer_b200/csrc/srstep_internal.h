@@ -92,6 +92,7 @@ struct sr_kvpool {
   sr_model* m = nullptr;
   int64_t num_pages = 0;
   float* data = nullptr;
+  std::vector<int32_t> owner;  // validation scratch: session listing each page (-2: none), reset after use
 };
 
 int sr_fail(int code, const std::string& msg);
