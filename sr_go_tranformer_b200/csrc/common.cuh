@@ -9,7 +9,7 @@ namespace sr {
 constexpr int kQBlock = 64;          // q8Block: 64 columns per scale (monolith.go:3793)
 constexpr int kMaxRows = 1024;       // rows per step (monolith.go:6275)
 constexpr int kMaxSessions = 256;    // sessions per step (monolith.go:6248)
-constexpr int kAttnSplit = 256;      // positions per split-K attention item (fast mode)
+constexpr int kAttnSplit = 512;      // positions per split-K attention item (fast mode)
 
 enum ParamFormat { kF32 = 0, kQ8 = 1, kQ4 = 2 };
 

@@ -16,7 +16,7 @@ namespace sr {
 // ---------------------------------------------------------------- metadata --
 // Ragged-batch metadata (M:6361-6375, 6420-6427): per row the session position
 // and page-table base; per selected session its last row (compacted head); and
-// the compact list of (row, 256-position split) items that the fast-mode
+// the compact list of (row, kAttnSplit-position split) items that the fast-mode
 // attention launches one CTA per KV head for.
 __global__ void __launch_bounds__(1024) k_meta(StepMeta m, int sessions, int rows) {
   __shared__ int warp_sum[32];

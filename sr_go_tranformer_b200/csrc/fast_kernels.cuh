@@ -212,7 +212,7 @@ inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int r
   if (o_bytes > ((size_t)1 << 30)) return false;
   if (items > st->items_cap) {
     // Grow by half again (within the 1 GiB cap): the item count creeps up as
-    // contexts cross 256-position boundaries, and every reallocation
+    // contexts cross split boundaries, and every reallocation
     // synchronises the device.
     const size_t unit_o = (size_t)dm.group * dm.hd * 4;
     const size_t cap = std::max(items, std::min(st->items_cap + st->items_cap / 2, ((size_t)1 << 30) / unit_o));

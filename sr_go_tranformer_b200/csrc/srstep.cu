@@ -320,7 +320,7 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
   m->page_cap = (int64_t)kMaxSessions * m->max_pages_per_session;
   m->upload_ints = kMetaHeader + m->page_cap;
   // computed region: per-row data, head maps, then the attention item table
-  // (at most ceil(context / 256) items for each of the 1024 rows)
+  // (at most ceil(context / kAttnSplit) items for each of the 1024 rows)
   const int64_t item_cap = (int64_t)kMaxRows * ((c.context + kAttnSplit - 1) / kAttnSplit);
   const int64_t meta_ints = m->upload_ints + kMetaComputed + kMaxRows + item_cap;
   if ((rc = sr_model_alloc(m, (void**)&m->meta_dev, (size_t)meta_ints * 4)) != SR_OK) { free_model(m); return rc; }
@@ -1166,7 +1166,7 @@ extern "C" int sr_model_stream(sr_model* m, void** stream) {
 // up front (the reference plans its page budget before admitting anything),
 // or an embedding runtime that owns every device allocation itself.  Its only
 // scratch -- the split-K attention partials (unnormalised outputs and the
-// (max, sum) pair of every row x KV head x 256-position split) -- lives in this
+// (max, sum) pair of every row x KV head x split of kAttnSplit positions) -- lives in this
 // file-scope device array, which every GPU that loads the library holds until
 // the process exits.  All calls on a device share it and it keeps the last
 // call's contents; nothing in it needs to start at zero, because each call

@@ -35,7 +35,7 @@ static_assert(kSampOffRng % 16 == 0, "RNG states must be 8-byte aligned");
 struct BatchInfo {
   int sessions, rows, max_len, heads;
   int64_t pages;
-  int attn_items;  // (row, 256-position split) pairs of the split-K attention
+  int attn_items;  // (row, kAttnSplit-position split) pairs of the split-K attention
 };
 
 // Event-based per-kernel-class timing on the model's stream.

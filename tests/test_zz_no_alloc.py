@@ -63,12 +63,12 @@ def test_noalloc_step_matches_step(srlib):
 def test_noalloc_step_rejects_oversized_scratch(srlib):
     from sr_go_tranformer_b200 import _abi as A
     from sr_go_tranformer_b200 import step as S
-    desc = S.make_desc(512, 256, 384, 2, 4, 2, 8192, rope_theta=1e5, tied=True, weight_format="q8", page_tokens=32)
+    desc = S.make_desc(512, 512, 384, 2, 8, 4, 8192, rope_theta=1e5, tied=True, weight_format="q8", page_tokens=32)
     model = S.Model(desc)
     model.init_synthetic(32)
     pool = S.PagePool(model, 256)
-    # 1024 rows at positions 7168..8191 cover 31,232 (row, 256-position split) items;
-    # x 2 KV heads x 2 query heads x 66 floats = 33 MB > 16 MiB
+    # 1024 rows at positions 7168..8191 cover 15,872 (row, 512-position split) items;
+    # x 4 KV heads x 2 query heads x 66 floats = 33.5 MB > 16 MiB
     k0, v0 = pool.read_row(0, 0, 0)
     b, keep = _batch(A, [7168], [[i % 512 for i in range(1024)]], [list(range(256))])
     rc = srlib.sr_step_noalloc(model.h, pool.h, C.byref(b), None)
