@@ -10,7 +10,7 @@
 // path within fp32 rounding (tolerance-checked), not bit for bit.
 //
 // head_dim 128 (Mistral, Qwen): k_attn_warp128 -- each of the 4 warps streams
-//   its own 64-position sub-split through a private 2-stage ring of
+//   its own sub-split (a quarter of the split) through a private 2-stage ring of
 //   8-position tiles (one 512-byte bulk copy per K or V row, issued by the
 //   row's lane, completing on the warp's mbarrier) and keeps its own softmax
 //   state, synchronising with __syncwarp only; the warps merge once at the
