@@ -50,6 +50,9 @@ struct StepMeta {
   int32_t* n_heads;     // [1]
   int32_t* row_item0;   // [rows] first attention item of the row
   int32_t* item_rs;     // [items] attention item -> (row << 16) | split
+  int32_t* single_rs;   // items of rows from 1-token chunks (decode): (row << 16) | split
+  int32_t* grp_rs;      // groups of up to 4 consecutive rows of a longer chunk:
+                        // (first row << 16) | ((rows - 1) << 13) | split
 };
 
 // Per-device model dimensions.  With tensor parallelism, heads, kv_heads,

@@ -14,14 +14,44 @@
 namespace sr {
 
 // ---------------------------------------------------------------- metadata --
+// Exclusive prefix sum over the 1024 threads of k_meta (one value per thread);
+// *total receives the sum.  Uses ws[32] of shared memory.
+__device__ __forceinline__ int meta_scan(int v, int* ws, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int x = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += x;
+  }
+  if (lane == 31) ws[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = ws[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += x;
+    }
+    ws[lane] = w;  // inclusive totals of warps 0..lane
+  }
+  __syncthreads();
+  const int excl = incl - v + (warp > 0 ? ws[warp - 1] : 0);
+  *total = ws[31];
+  __syncthreads();  // ws is reused by the next scan
+  return excl;
+}
+
 // Ragged-batch metadata (M:6361-6375, 6420-6427): per row the session position
 // and page-table base; per selected session its last row (compacted head); and
-// the compact list of (row, kAttnSplit-position split) items that the fast-mode
-// attention launches one CTA per KV head for.
+// the fast-mode attention's work lists: every (row, kAttnSplit-position split)
+// item (row_item0 / item_rs: where each row's split partials live), the items
+// of rows from 1-token chunks (single_rs), and (group of up to 4 consecutive
+// rows of a longer chunk, split) pairs (grp_rs), whose rows share K/V reads.
 __global__ void __launch_bounds__(1024) k_meta(StepMeta m, int sessions, int rows) {
-  __shared__ int warp_sum[32];
+  __shared__ int ws[32];
   const int r = threadIdx.x;  // rows <= 1024 = blockDim.x: one row per thread
-  int ns = 0;
+  int ns = 0, nsa = 0, nsb = 0, grp = 0;
   if (r < rows) {
     int lo = 0, hi = sessions - 1;
     while (lo < hi) {
@@ -32,31 +62,23 @@ __global__ void __launch_bounds__(1024) k_meta(StepMeta m, int sessions, int row
     m.row_pos[r] = pos;
     m.row_pbase[r] = m.page_off[lo];
     ns = (pos + 1 + kAttnSplit - 1) / kAttnSplit;
-  }
-  // exclusive scan of the rows' attention item counts
-  const int lane = r & 31, warp = r >> 5;
-  int incl = ns;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, off);
-    if (lane >= off) incl += v;
-  }
-  if (lane == 31) warp_sum[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    int w = warp_sum[lane];
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, w, off);
-      if (lane >= off) w += v;
+    const int len = m.tok_off[lo + 1] - m.tok_off[lo], k = r - m.tok_off[lo];
+    if (len == 1) {
+      nsa = ns;
+    } else if ((k & 3) == 0) {
+      grp = min(4, len - k);
+      nsb = (pos + grp + kAttnSplit - 1) / kAttnSplit;  // the group's last row reaches pos + grp
     }
-    warp_sum[lane] = w;  // inclusive totals of warps 0..lane
   }
-  __syncthreads();
-  const int base = incl - ns + (warp > 0 ? warp_sum[warp - 1] : 0);
+  int total;
+  const int base = meta_scan(ns, ws, &total);
+  const int base_a = meta_scan(nsa, ws, &total);
+  const int base_b = meta_scan(nsb, ws, &total);
   if (r < rows) {
     m.row_item0[r] = base;
     for (int s = 0; s < ns; s++) m.item_rs[base + s] = (r << 16) | s;
+    for (int s = 0; s < nsa; s++) m.single_rs[base_a + s] = (r << 16) | s;
+    for (int s = 0; s < nsb; s++) m.grp_rs[base_b + s] = (r << 16) | ((grp - 1) << 13) | s;
   }
   if (threadIdx.x == 0) {
     int h = 0;

@@ -85,12 +85,120 @@ struct WarpSmem {
   static constexpr size_t BYTES = (size_t)TOTAL * 4 + 4 * 2 * 8;
 };
 
+// One 8-position tile of a warp's online-softmax attention for the G query
+// heads of a KV head (head_dim 128): scores with 8 lanes per position, the
+// softmax state (mreg, lreg: head lane/8 + 4*round, replicated in its 8 lanes)
+// and the output (acc[g]: dims 4*lane..4*lane+3) updated in place.  kt / vt:
+// the tile's K and V rows in shared memory; tn <= 8 valid positions; sc / ps:
+// the warp's score and probability scratch.
+template <int G>
+__device__ __forceinline__ void warp_tile8(const float* kt, const float* vt, int tn, const float4 (&q)[G][4],
+                                           float (&mreg)[(G + 3) / 4], float (&lreg)[(G + 3) / 4], float4 (&acc)[G],
+                                           float* sc, float* ps, int lane) {
+  constexpr int HD = 128, MT = kWpMT, GP = (G + 3) & ~3;
+  constexpr int ROUNDS = (G + 3) / 4;
+  // scores: 8 lanes per position, 4 positions per pass, 2 passes
+#pragma unroll
+  for (int pass = 0; pass < 2; pass++) {
+    const int s = pass * 4 + (lane >> 3);
+    float part[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) part[g] = 0.f;
+    if (s < tn) {
+      const float* kr = kt + s * HD + 4 * (lane & 7);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float4 kx = *(const float4*)(kr + 32 * i);
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          part[g] = fmaf(q[g][i].x, kx.x, part[g]);
+          part[g] = fmaf(q[g][i].y, kx.y, part[g]);
+          part[g] = fmaf(q[g][i].z, kx.z, part[g]);
+          part[g] = fmaf(q[g][i].w, kx.w, part[g]);
+        }
+      }
+    }
+    if constexpr (G == 4) {
+      // reduce-scatter over the 8 lanes of the position: after the three
+      // exchanges lane bits (b0, b1) hold head 2*b0 + b1 (4 shuffles, not 12)
+      const bool b0 = lane & 1, b1 = lane & 2;
+      float k0 = b0 ? part[2] : part[0], k1 = b0 ? part[3] : part[1];
+      const float x0 = b0 ? part[0] : part[2], x1 = b0 ? part[1] : part[3];
+      k0 += __shfl_xor_sync(0xffffffffu, x0, 1);
+      k1 += __shfl_xor_sync(0xffffffffu, x1, 1);
+      float kk = b1 ? k1 : k0;
+      kk += __shfl_xor_sync(0xffffffffu, b1 ? k0 : k1, 2);
+      kk += __shfl_xor_sync(0xffffffffu, kk, 4);
+      if ((lane & 4) == 0) sc[(2 * (int)b0 + (int)b1) * MT + s] = s < tn ? kk : -INFINITY;
+    } else {
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1)
+#pragma unroll
+        for (int g = 0; g < G; g++) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+      if ((lane & 7) == 0)
+#pragma unroll
+        for (int g = 0; g < G; g++) sc[g * MT + s] = s < tn ? part[g] : -INFINITY;
+    }
+  }
+  __syncwarp();
+  // online softmax: lane = (head lane/8 + 4*round, position lane%8)
+  float alpha[ROUNDS];
+#pragma unroll
+  for (int k = 0; k < ROUNDS; k++) {
+    const int g = (lane >> 3) + 4 * k;
+    const float v = g < G ? sc[g * MT + (lane & 7)] : -INFINITY;
+    float mt = v;
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+    const float mo = mreg[k];
+    const float mn = fmaxf(mo, mt);
+    const float p = (v == -INFINITY) ? 0.f : __expf(v - mn);
+    float sum = p;
+#pragma unroll
+    for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const float al = (mo == -INFINITY) ? 0.f : __expf(mo - mn);
+    lreg[k] = lreg[k] * al + sum;
+    mreg[k] = mn;
+    alpha[k] = al;
+    if (g < G) ps[(lane & 7) * GP + g] = p;
+  }
+  __syncwarp();
+  // rescale and accumulate P.V: lane owns dims 4*lane..4*lane+3
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    const float al = __shfl_sync(0xffffffffu, alpha[g / 4], (g % 4) * 8);
+    acc[g].x *= al;
+    acc[g].y *= al;
+    acc[g].z *= al;
+    acc[g].w *= al;
+  }
+  for (int s = 0; s < tn; s++) {
+    const float4 v = *(const float4*)(vt + s * HD + 4 * lane);
+    const float* pp = ps + s * GP;
+#pragma unroll
+    for (int g4 = 0; g4 < GP; g4 += 4) {
+      const float4 p4 = *(const float4*)(pp + g4);
+      const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (g4 + j < G) {
+          acc[g4 + j].x = fmaf(pv[j], v.x, acc[g4 + j].x);
+          acc[g4 + j].y = fmaf(pv[j], v.y, acc[g4 + j].y);
+          acc[g4 + j].z = fmaf(pv[j], v.z, acc[g4 + j].z);
+          acc[g4 + j].w = fmaf(pv[j], v.w, acc[g4 + j].w);
+        }
+      }
+    }
+  }
+}
+
+// grid: the step's single-row items (rows of 1-token chunks) x KV heads
 template <int G>
 __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
   constexpr int HD = 128, MT = kWpMT, GP = WarpSmem<G>::GP;
   constexpr int ROUNDS = (G + 3) / 4;  // softmax passes: 4 heads x 8 positions per pass
   extern __shared__ __align__(16) float fsm[];
-  const int rs = a.meta.item_rs[blockIdx.x], kh = blockIdx.y;
+  const int rs = a.meta.single_rs[blockIdx.x], kh = blockIdx.y;
   const int r = rs >> 16, split = rs & 0xffff;
   const int L = a.meta.row_pos[r] + 1;
   const int s0 = split * kFaSplit;
@@ -173,99 +281,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
     const float* kt = kv + (t & 1) * 2 * MT * HD;
     const float* vt = kt + MT * HD;
     const int tn = min(MT, ws1 - (ws0 + t * MT));
-    // scores: 8 lanes per position, 4 positions per pass, 2 passes
-#pragma unroll
-    for (int pass = 0; pass < 2; pass++) {
-      const int s = pass * 4 + (lane >> 3);
-      float part[G];
-#pragma unroll
-      for (int g = 0; g < G; g++) part[g] = 0.f;
-      if (s < tn) {
-        const float* kr = kt + s * HD + 4 * (lane & 7);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const float4 kx = *(const float4*)(kr + 32 * i);
-#pragma unroll
-          for (int g = 0; g < G; g++) {
-            part[g] = fmaf(q[g][i].x, kx.x, part[g]);
-            part[g] = fmaf(q[g][i].y, kx.y, part[g]);
-            part[g] = fmaf(q[g][i].z, kx.z, part[g]);
-            part[g] = fmaf(q[g][i].w, kx.w, part[g]);
-          }
-        }
-      }
-      if constexpr (G == 4) {
-        // reduce-scatter over the 8 lanes of the position: after the three
-        // exchanges lane bits (b0, b1) hold head 2*b0 + b1 (4 shuffles, not 12)
-        const bool b0 = lane & 1, b1 = lane & 2;
-        float k0 = b0 ? part[2] : part[0], k1 = b0 ? part[3] : part[1];
-        const float x0 = b0 ? part[0] : part[2], x1 = b0 ? part[1] : part[3];
-        k0 += __shfl_xor_sync(0xffffffffu, x0, 1);
-        k1 += __shfl_xor_sync(0xffffffffu, x1, 1);
-        float kk = b1 ? k1 : k0;
-        kk += __shfl_xor_sync(0xffffffffu, b1 ? k0 : k1, 2);
-        kk += __shfl_xor_sync(0xffffffffu, kk, 4);
-        if ((lane & 4) == 0) sc[(2 * (int)b0 + (int)b1) * MT + s] = s < tn ? kk : -INFINITY;
-      } else {
-#pragma unroll
-        for (int off = 1; off < 8; off <<= 1)
-#pragma unroll
-          for (int g = 0; g < G; g++) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
-        if ((lane & 7) == 0)
-#pragma unroll
-          for (int g = 0; g < G; g++) sc[g * MT + s] = s < tn ? part[g] : -INFINITY;
-      }
-    }
-    __syncwarp();
-    // online softmax: lane = (head lane/8 + 4*round, position lane%8)
-    float alpha[ROUNDS];
-#pragma unroll
-    for (int k = 0; k < ROUNDS; k++) {
-      const int g = (lane >> 3) + 4 * k;
-      const float v = g < G ? sc[g * MT + (lane & 7)] : -INFINITY;
-      float mt = v;
-#pragma unroll
-      for (int off = 1; off < 8; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
-      const float mo = mreg[k];
-      const float mn = fmaxf(mo, mt);
-      const float p = (v == -INFINITY) ? 0.f : __expf(v - mn);
-      float sum = p;
-#pragma unroll
-      for (int off = 1; off < 8; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      const float al = (mo == -INFINITY) ? 0.f : __expf(mo - mn);
-      lreg[k] = lreg[k] * al + sum;
-      mreg[k] = mn;
-      alpha[k] = al;
-      if (g < G) ps[(lane & 7) * GP + g] = p;
-    }
-    __syncwarp();
-    // rescale and accumulate P.V: lane owns dims 4*lane..4*lane+3
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-      const float al = __shfl_sync(0xffffffffu, alpha[g / 4], (g % 4) * 8);
-      acc[g].x *= al;
-      acc[g].y *= al;
-      acc[g].z *= al;
-      acc[g].w *= al;
-    }
-    for (int s = 0; s < tn; s++) {
-      const float4 v = *(const float4*)(vt + s * HD + 4 * lane);
-      const float* pp = ps + s * GP;
-#pragma unroll
-      for (int g4 = 0; g4 < GP; g4 += 4) {
-        const float4 p4 = *(const float4*)(pp + g4);
-        const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          if (g4 + j < G) {
-            acc[g4 + j].x = fmaf(pv[j], v.x, acc[g4 + j].x);
-            acc[g4 + j].y = fmaf(pv[j], v.y, acc[g4 + j].y);
-            acc[g4 + j].z = fmaf(pv[j], v.z, acc[g4 + j].z);
-            acc[g4 + j].w = fmaf(pv[j], v.w, acc[g4 + j].w);
-          }
-        }
-      }
-    }
+    warp_tile8<G>(kt, vt, tn, q, mreg, lreg, acc, sc, ps, lane);
   }
   // merge the 4 warps of the split: O_w, m_w, l_w -> (O, m, l)
   __syncthreads();
@@ -303,7 +319,140 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
     }
   }
   __syncthreads();
-  fa_write_split(a, blockIdx.x, kh, G, HD, out, out + G * HD);
+  fa_write_split(a, a.meta.row_item0[r] + split, kh, G, HD, out, out + G * HD);
+}
+
+// ============================================ head_dim 128: rows of a chunk
+// Prefill chunks: one CTA per (group of up to 4 consecutive rows of one
+// session, split), one warp per row.  The split's K/V rows are loaded once into
+// a CTA ring of 16-position tiles that all warps read (a row at position p
+// sees positions < p + 1 of the same pages), so the group reads its prefix
+// once instead of once per row.  Warp 0's lanes issue the bulk copies; each
+// warp releases a stage through the empty barrier; every wait is bounded.
+constexpr int kRwTile = 16;
+constexpr int kRwStages = 3;
+template <int G>
+struct RowsSmem {
+  static constexpr int HD = 128;
+  static constexpr int GP = (G + 3) & ~3;
+  static constexpr int KV = kRwStages * 2 * kRwTile * HD;  // [stage][K|V][pos][HD]
+  static constexpr int PER_WARP = G * kWpMT + kWpMT * GP;  // scores, probabilities
+  static constexpr int TOTAL = KV + 4 * PER_WARP;            // floats, then full and empty barriers
+  static constexpr size_t BYTES = (size_t)TOTAL * 4 + 2 * kRwStages * 8;
+};
+
+// grid: the step's row groups x KV heads
+template <int G>
+__global__ void __launch_bounds__(kFaThreads) k_attn_rows128(FastAttnArgs a) {
+  constexpr int HD = 128, RT = kRwTile, NS = kRwStages;
+  constexpr int ROUNDS = (G + 3) / 4;
+  extern __shared__ __align__(16) float fsm[];
+  const int gr = a.meta.grp_rs[blockIdx.x], kh = blockIdx.y;
+  const int r0 = gr >> 16, nr = ((gr >> 13) & 7) + 1, split = gr & 0x1fff;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int s0 = split * kFaSplit;
+  const int s1 = min(a.meta.row_pos[r0 + nr - 1] + 1, s0 + kFaSplit);  // the group's last row reaches furthest
+  const int r = r0 + min(warp, nr - 1);
+  const int er = min(s1, a.meta.row_pos[r] + 1);  // this warp's row: positions [s0, er)
+  const bool has = warp < nr && er > s0;
+  float* kv = fsm;
+  float* sc = fsm + RowsSmem<G>::KV + warp * RowsSmem<G>::PER_WARP;
+  float* ps = sc + G * kWpMT;
+  uint64_t* full = (uint64_t*)(fsm + RowsSmem<G>::TOTAL);
+  uint64_t* empty = full + NS;
+  const int pbase = a.meta.row_pbase[r0];
+  const int pt = a.dm.page_tokens;
+  const int64_t lay = (int64_t)a.layer * 2 * pt * a.dm.kvd + (int64_t)kh * HD;
+  const int64_t vofs = (int64_t)pt * a.dm.kvd;
+  const int ntiles = (s1 - s0 + RT - 1) / RT;
+  if (tid == 0) {
+    for (int i = 0; i < NS; i++) {
+      tc::mbar_init(&full[i], 1);
+      tc::mbar_init(&empty[i], 4);  // one arrival per warp
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // warp 0 holds the split's page ids in lane registers (<= 32 pages)
+  const int pg0 = s0 / pt;
+  const int npg = (s1 - 1) / pt - pg0 + 1;
+  const bool page_regs = npg <= 32;
+  const int my_page = (warp == 0 && page_regs && lane < npg) ? a.meta.page_ids[pbase + pg0 + lane] : 0;
+  auto load_tile = [&](int t) {  // warp 0 only
+    const int st = t % NS;
+    float* dst = kv + st * 2 * RT * HD;
+    const int t0 = s0 + t * RT, tn = min(RT, s1 - t0);
+    if (lane == 0) tc::mbar_expect_tx(&full[st], (uint32_t)tn * 2 * HD * 4);
+    __syncwarp();
+    const int pos = t0 + min(lane, tn - 1);
+    const int pi = pos / pt;
+    const int pg = __shfl_sync(0xffffffffu, my_page, (pi - pg0) & 31);
+    if (lane < tn) {
+      const int64_t page = page_regs ? pg : a.meta.page_ids[pbase + pi];
+      const float* krow = a.pool + page * a.dm.page_elems + lay + (int64_t)(pos - pi * pt) * a.dm.kvd;
+      tc::bulk_load(dst + lane * HD, krow, HD * 4, &full[st]);
+      tc::bulk_load(dst + (RT + lane) * HD, krow + vofs, HD * 4, &full[st]);
+    }
+  };
+  bool ok = true;
+  if (warp == 0)
+    for (int t = 0; t < min(ntiles, NS - 1); t++) load_tile(t);
+
+  float4 q[G][4];
+  {
+    const float* qrow = a.Q + (int64_t)r * a.dm.qd + (int64_t)kh * G * HD;
+    const int jl = lane & 7;
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float4 v = *(const float4*)(qrow + g * HD + 4 * jl + 32 * i);
+        q[g][i] = make_float4(v.x * a.scale, v.y * a.scale, v.z * a.scale, v.w * a.scale);
+      }
+  }
+  float mreg[ROUNDS], lreg[ROUNDS];
+#pragma unroll
+  for (int k = 0; k < ROUNDS; k++) {
+    mreg[k] = -INFINITY;
+    lreg[k] = 0.f;
+  }
+  float4 acc[G];
+#pragma unroll
+  for (int g = 0; g < G; g++) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  for (int t = 0; t < ntiles; t++) {
+    if (warp == 0 && t + NS - 1 < ntiles) {
+      const int u = t - 1;  // the stage refilled now was read in iteration t - 1 by every warp
+      if (u >= 0) ok = ok && tc::mbar_wait(&empty[u % NS], (u / NS) & 1, a.err);
+      load_tile(t + NS - 1);
+    }
+    ok = ok && tc::mbar_wait(&full[t % NS], (t / NS) & 1, a.err);  // on expiry: error raised, garbage computed
+    const float* kt = kv + (t % NS) * 2 * RT * HD;
+    const float* vt = kt + RT * HD;
+    if (has) {
+#pragma unroll
+      for (int h = 0; h < RT / kWpMT; h++) {
+        const int p0 = s0 + t * RT + h * kWpMT;
+        const int tn = min(kWpMT, er - p0);
+        if (tn > 0) warp_tile8<G>(kt + h * kWpMT * HD, vt + h * kWpMT * HD, tn, q, mreg, lreg, acc, sc, ps, lane);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&empty[t % NS]);
+  }
+  if (has) {  // this row's split partial (O, m, l), same layout as fa_write_split
+    const int64_t unit = (int64_t)(a.meta.row_item0[r] + split) * a.dm.kv_heads + kh;
+#pragma unroll
+    for (int g = 0; g < G; g++) *(float4*)(a.part_o + (unit * G + g) * HD + 4 * lane) = acc[g];
+#pragma unroll
+    for (int k = 0; k < ROUNDS; k++) {
+      const int g = (lane >> 3) + 4 * k;
+      if ((lane & 7) == 0 && g < G) {
+        a.part_ml[(unit * G + g) * 2] = mreg[k];
+        a.part_ml[(unit * G + g) * 2 + 1] = lreg[k];
+      }
+    }
+  }
 }
 
 // ====================================================== head_dim 64: per CTA
@@ -457,7 +606,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_tile(FastAttnArgs a) {
   }
   if (tid < 2 * G) out[G * HD + tid] = ml[tid];
   __syncthreads();
-  fa_write_split(a, blockIdx.x, kh, G, HD, out, out + G * HD);
+  fa_write_split(a, a.meta.row_item0[r] + split, kh, G, HD, out, out + G * HD);
 }
 
 // Merge the splits of each (row, query head) and write the attention output.

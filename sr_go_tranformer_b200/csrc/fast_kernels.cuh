@@ -134,24 +134,39 @@ __global__ void k_swiglu_split(const float* __restrict__ G, const float* __restr
 }
 
 // ---------------------------------------------------------------- attention --
+// Work counts of one step's fast attention: all (row, split) items, those of
+// rows from 1-token chunks, and the (row group, split) pairs of longer chunks.
+struct FaWork {
+  int items, single, groups;
+};
+
 template <int HD, int G>
-inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n, int items) {
+inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n, const FaWork& w) {
   const size_t smem = fa_smem_bytes<HD, G>();
-  const dim3 grid(items, a.dm.kv_heads);
   if constexpr (HD == 128) {
-    cudaFuncSetAttribute(k_attn_warp128<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_attn_warp128<G><<<grid, kFaThreads, smem, m->stream>>>(a);
+    if (w.single > 0) {  // decode rows: 4 warps split each row's positions
+      cudaFuncSetAttribute(k_attn_warp128<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      k_attn_warp128<G><<<dim3(w.single, a.dm.kv_heads), kFaThreads, smem, m->stream>>>(a);
+      sr_count_launch(m);
+    }
+    if (w.groups > 0) {  // prefill rows: one warp per row, shared K/V tiles
+      const size_t rsm = RowsSmem<G>::BYTES;
+      cudaFuncSetAttribute(k_attn_rows128<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+      k_attn_rows128<G><<<dim3(w.groups, a.dm.kv_heads), kFaThreads, rsm, m->stream>>>(a);
+      sr_count_launch(m);
+    }
   } else {
     cudaFuncSetAttribute(k_attn_tile<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_attn_tile<HD, G><<<grid, kFaThreads, smem, m->stream>>>(a);
+    k_attn_tile<HD, G><<<dim3(w.items, a.dm.kv_heads), kFaThreads, smem, m->stream>>>(a);
+    sr_count_launch(m);
   }
   k_attn_combine<HD><<<dim3(n, a.dm.heads), HD, 0, m->stream>>>(a);
-  sr_count_launch(m, 2);
+  sr_count_launch(m);
   return true;
 }
 
 template <int HD>
-inline bool fa_dispatch_g(sr_model* m, const FastAttnArgs& a, int n, int items) {
+inline bool fa_dispatch_g(sr_model* m, const FastAttnArgs& a, int n, const FaWork& items) {
   switch (a.dm.group) {
     case 1: return fa_launch<HD, 1>(m, a, n, items);
     case 2: return fa_launch<HD, 2>(m, a, n, items);
@@ -179,7 +194,7 @@ inline size_t fa_scratch_floats(const ModelDims& dm, int items, size_t* units_ou
 
 // Launch split + combine with caller-provided scratch (no allocation).  With
 // xh/xl set, the combine writes bf16 hi/lo operand planes instead of fp32 A.
-inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, int items, int layer, float* part_o,
+inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, const FaWork& items, int layer, float* part_o,
                                float* part_ml, __nv_bfloat16* xh = nullptr, __nv_bfloat16* xl = nullptr) {
   const ModelDims& dm = m->dm;
   FastAttnArgs a;
@@ -201,13 +216,13 @@ inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, int i
 
 // Returns false (exact kernel runs instead) for unsupported shapes or when the
 // split scratch would exceed its cap.  The scratch grows on demand.
-inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int row_items, int layer,
+inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, const FaWork& work, int layer,
                                __nv_bfloat16* xh = nullptr, __nv_bfloat16* xl = nullptr) {
   const ModelDims& dm = m->dm;
   if (!fast_attention_supported(dm)) return false;
   FastState* st = fast_state(m);
   size_t items = 0;
-  fa_scratch_floats(dm, row_items, &items);
+  fa_scratch_floats(dm, work.items, &items);
   const size_t o_bytes = items * dm.group * dm.hd * 4;
   if (o_bytes > ((size_t)1 << 30)) return false;
   if (items > st->items_cap) {
@@ -229,7 +244,7 @@ inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, int r
     }
     st->items_cap = cap;
   }
-  return fast_attention_run(m, pool_data, n, row_items, layer, st->part_o, st->part_ml, xh, xl);
+  return fast_attention_run(m, pool_data, n, work, layer, st->part_o, st->part_ml, xh, xl);
 }
 
 // ------------------------------------------------------------------- linear --

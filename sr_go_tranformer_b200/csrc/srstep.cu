@@ -322,7 +322,7 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
   // computed region: per-row data, head maps, then the attention item table
   // (at most ceil(context / kAttnSplit) items for each of the 1024 rows)
   const int64_t item_cap = (int64_t)kMaxRows * ((c.context + kAttnSplit - 1) / kAttnSplit);
-  const int64_t meta_ints = m->upload_ints + kMetaComputed + kMaxRows + item_cap;
+  const int64_t meta_ints = m->upload_ints + kMetaComputed + kMaxRows + 3 * item_cap;
   if ((rc = sr_model_alloc(m, (void**)&m->meta_dev, (size_t)meta_ints * 4)) != SR_OK) { free_model(m); return rc; }
   if (cudaMallocHost(&m->h_stage, (size_t)(m->upload_ints * 4 + kSampleStageBytes)) != cudaSuccess) {
     cudaGetLastError();
@@ -346,6 +346,8 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
     s.n_heads = cbase + 2 * kMaxRows + 2 * kMaxSessions;
     s.row_item0 = cbase + kMetaComputed;
     s.item_rs = cbase + kMetaComputed + kMaxRows;
+    s.single_rs = s.item_rs + item_cap;
+    s.grp_rs = s.single_rs + item_cap;
   }
   // Sampler device buffers.
   {
@@ -654,7 +656,7 @@ int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* 
     return sr_fail(SR_EINVAL, "null batch array");
   if (b->token_offsets[0] != 0 || b->page_offsets[0] != 0) return sr_fail(SR_EINVAL, "offsets must start at 0");
   const int pt = c.page_tokens;
-  int64_t n = 0, max_end = 0, heads = 0, items = 0;
+  int64_t n = 0, max_end = 0, heads = 0, items = 0, single = 0, groups = 0;
   for (int i = 0; i < S; i++) {
     int64_t len = (int64_t)b->token_offsets[i + 1] - b->token_offsets[i];
     if (len < 1 || len > kMaxRows - n)
@@ -670,6 +672,10 @@ int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* 
     for (int64_t j = b->page_offsets[i]; j < b->page_offsets[i + 1]; j++)
       if (b->page_ids[j] < 0 || b->page_ids[j] >= pool->num_pages) return sr_fail(SR_EINVAL, "invalid KV page id");
     for (int64_t L = pos + 1; L <= pos + len; L++) items += (L + kAttnSplit - 1) / kAttnSplit;
+    if (len == 1)
+      single += (pos + 1 + kAttnSplit - 1) / kAttnSplit;
+    else
+      for (int64_t k = 0; k < len; k += 4) groups += (pos + k + std::min<int64_t>(4, len - k) + kAttnSplit - 1) / kAttnSplit;
     n += len;
     max_end = std::max(max_end, pos + len);
     heads += (!b->want_logits || b->want_logits[i]) ? 1 : 0;
@@ -716,6 +722,8 @@ int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* 
   info->heads = (int)heads;
   info->pages = b->page_offsets[S];
   info->attn_items = (int)items;
+  info->attn_single = (int)single;
+  info->attn_groups = (int)groups;
   return SR_OK;
 }
 
@@ -864,7 +872,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     sr_count_launch(m, 3);  // two norms and RoPE/KV of this layer
     bool a_split = false;   // attention wrote the O projection's operand planes
     SR_LAUNCH(m, SR_PROF_ATTENTION,
-              if (fixed_scratch) fast_attention_run(m, pool->data, n, info.attn_items, l, scratch->part_o, scratch->part_ml);
+              if (fixed_scratch) fast_attention_run(m, pool->data, n, FaWork{info.attn_items, info.attn_single, info.attn_groups}, l, scratch->part_o, scratch->part_ml);
               else if (fast) a_split = fast_attention(m, pool, n, info, l, xh, xl);
               else launch_attention_exact(m, pool, n, info.max_len, l));
     // O projection: X += O(a); a tensor-parallel rank writes its partial sum to
@@ -1081,7 +1089,8 @@ extern "C" int sr_step_sample(sr_model* m, sr_kvpool* pool, const sr_batch* batc
 // when they also wrote xh/xl, if given), else the exact kernel into fp32 A.
 static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, const BatchInfo& info, int layer,
                            __nv_bfloat16* xh, __nv_bfloat16* xl) {
-  if (fast_attention_try(m, pool->data, n, info.attn_items, layer, xh, xl)) return xh != nullptr;
+  if (fast_attention_try(m, pool->data, n, FaWork{info.attn_items, info.attn_single, info.attn_groups}, layer, xh, xl))
+    return xh != nullptr;
   launch_attention_exact(m, pool, n, info.max_len, layer);
   return false;
 }

@@ -36,6 +36,8 @@ struct BatchInfo {
   int sessions, rows, max_len, heads;
   int64_t pages;
   int attn_items;  // (row, kAttnSplit-position split) pairs of the split-K attention
+  int attn_single;  // of those, the items of rows from 1-token chunks
+  int attn_groups;  // (group of up to 4 consecutive rows of a longer chunk, split) pairs
 };
 
 // Event-based per-kernel-class timing on the model's stream.
