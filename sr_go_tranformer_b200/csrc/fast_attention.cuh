@@ -455,6 +455,245 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_rows128(FastAttnArgs a) {
   }
 }
 
+// ============================= head_dim 128, 4 query heads per KV head:
+// prefill rows on the tensor cores.  A group's 4 rows x 4 query heads are the
+// 16 rows of an mma.m16n8k16 tile: S = Q K^T and O += P V each run as three
+// bf16 products of hi/lo splits (Qh Kh + Qh Kl + Ql Kh; Ph Vh + Ph Vl + Pl Vh,
+// about 2^-16 relative per product) with fp32 accumulation, and the online
+// softmax works on the accumulator fragments (the score fragments of two
+// 8-position tiles are the P operand of the 16-position P.V product).  The two
+// warps of a CTA take the split's 16-position tiles alternately (so short
+// prefixes keep both busy), each through a private 2-stage ring; K/V rows are
+// padded to 132 floats so that the fragment loads are (nearly) free of bank
+// conflicts.
+constexpr int kMmTile = 16;
+constexpr int kMmStride = 132;
+constexpr int kMmWarps = 2;
+struct MmaSmem {
+  static constexpr int PER_WARP = 2 * 2 * kMmTile * kMmStride;          // [stage][K|V][pos][132]
+  static constexpr int MERGE = kMmWarps * (16 * 128 + 2 * 16);          // per warp: O[16][128], (m, l)[16]
+  static constexpr int TOTAL = kMmWarps * PER_WARP > MERGE ? kMmWarps * PER_WARP : MERGE;  // floats, then barriers
+  static constexpr size_t BYTES = (size_t)TOTAL * 4 + kMmWarps * 2 * 8;
+};
+
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+  const __nv_bfloat16 l0 = __float2bfloat16_rn(x0 - __bfloat162float(h0));
+  const __nv_bfloat16 l1 = __float2bfloat16_rn(x1 - __bfloat162float(h1));
+  hi = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);  // lower k in the low half
+  lo = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// grid: the step's row groups x KV heads (query heads per KV head = 4)
+__global__ void __launch_bounds__(kMmWarps * 32) k_attn_mma128(FastAttnArgs a) {
+  constexpr int HD = 128, T = kMmTile, ST = kMmStride, G = 4;
+  extern __shared__ __align__(16) float fsm[];
+  const int gr = a.meta.grp_rs[blockIdx.x], kh = blockIdx.y;
+  const int r0 = gr >> 16, nr = ((gr >> 13) & 7) + 1, split = gr & 0x1fff;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int p0 = a.meta.row_pos[r0];  // row k of the group sits at position p0 + k
+  const int s0 = split * kFaSplit;
+  const int s1 = min(p0 + nr, s0 + kFaSplit);
+  const int nall = (s1 - s0 + T - 1) / T;                           // the split's tiles
+  const int ntiles = nall > warp ? (nall - warp + kMmWarps - 1) / kMmWarps : 0;  // this warp's: warp, warp+2, ...
+  float* kv = fsm + warp * MmaSmem::PER_WARP;
+  uint64_t* bar = (uint64_t*)(fsm + MmaSmem::TOTAL) + warp * 2;
+  const int pbase = a.meta.row_pbase[r0];
+  const int pt = a.dm.page_tokens;
+  const int64_t lay = (int64_t)a.layer * 2 * pt * a.dm.kvd + (int64_t)kh * HD;
+  const int64_t vofs = (int64_t)pt * a.dm.kvd;
+  const int pg0 = s0 / pt;
+  const int npg = (s1 - 1) / pt - pg0 + 1;
+  const bool page_regs = npg <= 32;
+  const int my_page = (page_regs && lane < npg) ? a.meta.page_ids[pbase + pg0 + lane] : 0;
+  if (lane == 0) {
+    tc::mbar_init(&bar[0], 1);
+    tc::mbar_init(&bar[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  auto load_tile = [&](int t) {  // this warp's t-th tile: split tile warp + t * kMmWarps
+    const int st = t & 1;
+    float* dst = kv + st * 2 * T * ST;
+    const int t0 = s0 + (warp + t * kMmWarps) * T, tn = min(T, s1 - t0);
+    if (lane == 0) tc::mbar_expect_tx(&bar[st], (uint32_t)tn * 2 * HD * 4);
+    __syncwarp();
+    const int pos = t0 + min(lane, tn - 1);
+    const int pi = pos / pt;
+    const int pg = __shfl_sync(0xffffffffu, my_page, (pi - pg0) & 31);
+    if (lane < tn) {
+      const int64_t page = page_regs ? pg : a.meta.page_ids[pbase + pi];
+      const float* krow = a.pool + page * a.dm.page_elems + lay + (int64_t)(pos - pi * pt) * a.dm.kvd;
+      tc::bulk_load(dst + lane * ST, krow, HD * 4, &bar[st]);
+      tc::bulk_load(dst + (T + lane) * ST, krow + vofs, HD * 4, &bar[st]);
+    }
+  };
+  if (ntiles > 0) load_tile(0);
+
+  // query rows i = 4k + g (row k of the group, head g); this thread's rows gid and gid + 8
+  const int k0 = gid >> 2, k1 = (gid + 8) >> 2, g0 = gid & 3;
+  const int e0 = k0 < nr ? p0 + k0 + 1 : 0, e1 = k1 < nr ? p0 + k1 + 1 : 0;  // positions < e are visible
+  uint32_t qh[8][4], ql[8][4];
+  {
+    const float* q0 = a.Q + (int64_t)(r0 + min(k0, nr - 1)) * a.dm.qd + (int64_t)(kh * G + g0) * HD;
+    const float* q1 = a.Q + (int64_t)(r0 + min(k1, nr - 1)) * a.dm.qd + (int64_t)(kh * G + g0) * HD;
+    const float z0 = k0 < nr ? a.scale : 0.f, z1 = k1 < nr ? a.scale : 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) {
+      const int c = ks * 16 + tig * 2;
+      const float2 x0 = *(const float2*)(q0 + c), x1 = *(const float2*)(q1 + c);
+      const float2 y0 = *(const float2*)(q0 + c + 8), y1 = *(const float2*)(q1 + c + 8);
+      split_bf16x2(x0.x * z0, x0.y * z0, qh[ks][0], ql[ks][0]);
+      split_bf16x2(x1.x * z1, x1.y * z1, qh[ks][1], ql[ks][1]);
+      split_bf16x2(y0.x * z0, y0.y * z0, qh[ks][2], ql[ks][2]);
+      split_bf16x2(y1.x * z1, y1.y * z1, qh[ks][3], ql[ks][3]);
+    }
+  }
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // l: this thread's columns only
+  float o[16][4];
+#pragma unroll
+  for (int dn = 0; dn < 16; dn++) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
+  bool ok = true;
+
+  for (int t = 0; t < ntiles; t++) {
+    __syncwarp();  // the stage about to be refilled has been consumed
+    if (t + 1 < ntiles) load_tile(t + 1);
+    ok = ok && tc::mbar_wait(&bar[t & 1], (t >> 1) & 1, a.err);  // on expiry: error raised, garbage computed
+    float* Kt = kv + (t & 1) * 2 * T * ST;
+    float* Vt = Kt + T * ST;
+    const int tp0 = s0 + (warp + t * kMmWarps) * T, tn = min(T, s1 - tp0);
+    if (tn < T) {  // rows past the tile's end: zero V so that 0-probability columns add exactly nothing
+      for (int idx = lane; idx < (T - tn) * HD; idx += 32) Vt[(tn + idx / HD) * ST + idx % HD] = 0.f;
+      __syncwarp();
+    }
+    // S = Q K^T over the tile's two 8-position halves
+    float sacc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) {
+#pragma unroll
+      for (int nt = 0; nt < 2; nt++) {
+        const float* kr = Kt + (nt * 8 + gid) * ST + ks * 16 + tig * 2;
+        const float2 x = *(const float2*)kr, y = *(const float2*)(kr + 8);
+        uint32_t bh0, bl0, bh1, bl1;
+        split_bf16x2(x.x, x.y, bh0, bl0);
+        split_bf16x2(y.x, y.y, bh1, bl1);
+        mma_bf16_16816(sacc[nt], qh[ks], bh0, bh1);
+        mma_bf16_16816(sacc[nt], qh[ks], bl0, bl1);
+        mma_bf16_16816(sacc[nt], ql[ks], bh0, bh1);
+      }
+    }
+    // causal mask and online softmax on rows gid (c0, c1) and gid + 8 (c2, c3)
+    const int lim0 = min(e0, tp0 + tn), lim1 = min(e1, tp0 + tn);
+    float mt0 = -INFINITY, mt1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int pos = tp0 + nt * 8 + tig * 2 + e;
+        sacc[nt][e] = pos < lim0 ? sacc[nt][e] : -INFINITY;
+        sacc[nt][2 + e] = pos < lim1 ? sacc[nt][2 + e] : -INFINITY;
+        mt0 = fmaxf(mt0, sacc[nt][e]);
+        mt1 = fmaxf(mt1, sacc[nt][2 + e]);
+      }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, off));
+      mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, off));
+    }
+    const float mn0 = fmaxf(m0, mt0), mn1 = fmaxf(m1, mt1);
+    const float al0 = (m0 == -INFINITY) ? 0.f : __expf(m0 - mn0);
+    const float al1 = (m1 == -INFINITY) ? 0.f : __expf(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float pr[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        pr[nt][e] = sacc[nt][e] == -INFINITY ? 0.f : __expf(sacc[nt][e] - mn0);
+        pr[nt][2 + e] = sacc[nt][2 + e] == -INFINITY ? 0.f : __expf(sacc[nt][2 + e] - mn1);
+      }
+    l0 = l0 * al0 + pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1];
+    l1 = l1 * al1 + pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3];
+#pragma unroll
+    for (int dn = 0; dn < 16; dn++) {
+      o[dn][0] *= al0;
+      o[dn][1] *= al0;
+      o[dn][2] *= al1;
+      o[dn][3] *= al1;
+    }
+    // P as the A operand (16 rows x 16 positions), hi/lo
+    uint32_t ph[4], pl[4];
+    split_bf16x2(pr[0][0], pr[0][1], ph[0], pl[0]);
+    split_bf16x2(pr[0][2], pr[0][3], ph[1], pl[1]);
+    split_bf16x2(pr[1][0], pr[1][1], ph[2], pl[2]);
+    split_bf16x2(pr[1][2], pr[1][3], ph[3], pl[3]);
+    // O += P V over the 16 eight-dim slices
+#pragma unroll
+    for (int dn = 0; dn < 16; dn++) {
+      const float* vc = Vt + tig * 2 * ST + dn * 8 + gid;
+      uint32_t vh0, vl0, vh1, vl1;
+      split_bf16x2(vc[0], vc[ST], vh0, vl0);
+      split_bf16x2(vc[8 * ST], vc[9 * ST], vh1, vl1);
+      mma_bf16_16816(o[dn], ph, vh0, vh1);
+      mma_bf16_16816(o[dn], ph, vl0, vl1);
+      mma_bf16_16816(o[dn], pl, vh0, vh1);
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  // merge the warps: O_w[16][128], (m, l)_w[16] -> the rows' split partials
+  __syncthreads();
+  float* mo = fsm + warp * (16 * HD + 32);
+  float* mml = mo + 16 * HD;
+#pragma unroll
+  for (int dn = 0; dn < 16; dn++) {
+    const int c = dn * 8 + tig * 2;
+    *(float2*)(mo + gid * HD + c) = make_float2(o[dn][0], o[dn][1]);
+    *(float2*)(mo + (gid + 8) * HD + c) = make_float2(o[dn][2], o[dn][3]);
+  }
+  if (tig == 0) {
+    mml[gid * 2] = m0;
+    mml[gid * 2 + 1] = l0;
+    mml[(gid + 8) * 2] = m1;
+    mml[(gid + 8) * 2 + 1] = l1;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 16 * HD; idx += kMmWarps * 32) {
+    const int i = idx / HD, d = idx % HD, k = i >> 2, g = i & 3;
+    if (k >= nr || p0 + k + 1 <= s0) continue;  // no such row, or the row does not reach this split
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kMmWarps; w++) M = fmaxf(M, fsm[w * (16 * HD + 32) + 16 * HD + i * 2]);
+    float ov = 0.f, lv = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMmWarps; w++) {
+      const float* base = fsm + w * (16 * HD + 32);
+      const float mw = base[16 * HD + i * 2];
+      const float ew = (mw == -INFINITY) ? 0.f : __expf(mw - M);
+      ov += ew * base[i * HD + d];
+      lv += ew * base[16 * HD + i * 2 + 1];
+    }
+    const int64_t unit = (int64_t)(a.meta.row_item0[r0 + k] + split) * a.dm.kv_heads + kh;
+    a.part_o[(unit * G + g) * HD + d] = ov;
+    if (d == 0) {
+      a.part_ml[(unit * G + g) * 2] = M;
+      a.part_ml[(unit * G + g) * 2 + 1] = lv;
+    }
+  }
+}
+
 // ====================================================== head_dim 64: per CTA
 constexpr int kFaTile = 32;
 

@@ -149,10 +149,15 @@ inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n, const FaWork& w
       k_attn_warp128<G><<<dim3(w.single, a.dm.kv_heads), kFaThreads, smem, m->stream>>>(a);
       sr_count_launch(m);
     }
-    if (w.groups > 0) {  // prefill rows: one warp per row, shared K/V tiles
-      const size_t rsm = RowsSmem<G>::BYTES;
-      cudaFuncSetAttribute(k_attn_rows128<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
-      k_attn_rows128<G><<<dim3(w.groups, a.dm.kv_heads), kFaThreads, rsm, m->stream>>>(a);
+    if (w.groups > 0) {  // prefill rows
+      if constexpr (G == 4) {  // 4 rows x 4 heads: one tensor-core M tile
+        cudaFuncSetAttribute(k_attn_mma128, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MmaSmem::BYTES);
+        k_attn_mma128<<<dim3(w.groups, a.dm.kv_heads), kMmWarps * 32, MmaSmem::BYTES, m->stream>>>(a);
+      } else {  // one warp per row, shared K/V tiles
+        const size_t rsm = RowsSmem<G>::BYTES;
+        cudaFuncSetAttribute(k_attn_rows128<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+        k_attn_rows128<G><<<dim3(w.groups, a.dm.kv_heads), kFaThreads, rsm, m->stream>>>(a);
+      }
       sr_count_launch(m);
     }
   } else {
