@@ -1,7 +1,7 @@
 """GPU parity of SR_MODE_FAST (split-K attention, FFMA norms, tensor-core
 projections) against the CPU oracle within a stated tolerance.
 
-Fast mode reorders fp32 sums (online softmax over 256-position splits, FMA
+Fast mode reorders fp32 sums (online softmax over split-K attention splits, FMA
 contraction, bf16x2-split tensor-core products), so logits are compared with
 an absolute tolerance of FAST_ATOL on logits of magnitude ~1 and greedy ids
 must agree except on recorded near-ties (margin below FAST_TIE).
@@ -93,3 +93,42 @@ def test_fast_qwen_shape_bias_q4(oracle, srlib):
     prompts = [rng.integers(0, 1024, size=n).tolist() for n in (520, 40)]
     worst, ties = run_pair(oracle, srlib, om, prompts, chunk=200, decode_steps=2)
     assert worst <= FAST_ATOL
+
+
+def test_fast_qwen_shape_32k_context_decode(oracle, srlib):
+    """Config 5's attention shape (hd 128, 7 query heads per KV head, QKV bias,
+    q4-mixed) at the full 32,768-token context: one decode step whose rows read
+    32,000 / 20,000 / 777 earlier positions (up to 63 attention splits), with
+    the same K/V pages on both sides (filled synthetically on the device, read
+    back for the oracle: a 32K-token CPU prefill would take minutes)."""
+    from sr_go_tranformer_b200 import step as S
+    pt = 16
+    cfg = oracle.make_config(512, 896, 512, 1, 7, 1, 32768, rope_theta=1e6, tied=False, qkv_bias=True,
+                             weight_format="q4-mixed", page_tokens=pt)
+    om = oracle.Model(cfg)
+    om.init_synthetic(12, 0.02)
+    dm = device_from_oracle(om, srlib, mode="fast")
+    pos = [32000, 20000, 777]
+    npages = sum((p + 1 + pt - 1) // pt for p in pos)
+    pool = S.PagePool(dm, npages)
+    pool.fill_synthetic(77, 0.5)
+    opool = np.zeros(npages * om.page_elements, dtype=np.float32)
+    kd = dm.kv_dim
+    caches = []
+    for p in pos:
+        c = dm.new_cache(pool)
+        c.ensure_pages(p + 1)
+        for q in range(p):  # the oracle sees the same earlier rows
+            pg, slot = c.pages[q // pt], q % pt
+            k, v = pool.read_row(pg, 0, slot)
+            base = pg * om.page_elements + slot * kd
+            opool[base:base + kd] = k
+            opool[base + pt * kd:base + pt * kd + kd] = v
+        c.pos = p
+        caches.append(c)
+    rng = np.random.default_rng(4)
+    chunks = [[int(t)] for t in rng.integers(0, 512, size=len(pos))]
+    got = dm.prefill_selected(caches, chunks, [True] * len(pos))
+    exp = om.step(opool, pos, chunks, [c.pages for c in caches], [True] * len(pos), threads=8)
+    err = float(np.abs(got - exp).max())
+    assert err <= FAST_ATOL, f"32K-context decode logits differ by {err:.3g}"
