@@ -166,6 +166,12 @@ int sr_kvpool_create(sr_model *m, int64_t num_pages, sr_kvpool **out);
 int sr_kvpool_destroy(sr_kvpool *p);
 /* Copy one K and one V row (kvDim floats each) of (page, layer, slot) to host. */
 int sr_kvpool_read_row(const sr_kvpool *p, int64_t page, int32_t layer, int32_t slot, float *k_out, float *v_out);
+/* Copy the first `rows` token slots (0..page_tokens) of every layer's K and V
+ * planes of page src_page into page dst_page: copyKVPrefixRows (:5907-5914),
+ * the device half of the prefix cache's restore and capture (:5881-5952).
+ * Enqueued on the model's stream, so it is ordered with the steps around it;
+ * the pages may not overlap a step's writes in flight on another stream. */
+int sr_kvpool_copy_rows(sr_kvpool *p, int64_t dst_page, int64_t src_page, int32_t rows);
 /* Fill every page with deterministic pseudo-random values (benchmark state). */
 int sr_kvpool_fill_synthetic(sr_kvpool *p, uint64_t seed, float scale);
 
@@ -245,6 +251,13 @@ typedef struct sr_engine_config {
     int64_t cache_bytes;         /* KV budget; pool Limit = cache_bytes / page bytes */
     int32_t eos_id;              /* -1: no EOS */
     int32_t blocked_id;          /* -1 for HF models */
+    /* Prefix cache (EngineConfig.PrefixCacheBytes / PrefixCacheTail, :7639-7640):
+     * bytes carved out of cache_bytes for the one-entry prefix snapshot (0 = off;
+     * pool Limit = (cache_bytes - prefix_cache_bytes) / page bytes), and whether
+     * matching tokens inside a partial page are reused too. */
+    int64_t prefix_cache_bytes;
+    int32_t prefix_cache_tail;
+    int32_t reserved;
 } sr_engine_config;
 typedef struct sr_request {
     const int32_t *ids;
@@ -257,6 +270,9 @@ typedef struct sr_engine_stats {
     int64_t submitted, completed, rejected, failed, active, queued;
     int64_t input_tokens, generated_tokens, ticks, peak_tick_tokens;
     int64_t pool_limit, pool_reserved, pool_allocated;
+    /* EngineStats.PrefixHits / PrefixTokens / PrefixBytes (:8231-8234, :8357-8360);
+     * pool_allocated includes the prefix snapshot's pages, as Allocated does. */
+    int64_t prefix_hits, prefix_tokens, prefix_bytes;
 } sr_engine_stats;
 
 int sr_engine_create(sr_model *m, const sr_engine_config *c, sr_engine **out);
@@ -282,6 +298,13 @@ int sr_engine_latency(const sr_engine *e, double *ttft_p50_ms, double *itl_p50_m
 int sr_engine_last_schedule(const sr_engine *e, int32_t *counts, int32_t cap, int32_t *n_sessions);
 /* Page table of active session i in admission order (up to cap ids). */
 int sr_engine_session_pages(const sr_engine *e, int32_t i, int32_t *pages, int32_t cap, int32_t *n_pages);
+/* Drop the prefix snapshot (the engine's clearPrefix, :8236-8241): sessions
+ * admitted before the call never capture into it again.  Like the reference,
+ * which takes the request only while no session is active, the clear is applied
+ * at once when the engine is idle and otherwise at the start of the first tick
+ * that finds it idle.  Snapshot pages stay in device memory while a session
+ * borrows them (prefixSnapshot.clear, :5915-5921). */
+int sr_engine_clear_prefix(sr_engine *e);
 
 #ifdef __cplusplus
 }

@@ -25,6 +25,7 @@ EXPORTED = [
     "sr_engine_destroy", "sr_engine_submit", "sr_engine_tick", "sr_engine_poll", "sr_engine_stats_get",
     "sr_engine_last_schedule", "sr_engine_session_pages", "sr_profile_set", "sr_profile_read", "sr_model_stream",
     "sr_step_noalloc", "sr_model_create_tp", "sr_tp_unique_id", "sr_tp_shard", "sr_engine_latency",
+    "sr_kvpool_copy_rows", "sr_engine_clear_prefix",
 ]
 PROF_CLASSES = ["meta", "embed", "norm", "linear", "rope_kv", "attention", "swiglu", "head", "sample"]
 
@@ -57,7 +58,8 @@ class Sampling(C.Structure):
 class EngineConfig(C.Structure):
     _fields_ = [("max_batch", C.c_int32), ("token_budget", C.c_int32), ("prefill_chunk", C.c_int32),
                 ("mixed_prefill_chunk", C.c_int32), ("cache_bytes", C.c_int64), ("eos_id", C.c_int32),
-                ("blocked_id", C.c_int32)]
+                ("blocked_id", C.c_int32), ("prefix_cache_bytes", C.c_int64), ("prefix_cache_tail", C.c_int32),
+                ("reserved", C.c_int32)]
 
 
 class Request(C.Structure):
@@ -68,7 +70,8 @@ class Request(C.Structure):
 class EngineStats(C.Structure):
     _fields_ = [(k, C.c_int64) for k in ("submitted", "completed", "rejected", "failed", "active", "queued",
                                           "input_tokens", "generated_tokens", "ticks", "peak_tick_tokens",
-                                          "pool_limit", "pool_reserved", "pool_allocated")]
+                                          "pool_limit", "pool_reserved", "pool_allocated", "prefix_hits",
+                                          "prefix_tokens", "prefix_bytes")]
 
 
 class SRError(RuntimeError):
@@ -105,6 +108,8 @@ def lib():
         "sr_kvpool_destroy": (C.c_int, [P]),
         "sr_kvpool_read_row": (C.c_int, [P, I64, I32, I32, P, P]),
         "sr_kvpool_fill_synthetic": (C.c_int, [P, U64, C.c_float]),
+        "sr_kvpool_copy_rows": (C.c_int, [P, I64, I64, I32]),
+        "sr_engine_clear_prefix": (C.c_int, [P]),
         "sr_step": (C.c_int, [P, P, C.POINTER(Batch), P, P]),
         "sr_step_logits": (C.c_int, [P, C.POINTER(P)]),
         "sr_step_noalloc": (C.c_int, [P, P, C.POINTER(Batch), P]),

@@ -4,8 +4,10 @@
 // The Go engine keeps its own loop and calls sr_step / sr_sample through cgo;
 // this C++ engine reproduces that loop's integer decisions (admission, page
 // reservation, scheduleTokens, the LIFO page pool, finishing) for callers that
-// have no Go runtime (tests, benchmarks).  HTTP, SSE streaming, tokenisation,
-// prefix caching and cancellation watchers are outside this restatement.
+// have no Go runtime (tests, benchmarks), including the one-entry prefix
+// snapshot (M:5868-5952) whose page copies run on the device.  HTTP, SSE
+// streaming, tokenisation and cancellation watchers are outside this
+// restatement.
 #include <algorithm>
 #include <chrono>
 #include <deque>
@@ -32,6 +34,9 @@ struct EngSession {
   EngRequest req;
   std::vector<int32_t> pages;  // KVCache.Pages (page ids)
   int32_t reserved = 0;        // KVCache.reserved
+  bool shared = false;         // KVCache.shared != nil (the engine has one snapshot)
+  int32_t shared_pages = 0;    // KVCache.sharedPages
+  int64_t prefix_epoch = 0;    // engineSession.PrefixEpoch
   int32_t pos = 0;             // KVCache.Pos
   int32_t cursor = 0;          // engineSession.Cursor
   std::vector<int32_t> output, history;
@@ -46,6 +51,18 @@ struct Finished {
   int32_t reason;  // 0 length, 1 eos, 2 error, 3 busy
 };
 
+// prefixSnapshot (M:5868-5877).  Its i-th page is device page limit + i of the
+// engine's pool; the pool holds prefix_limit such pages after the Limit pages
+// that pagePool hands out.  valid stands for p.model != nil (one model per
+// engine, whose revision never changes).
+struct PrefixSnapshot {
+  bool valid = false;
+  std::vector<int32_t> ids;
+  int32_t pages = 0;  // len(p.pages)
+  int32_t borrowers = 0;
+  bool include_tail = false;
+};
+
 }  // namespace
 
 struct sr_engine {
@@ -55,6 +72,9 @@ struct sr_engine {
   // pagePool (M:5849-5866): Limit, Reserved, Allocated and the LIFO free list.
   int64_t limit = 0, reserved = 0, allocated = 0;
   std::vector<int32_t> free_pages;
+  PrefixSnapshot prefix;
+  int64_t prefix_limit = 0, prefix_epoch = 0;
+  bool clear_pending = false;
   std::deque<EngRequest> queue;
   std::vector<EngSession> sessions;
   int32_t rotation = 0;
@@ -81,14 +101,100 @@ static int32_t acquire(sr_engine* e) {
   return (int32_t)(e->allocated++);
 }
 
-// KVCache.Close (M:6044-6062): pages return to the free list in page order.
+// KVCache.Close (M:6044-6062): owned pages return to the free list in page
+// order; borrowed snapshot pages only drop the borrow.
 static void close_session(sr_engine* e, EngSession& s) {
-  e->free_pages.insert(e->free_pages.end(), s.pages.begin(), s.pages.end());
+  e->free_pages.insert(e->free_pages.end(), s.pages.begin() + s.shared_pages, s.pages.end());
   e->reserved -= s.reserved;
+  if (s.shared) {
+    PrefixSnapshot& p = e->prefix;
+    p.borrowers--;
+    if (p.borrowers == 0 && !p.valid) p.pages = 0;
+    s.shared = false;
+  }
   s.pages.clear();
+  s.shared_pages = 0;
+}
+
+static int32_t snapshot_page(const sr_engine* e, int32_t i) { return (int32_t)(e->limit + i); }
+
+// prefixSnapshot.restore (M:5881-5905): borrow the snapshot's whole matching
+// pages; with tail reuse, copy the matching rows of the next page into a page
+// of the session's own.  The last prompt id always runs through the model.
+static int restore_prefix(sr_engine* e, EngSession& s) {
+  PrefixSnapshot& p = e->prefix;
+  const std::vector<int32_t>& ids = s.req.ids;
+  if (!p.valid || ids.size() < 2) return SR_OK;
+  const size_t n = std::min(p.ids.size(), ids.size() - 1);
+  size_t matched = 0;
+  while (matched < n && p.ids[matched] == ids[matched]) matched++;
+  const int32_t pt = e->m->d.page_tokens;
+  const int32_t full = (int32_t)(matched / pt);
+  if (full > 0) {
+    for (int32_t i = 0; i < full; i++) s.pages.push_back(snapshot_page(e, i));
+    s.shared = true;
+    s.shared_pages = full;
+    p.borrowers++;
+  }
+  s.pos = full * pt;
+  const int32_t tail = (int32_t)(matched % pt);
+  if (p.include_tail && tail > 0) {
+    while ((int64_t)s.pages.size() < full + 1) s.pages.push_back(acquire(e));  // ensurePages(matched)
+    int rc = sr_kvpool_copy_rows(e->pool, s.pages[full], snapshot_page(e, full), tail);
+    if (rc != SR_OK) return rc;
+    s.pos = (int32_t)matched;
+  }
+  return SR_OK;
+}
+
+// prefixSnapshot.capture (M:5927-5952): keep the committed positions of a
+// successfully finished session.  Skipped while another session borrows the
+// snapshot; the session's own borrowed pages are already in place.
+static int capture_prefix(sr_engine* e, const EngSession& s) {
+  PrefixSnapshot& p = e->prefix;
+  const bool sole = s.shared && p.borrowers == 1 && p.valid;
+  if (p.borrowers != 0 && !sole) return SR_OK;
+  const int64_t pt = e->m->d.page_tokens;
+  int64_t positions = s.pos;
+  if (!p.include_tail) positions -= positions % pt;
+  const int64_t n = std::min<int64_t>(e->prefix_limit, (positions + pt - 1) / pt);
+  positions = std::min<int64_t>(positions, n * pt);
+  if (n == 0) return SR_OK;
+  if (p.pages < n) p.pages = (int32_t)n;
+  for (int64_t i = 0; i < n; i++) {
+    const int32_t dst = snapshot_page(e, (int32_t)i);
+    if (dst != s.pages[i]) {
+      int rc = sr_kvpool_copy_rows(e->pool, dst, s.pages[i], (int32_t)std::min<int64_t>(pt, positions - i * pt));
+      if (rc != SR_OK) return rc;
+    }
+  }
+  p.ids.assign(s.history.begin(), s.history.begin() + positions);
+  p.valid = true;
+  return SR_OK;
+}
+
+// prefixSnapshot.clear (M:5915-5921) behind the actor's clearPrefix (M:8236-8241).
+static void clear_prefix(sr_engine* e) {
+  e->prefix_epoch++;
+  e->prefix.ids.clear();
+  e->prefix.valid = false;
+  if (e->prefix.borrowers == 0) e->prefix.pages = 0;
+  e->clear_pending = false;
+}
+
+static void account(sr_engine* e) {  // the actor's accounting (M:8230-8235)
+  e->st.prefix_bytes = (int64_t)e->prefix.pages * e->m->dm.page_elems * 4;
+  e->st.pool_reserved = e->reserved;
+  e->st.pool_allocated = e->allocated + e->prefix.pages;
 }
 
 static void finish(sr_engine* e, EngSession& s, int32_t reason) {
+  // finish (M:8285-8293): a successful session whose epoch is current offers its
+  // positions to the snapshot before its cache closes.
+  if (reason <= 1 && s.prefix_epoch == e->prefix_epoch && e->prefix_limit > 0) {
+    int rc = capture_prefix(e, s);
+    if (rc != SR_OK) reason = 2;
+  }
   close_session(e, s);
   e->st.active--;
   if (reason <= 1) e->st.completed++;
@@ -136,14 +242,23 @@ extern "C" int sr_engine_create(sr_model* m, const sr_engine_config* cfg, sr_eng
       c.mixed_prefill_chunk < 1 || c.mixed_prefill_chunk > 1024 || c.token_budget < c.max_batch ||
       c.token_budget > 1024)
     return sr_fail(SR_EINVAL, "invalid engine capacity or token budget");
+  if (c.prefix_cache_bytes < 0 || c.prefix_cache_bytes >= c.cache_bytes)  // M:7999-8003
+    return sr_fail(SR_EINVAL, "prefix cache must be nonnegative and smaller than total KV budget");
+  if (c.prefix_cache_tail && c.prefix_cache_bytes == 0)
+    return sr_fail(SR_EINVAL, "prefix cache tail reuse requires a positive prefix cache budget");
   const int64_t page_bytes = m->dm.page_elems * 4;
-  const int64_t limit = c.cache_bytes / page_bytes;  // newEngine (M:8031-8035)
+  const int64_t prefix_limit = c.prefix_cache_bytes / page_bytes;  // newEngine (M:8031-8035)
+  if (c.prefix_cache_bytes != 0 && prefix_limit == 0)
+    return sr_fail(SR_EINVAL, "prefix cache budget cannot hold one KV page");
+  const int64_t limit = (c.cache_bytes - c.prefix_cache_bytes) / page_bytes;
   if (limit < 1) return sr_fail(SR_EINVAL, "cache budget cannot hold one KV page");
   sr_engine* e = new sr_engine();
   e->m = m;
   e->c = c;
   e->limit = limit;
-  int rc = sr_kvpool_create(m, limit, &e->pool);
+  e->prefix_limit = prefix_limit;
+  e->prefix.include_tail = c.prefix_cache_tail != 0;
+  int rc = sr_kvpool_create(m, limit + prefix_limit, &e->pool);
   if (rc != SR_OK) {
     delete e;
     return rc;
@@ -189,7 +304,9 @@ extern "C" int sr_engine_tick(sr_engine* e, int32_t* rows) {
   if (!e || !rows) return sr_fail(SR_EINVAL, "null argument");
   *rows = 0;
   const int64_t pt = e->m->d.page_tokens;
-  // Admission (M:8325-8366): reserve whole pages for prompt + max_tokens.
+  if (e->clear_pending && e->sessions.empty()) clear_prefix(e);
+  // Admission (M:8325-8366): reserve whole pages for prompt + max_tokens, then
+  // restore the matching prefix from the snapshot.
   while ((int)e->sessions.size() < e->c.max_batch && !e->queue.empty()) {
     EngRequest r = std::move(e->queue.front());
     e->queue.pop_front();
@@ -205,8 +322,25 @@ extern "C" int sr_engine_tick(sr_engine* e, int32_t* rows) {
     s.history = r.ids;
     s.rng = r.seed;  // RNG{r.Sampling.Seed}
     s.req = std::move(r);
+    s.prefix_epoch = e->prefix_epoch;
+    int rc = restore_prefix(e, s);
+    if (rc != SR_OK) {
+      std::string msg = sr_last_error();
+      close_session(e, s);
+      e->st.failed++;
+      e->finished.push_back(Finished{s.req.id, {}, 2});
+      account(e);
+      sr_fail(rc, msg);
+      return rc;
+    }
+    if (s.pos > 0) {
+      e->st.prefix_hits++;
+      e->st.prefix_tokens += s.pos;
+    }
+    s.cursor = s.pos;  // engineSession.Cursor = cache.Pos
     e->sessions.push_back(std::move(s));
     e->st.active++;
+    account(e);
   }
   e->st.queued = (int64_t)e->queue.size();
   if (e->sessions.empty()) return SR_OK;
@@ -265,8 +399,7 @@ extern "C" int sr_engine_tick(sr_engine* e, int32_t* rows) {
     std::string msg = sr_last_error();
     for (auto& s : e->sessions) finish(e, s, 2);
     e->sessions.clear();
-    e->st.pool_reserved = e->reserved;
-    e->st.pool_allocated = e->allocated;
+    account(e);
     sr_fail(rc, msg);
     return rc;
   }
@@ -302,8 +435,15 @@ extern "C" int sr_engine_tick(sr_engine* e, int32_t* rows) {
     else alive.push_back(std::move(s));
   }
   e->sessions = std::move(alive);
-  e->st.pool_reserved = e->reserved;
-  e->st.pool_allocated = e->allocated;
+  account(e);
+  return SR_OK;
+}
+
+extern "C" int sr_engine_clear_prefix(sr_engine* e) {
+  if (!e) return sr_fail(SR_EINVAL, "null engine");
+  e->clear_pending = true;
+  if (e->sessions.empty()) clear_prefix(e);
+  account(e);
   return SR_OK;
 }
 
@@ -351,7 +491,8 @@ extern "C" int sr_engine_stats_get(const sr_engine* e, sr_engine_stats* s) {
   s->queued = (int64_t)e->queue.size();
   s->pool_limit = e->limit;
   s->pool_reserved = e->reserved;
-  s->pool_allocated = e->allocated;
+  s->pool_allocated = e->allocated + e->prefix.pages;
+  s->prefix_bytes = (int64_t)e->prefix.pages * e->m->dm.page_elems * 4;
   return SR_OK;
 }
 

@@ -625,6 +625,38 @@ extern "C" int sr_kvpool_read_row(const sr_kvpool* p, int64_t page, int32_t laye
   CK(cudaMemcpy(v_out, base + (int64_t)dm.page_tokens * dm.kvd, (size_t)dm.kvd * 4, cudaMemcpyDeviceToHost));
   return SR_OK;
 }
+// copyKVPrefixRows (M:5907-5914): the first `rows` slots of every layer's K and
+// V planes.  grid (2*layers planes, chunks); float4 when the plane stride and
+// the copied length allow it.
+__global__ void k_copy_rows(float* __restrict__ dst, const float* __restrict__ src, int64_t plane_elems,
+                            int64_t copy_elems) {
+  const int64_t base = (int64_t)blockIdx.x * plane_elems;
+  const int64_t step = (int64_t)gridDim.y * blockDim.x;
+  if ((plane_elems & 3) == 0 && (copy_elems & 3) == 0) {
+    const float4* s = (const float4*)(src + base);
+    float4* d = (float4*)(dst + base);
+    for (int64_t i = blockIdx.y * (int64_t)blockDim.x + threadIdx.x; i < copy_elems / 4; i += step) d[i] = s[i];
+  } else {
+    for (int64_t i = blockIdx.y * (int64_t)blockDim.x + threadIdx.x; i < copy_elems; i += step)
+      dst[base + i] = src[base + i];
+  }
+}
+extern "C" int sr_kvpool_copy_rows(sr_kvpool* p, int64_t dst_page, int64_t src_page, int32_t rows) {
+  if (!p) return sr_fail(SR_EINVAL, "null pool");
+  const ModelDims& dm = p->m->dm;
+  if (dst_page < 0 || dst_page >= p->num_pages || src_page < 0 || src_page >= p->num_pages)
+    return sr_fail(SR_EINVAL, "page id out of range");
+  if (rows < 0 || rows > dm.page_tokens) return sr_fail(SR_EINVAL, "rows must be 0..page_tokens");
+  if (rows == 0 || dst_page == src_page) return SR_OK;
+  CK(cudaSetDevice(p->m->device));
+  const int64_t plane = (int64_t)dm.page_tokens * dm.kvd, copy = (int64_t)rows * dm.kvd;
+  const int chunks = (int)std::min<int64_t>(32, (copy / 4 + 1023) / 1024 + 1);
+  k_copy_rows<<<dim3(2 * dm.layers, chunks), 256, 0, p->m->stream>>>(p->data + dst_page * dm.page_elems,
+                                                                       p->data + src_page * dm.page_elems, plane,
+                                                                       copy);
+  CK(cudaGetLastError());
+  return SR_OK;
+}
 __global__ void k_fill_pool(float* data, int64_t count, uint64_t seed, float scale) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
     uint64_t z = seed + (uint64_t)(i + 1) * 0x9e3779b97f4a7c15ULL;

@@ -15,10 +15,13 @@ class Engine:
     REASONS = {0: "length", 1: "eos", 2: "error", 3: "busy"}
 
     def __init__(self, model, max_batch, token_budget=0, prefill_chunk=0, mixed_prefill_chunk=0, cache_bytes=0,
-                 eos_id=-1, blocked_id=-1):
+                 eos_id=-1, blocked_id=-1, prefix_cache_bytes=0, prefix_cache_tail=False):
+        """prefix_cache_bytes / prefix_cache_tail: EngineConfig.PrefixCacheBytes /
+        PrefixCacheTail (M:7639-7640), the one-entry prefix snapshot's allowance
+        carved out of cache_bytes and sub-page reuse."""
         self.model = model
         cfg = A.EngineConfig(max_batch, token_budget, prefill_chunk, mixed_prefill_chunk, int(cache_bytes), eos_id,
-                             blocked_id)
+                             blocked_id, int(prefix_cache_bytes), int(bool(prefix_cache_tail)), 0)
         h = C.c_void_p()
         A.check(A.lib().sr_engine_create(model.h, C.byref(cfg), C.byref(h)))
         self.h = h
@@ -66,6 +69,10 @@ class Engine:
         t, g, nt, ng = C.c_double(), C.c_double(), C.c_int64(), C.c_int64()
         A.check(A.lib().sr_engine_latency(self.h, C.byref(t), C.byref(g), C.byref(nt), C.byref(ng)))
         return {"ttft_p50_ms": t.value, "itl_p50_ms": g.value, "first_tokens": nt.value, "gaps": ng.value}
+
+    def clear_prefix(self):
+        """Drop the prefix snapshot (clearPrefix, M:8236-8241); applied once the engine is idle."""
+        A.check(A.lib().sr_engine_clear_prefix(self.h))
 
     def last_schedule(self, cap=256):
         out = np.zeros(cap, dtype=np.int32)

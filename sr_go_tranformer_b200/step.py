@@ -284,6 +284,11 @@ class PagePool:
     def fill_synthetic(self, seed, scale=1.0):
         A.check(A.lib().sr_kvpool_fill_synthetic(self.h, seed, scale))
 
+    def copy_rows(self, dst, src, rows):
+        """copyKVPrefixRows (M:5907-5914): the first `rows` slots of every layer's K
+        and V planes of page src into page dst, on the model's stream."""
+        A.check(A.lib().sr_kvpool_copy_rows(self.h, int(dst), int(src), int(rows)))
+
 
 class KVCache:
     """KVCache (M:5954-6062): committed position and page ids."""

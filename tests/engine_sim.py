@@ -5,22 +5,73 @@ A pure-Python restatement of Engine.run's integer decisions
 (M:8348-8361), scheduleTokens (M:8180-8210), lazily acquired LIFO pages
 (pagePool.acquire M:5854-5866, KVCache.Close M:6044-6062), one prefillSelected
 per tick, sampleWithBlocked for sessions whose prompt is consumed, and
-finishing on EOS or max_tokens.  Small cases only: every step runs on the
-oracle.
+finishing on EOS or max_tokens.  With prefix_limit > 0 it also keeps the
+engine's one-entry prefix snapshot (prefixSnapshot, M:5868-5952): restore at
+admission (M:8356), capture when a session finishes (M:8285-8288), snapshot
+page i stored as pool page limit + i.  Small cases only: every step runs on
+the oracle.
 """
 
 import numpy as np
 
 
-def simulate(model, requests, limit, max_batch, budget, chunk, mixed_chunk, eos_id=-1, blocked=-1, threads=4):
+def simulate(model, requests, limit, max_batch, budget, chunk, mixed_chunk, eos_id=-1, blocked=-1, threads=4,
+             prefix_limit=0, prefix_tail=False, stats=None):
     """requests: list of dicts(ids, max_tokens, temperature, top_k, top_p, penalty, seed).
-    Returns ({request index: (output ids, reason)}, trace of per-tick (counts, page tables))."""
+    Returns ({request index: (output ids, reason)}, trace of per-tick (counts, page tables)).
+    stats, when a dict, receives prefix_hits / prefix_tokens / prefix_pages."""
     from oracle import oracle as O
     pt = model.cfg.page_tokens
-    pool = np.zeros(limit * model.page_elements, dtype=np.float32)
+    kvd = model.cfg.kv_heads * (model.cfg.dim // model.cfg.heads)
+    pe = model.page_elements
+    pool = np.zeros((limit + prefix_limit) * pe, dtype=np.float32)
     free, allocated, reserved = [], 0, 0
     queue = list(enumerate(requests))
     sessions, rotation, finished, trace = [], 0, {}, []
+    snap = dict(valid=False, ids=[], pages=0, borrowers=0)
+    hits = tokens = 0
+
+    def copy_rows(dst, src, rows):
+        d, s_ = dst * pe, src * pe
+        for off in range(0, pe, pt * kvd):
+            pool[d + off:d + off + rows * kvd] = pool[s_ + off:s_ + off + rows * kvd]
+
+    def restore(s):
+        ids = s["req"]["ids"]
+        if not snap["valid"] or len(ids) < 2:
+            return
+        n = min(len(snap["ids"]), len(ids) - 1)
+        matched = 0
+        while matched < n and snap["ids"][matched] == ids[matched]:
+            matched += 1
+        full = matched // pt
+        if full > 0:
+            s["pages"] = [limit + i for i in range(full)]
+            s["shared"] = full
+            snap["borrowers"] += 1
+        s["pos"] = full * pt
+        if prefix_tail and matched % pt:
+            s["pages"].append(acquire())
+            copy_rows(s["pages"][full], limit + full, matched % pt)
+            s["pos"] = matched
+
+    def capture(s):
+        sole = s["shared"] > 0 and snap["borrowers"] == 1 and snap["valid"]
+        if snap["borrowers"] != 0 and not sole:
+            return
+        positions = s["pos"]
+        if not prefix_tail:
+            positions -= positions % pt
+        n = min(prefix_limit, (positions + pt - 1) // pt)
+        positions = min(positions, n * pt)
+        if n == 0:
+            return
+        snap["pages"] = max(snap["pages"], n)
+        for i in range(n):
+            if limit + i != s["pages"][i]:
+                copy_rows(limit + i, s["pages"][i], min(pt, positions - i * pt))
+        snap["ids"] = list(s["history"][:positions])
+        snap["valid"] = True
 
     def acquire():
         nonlocal allocated
@@ -31,8 +82,12 @@ def simulate(model, requests, limit, max_batch, budget, chunk, mixed_chunk, eos_
 
     def close(s):
         nonlocal reserved
-        free.extend(s["pages"])
+        free.extend(s["pages"][s["shared"]:])
         reserved -= s["reserved"]
+        if s["shared"]:
+            snap["borrowers"] -= 1
+            if snap["borrowers"] == 0 and not snap["valid"]:
+                snap["pages"] = 0
 
     while queue or sessions:
         while len(sessions) < max_batch and queue:
@@ -42,8 +97,15 @@ def simulate(model, requests, limit, max_batch, budget, chunk, mixed_chunk, eos_
                 finished[rid] = ([], "busy")
                 continue
             reserved += pages
-            sessions.append(dict(rid=rid, req=r, pages=[], reserved=pages, pos=0, cursor=0, output=[],
-                                 history=list(r["ids"]), rng=r.get("seed", 1)))
+            s = dict(rid=rid, req=r, pages=[], reserved=pages, pos=0, cursor=0, output=[], shared=0,
+                     history=list(r["ids"]), rng=r.get("seed", 1))
+            if prefix_limit:
+                restore(s)
+                if s["pos"] > 0:
+                    hits += 1
+                    tokens += s["pos"]
+                s["cursor"] = s["pos"]
+            sessions.append(s)
         if not sessions:
             break
         n = len(sessions)
@@ -84,9 +146,13 @@ def simulate(model, requests, limit, max_batch, budget, chunk, mixed_chunk, eos_
             elif len(s["output"]) == r["max_tokens"]:
                 reason = "length"
             if reason:
+                if prefix_limit:
+                    capture(s)
                 close(s)
                 finished[s["rid"]] = (list(s["output"]), reason)
             else:
                 alive.append(s)
         sessions = alive
+    if stats is not None:
+        stats.update(prefix_hits=hits, prefix_tokens=tokens, prefix_pages=snap["pages"])
     return finished, trace

@@ -316,3 +316,102 @@ def test_engine_matches_oracle_simulation(oracle, srlib):
     assert lat["first_tokens"] == len(produced)
     assert lat["gaps"] == st["generated_tokens"] - len(produced)
     assert lat["ttft_p50_ms"] > 0 and lat["itl_p50_ms"] > 0
+
+
+def test_kvpool_copy_rows(oracle, srlib):
+    """sr_kvpool_copy_rows restates copyKVPrefixRows (M:5907-5914): the first
+    `rows` slots of every layer's K and V planes move bit for bit, the rest of
+    the destination page is untouched."""
+    S = _step_mod()
+    om, dm = synthetic_pair(oracle, srlib, "q8", 16)
+    pool = S.PagePool(dm, 8)
+    pool.fill_synthetic(5, 1.0)
+    pt, L = om.cfg.page_tokens, om.cfg.layers
+    before = {(p, l, s): pool.read_row(p, l, s) for p in (2, 6) for l in range(L) for s in range(pt)}
+    pool.copy_rows(6, 2, 5)
+    for l in range(L):
+        for s in range(pt):
+            k, v = pool.read_row(6, l, s)
+            src = before[(2, l, s)] if s < 5 else before[(6, l, s)]
+            assert_same(k, src[0], f"K layer {l} slot {s}")
+            assert_same(v, src[1], f"V layer {l} slot {s}")
+    pool.copy_rows(6, 2, pt)  # whole page
+    for l in range(L):
+        for s in range(pt):
+            k, v = pool.read_row(6, l, s)
+            assert_same(k, before[(2, l, s)][0], "K full")
+            assert_same(v, before[(2, l, s)][1], "V full")
+    for bad in ((8, 2, 1), (6, -1, 1), (6, 2, pt + 1), (6, 2, -1)):
+        with pytest.raises(Exception):
+            pool.copy_rows(*bad)
+
+
+def _prefix_requests(seed, n, system=40, vocab=300):
+    rng = np.random.default_rng(seed)
+    head = rng.integers(0, vocab, size=system).tolist()
+    reqs = []
+    for i in range(n):
+        r = dict(ids=head + rng.integers(0, vocab, size=int(rng.integers(1, 9))).tolist(),
+                 max_tokens=int(rng.integers(2, 6)), seed=70 + i)
+        if i % 2:
+            r.update(temperature=0.7, top_k=20, top_p=0.9, penalty=1.1)
+        reqs.append(r)
+    return reqs
+
+
+def _run_engine(eng, reqs):
+    ids = [eng.submit(r["ids"], r["max_tokens"], r.get("temperature", 0.0), r.get("top_k", 0), r.get("top_p", 1.0),
+                      r.get("penalty", 1.0), r["seed"]) for r in reqs]
+    done = eng.run_to_completion()
+    return {i: done[rid] for i, rid in enumerate(ids)}
+
+
+@pytest.mark.parametrize("tail,max_batch", [(False, 1), (True, 1), (True, 3)])
+def test_engine_prefix_cache_matches_simulation(oracle, srlib, tail, max_batch):
+    """The C++ engine's prefix snapshot (restore M:5881-5905 at admission,
+    capture M:5927-5952 at finish, device page copies) against the oracle
+    simulation: identical outputs, hits and reused tokens, and the outputs of
+    an engine without the cache."""
+    from engine_sim import simulate
+    from sr_go_tranformer_b200.engine import Engine
+    om, dm = synthetic_pair(oracle, srlib, "q8", 16, vocab=300)
+    reqs = _prefix_requests(12, 6)
+    limit, plimit = 24, 4
+    page_bytes = om.page_elements * 4
+    eng = Engine(dm, max_batch=max_batch, token_budget=16, prefill_chunk=8, mixed_prefill_chunk=1,
+                 cache_bytes=(limit + plimit) * page_bytes, prefix_cache_bytes=plimit * page_bytes,
+                 prefix_cache_tail=tail)
+    got = _run_engine(eng, reqs)
+    st = eng.stats()
+    sim = {}
+    want, _ = simulate(om, reqs, limit, max_batch, 16, 8, 1, prefix_limit=plimit, prefix_tail=tail, stats=sim)
+    base, _ = simulate(om, reqs, limit, max_batch, 16, 8, 1)
+    assert want == base
+    for k in want:
+        assert got[k] == want[k], (k, got[k], want[k])
+    assert st["prefix_hits"] == sim["prefix_hits"] > 0
+    assert st["prefix_tokens"] == sim["prefix_tokens"]
+    assert st["prefix_bytes"] == sim["prefix_pages"] * page_bytes
+    assert st["pool_limit"] == limit and st["pool_reserved"] == 0 and st["active"] == 0
+    # clearPrefix (M:8236-8241): applied at once when idle; the next request
+    # finds no snapshot
+    eng.clear_prefix()
+    assert eng.stats()["prefix_bytes"] == 0
+    again = _run_engine(eng, reqs[1:2])
+    assert again[0] == want[1]
+    assert eng.stats()["prefix_hits"] == st["prefix_hits"]
+    eng.close()
+
+
+def test_engine_prefix_config_errors(oracle, srlib):
+    """normalizeEngineConfig / newEngine prefix checks (M:7999-8003, 8031-8034)."""
+    from sr_go_tranformer_b200.engine import Engine
+    om, dm = synthetic_pair(oracle, srlib, "q8", 16, vocab=300)
+    pb = om.page_elements * 4
+    for kw in (dict(cache_bytes=8 * pb, prefix_cache_bytes=8 * pb), dict(cache_bytes=8 * pb, prefix_cache_bytes=-1),
+               dict(cache_bytes=8 * pb, prefix_cache_tail=True), dict(cache_bytes=8 * pb, prefix_cache_bytes=pb // 2)):
+        with pytest.raises(Exception):
+            Engine(dm, max_batch=2, **kw)
+    e = Engine(dm, max_batch=2, cache_bytes=8 * pb, prefix_cache_bytes=3 * pb)
+    assert e.stats()["pool_limit"] == 5
+    e.close()
