@@ -318,6 +318,8 @@ def main():
     ap.add_argument("--ref-sessions", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"])
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+                    help="tensor-parallel all-reduce: the library's NVLink peer-memory kernels or NCCL")
     ap.add_argument("--no-ttft", action="store_true", help="skip the serving run that measures TTFT")
     args = ap.parse_args()
     cfg = dict(CONFIG)
@@ -345,6 +347,10 @@ def main():
             dist.broadcast_object_list(obj, src=0)
             tp_args = (rank, world, obj[0])
     model = make_model(cfg, local, args.mode, tp=tp_args)
+    if tp and args.allreduce == "peer":
+        handles = [None] * world
+        dist.all_gather_object(handles, model.tp_peer_handle())
+        model.tp_peer_open(handles)
     st = DecodeState(cfg, model, W, workload_rank=0 if tp else rank)
     for _ in range(W):
         st.step()
@@ -411,6 +417,7 @@ def main():
             "config": {"workload": cfg["name"], "sessions": cfg["sessions"], "layers": cfg["layers"],
                        "page_tokens": cfg["page_tokens"], "weights": "q8 (64-col blocks, fp32 scales)",
                        "mode": args.mode, "parallelism": f"tp{world}" if tp else f"replicas{world}",
+                       "allreduce": (args.allreduce if tp else None),
                        "kv_state": "synthetic prefilled pages (prompt + decode offset)",
                        "l2": "inputs larger than L2 (KV pool > 100 GB)",
                        "sampling": "T0.8 k40 p0.95 penalty1.1, SplitMix64"},
@@ -438,6 +445,8 @@ def main():
         print(json.dumps(line))
     if dist:
         dist.barrier()
+    model.close()  # every rank: the peer all-reduce's last barrier
+    if dist:
         dist.destroy_process_group()
     return 0
 

@@ -129,6 +129,19 @@ int sr_tp_unique_id(void *id_out);
 /* Host-only: rows [shard[0], shard[0]+shard[1]) and columns [shard[2],
  * shard[2]+shard[3]) of parameter `index` that rank `rank` of `size` holds. */
 int sr_tp_shard(const sr_model_desc *desc, int32_t rank, int32_t size, int32_t index, int32_t *shard);
+/* All-reduce over NVLink peer memory (no counterpart in the reference, which
+ * runs on one CPU process).  By default a tensor-parallel step all-reduces the
+ * o_proj / down_proj partial sums with NCCL.  After every rank has called
+ * sr_tp_peer_open with all ranks' handles (rank order, SR_TP_PEER_HANDLE_BYTES
+ * each, exchanged by the caller like the NCCL id), it uses two kernels of plain
+ * peer loads and stores over CUDA IPC mappings instead: each rank sums one
+ * chunk of the array in rank order and gathers the others, so every rank holds
+ * bit-identical sums.  Barrier waits are bounded; a rank that does not join a
+ * step makes the others' step return SR_ETIMEOUT.  sr_model_destroy runs a
+ * last bounded barrier, so all ranks must destroy their models. */
+#define SR_TP_PEER_HANDLE_BYTES 64
+int sr_tp_peer_handle(sr_model *m, void *handle_out);
+int sr_tp_peer_open(sr_model *m, const void *handles);
 int sr_model_destroy(sr_model *m);
 int sr_model_param_count(const sr_model *m, int32_t *count);
 int sr_model_param_info(const sr_model *m, int32_t index, sr_param_info *out);

@@ -20,6 +20,7 @@
 #include "sampler.cuh"
 #include "srstep_internal.h"
 #include "nccl_dl.h"
+#include "tp_peer.cuh"
 
 using namespace sr;
 
@@ -77,9 +78,11 @@ static float hf_inverse_frequency(const sr_model_desc& c, int hd, int index) {
   return inv;
 }
 
+static void peer_close(sr_model* m);
 static void free_model(sr_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
+  peer_close(m);
   if (m->nccl_comm) nccl::api().CommDestroy((nccl::Comm)m->nccl_comm);
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_stage) cudaFreeHost(m->h_stage);
@@ -218,6 +221,140 @@ extern "C" int sr_model_create_tp(const sr_model_desc* desc, int device, int32_t
   return model_create(desc, device, tp_rank, tp_size, nccl_id, out);
 }
 
+// ------------------------------------------------- tensor-parallel peer memory --
+// One exported allocation per rank: the two all-reduce buffers, the barrier
+// slots and the finished-CTA counter (tp_peer.cuh).  tables (device) holds
+// every rank's buffer 0, buffer 1 and slot pointers once the peers are open.
+struct PeerHost {
+  uint8_t* base = nullptr;
+  size_t buf_bytes = 0;
+  float* buf[2] = {};
+  int* slots = nullptr;
+  int* counter = nullptr;
+  int* err = nullptr;
+  void** tables = nullptr;
+  std::vector<void*> opened;  // peers' allocations mapped through IPC
+  uint32_t epoch = 0;
+  int cur = 0;
+  bool open = false, ran = false;
+};
+constexpr size_t kPeerTail = 1024;  // slots (peer::kSlots ints), counter, error flag
+static_assert(peer::kSlots * 4 + 64 <= kPeerTail, "peer tail too small");
+static_assert(sizeof(cudaIpcMemHandle_t) == SR_TP_PEER_HANDLE_BYTES, "IPC handle size");
+
+static int peer_alloc(sr_model* m, size_t buf_bytes) {
+  PeerHost* ph = new PeerHost();
+  m->peer = ph;
+  ph->buf_bytes = buf_bytes;
+  int rc = sr_model_alloc(m, (void**)&ph->base, 2 * buf_bytes + kPeerTail);
+  if (rc != SR_OK) return rc;
+  ph->buf[0] = (float*)ph->base;
+  ph->buf[1] = (float*)(ph->base + buf_bytes);
+  ph->slots = (int*)(ph->base + 2 * buf_bytes);
+  ph->counter = ph->slots + peer::kSlots;
+  ph->err = ph->counter + 4;
+  if (cudaMemset(ph->base + 2 * buf_bytes, 0, kPeerTail) != cudaSuccess) {
+    cudaGetLastError();
+    return sr_fail(SR_EDEVICE, "clearing the all-reduce barrier slots failed");
+  }
+  if ((rc = sr_model_alloc(m, (void**)&ph->tables, (size_t)3 * m->dm.tp_size * sizeof(void*))) != SR_OK) return rc;
+  m->T = ph->buf[0];
+  return SR_OK;
+}
+
+// A last barrier over the peers (bounded) before this rank's memory goes away,
+// so that no rank still reads it; then the IPC mappings close.
+__global__ void k_peer_barrier(peer::Args a) {
+  if (threadIdx.x < a.size) {
+    __threadfence_system();
+    peer::st_release_sys(a.flags[threadIdx.x] + a.rank, (int)a.epoch);
+  }
+  peer::wait_all(a, 0);
+}
+static void peer_close(sr_model* m) {
+  PeerHost* ph = (PeerHost*)m->peer;
+  if (!ph) return;
+  if (ph->open && m->stream) {
+    peer::Args a{};
+    a.flags = (int* const*)(ph->tables + (size_t)2 * m->dm.tp_size);
+    a.err = ph->err;
+    a.epoch = ++ph->epoch;
+    a.rank = m->dm.tp_rank;
+    a.size = m->dm.tp_size;
+    cudaMemsetAsync(ph->err, 0, 4, m->stream);
+    k_peer_barrier<<<1, 64, 0, m->stream>>>(a);
+    cudaStreamSynchronize(m->stream);
+    cudaGetLastError();
+  }
+  for (void* p : ph->opened) cudaIpcCloseMemHandle(p);
+  delete ph;
+  m->peer = nullptr;
+}
+
+extern "C" int sr_tp_peer_handle(sr_model* m, void* handle_out) {
+  if (!m || !handle_out) return sr_fail(SR_EINVAL, "null argument");
+  PeerHost* ph = (PeerHost*)m->peer;
+  if (!ph) return sr_fail(SR_EINVAL, "not a tensor-parallel model");
+  CK(cudaSetDevice(m->device));
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, ph->base));
+  memcpy(handle_out, &h, sizeof(h));
+  return SR_OK;
+}
+
+extern "C" int sr_tp_peer_open(sr_model* m, const void* handles) {
+  if (!m || !handles) return sr_fail(SR_EINVAL, "null argument");
+  PeerHost* ph = (PeerHost*)m->peer;
+  if (!ph) return sr_fail(SR_EINVAL, "not a tensor-parallel model");
+  if (ph->open) return sr_fail(SR_EINVAL, "peer memory is already open");
+  const int size = m->dm.tp_size, rank = m->dm.tp_rank;
+  if (size > peer::kMaxRanks) return sr_fail(SR_EUNSUPPORTED, "peer all-reduce supports at most 64 ranks");
+  if (m->dm.dim % 4) return sr_fail(SR_EUNSUPPORTED, "peer all-reduce needs a model width divisible by 4");
+  CK(cudaSetDevice(m->device));
+  std::vector<void*> host((size_t)3 * size);
+  for (int q = 0; q < size; q++) {
+    uint8_t* b = ph->base;
+    if (q != rank) {
+      cudaIpcMemHandle_t h;
+      memcpy(&h, (const uint8_t*)handles + (size_t)q * SR_TP_PEER_HANDLE_BYTES, sizeof(h));
+      void* p = nullptr;
+      cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        for (void* o : ph->opened) cudaIpcCloseMemHandle(o);
+        ph->opened.clear();
+        return sr_fail(SR_EDEVICE, "opening rank " + std::to_string(q) + "'s memory: " + cudaGetErrorString(e));
+      }
+      ph->opened.push_back(p);
+      b = (uint8_t*)p;
+    }
+    host[q] = b;
+    host[size + q] = b + ph->buf_bytes;
+    host[2 * size + q] = b + 2 * ph->buf_bytes;
+  }
+  CK(cudaMemcpy(ph->tables, host.data(), host.size() * sizeof(void*), cudaMemcpyHostToDevice));
+  ph->open = true;
+  return SR_OK;
+}
+
+// After the step's stream synchronize: SR_ETIMEOUT if an all-reduce barrier
+// wait expired (a rank did not take part).
+static int tp_check(sr_model* m) {
+  PeerHost* ph = (PeerHost*)m->peer;
+  if (!ph || !ph->ran) return SR_OK;
+  ph->ran = false;
+  int h = 0;
+  if (cudaMemcpy(&h, ph->err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return sr_fail(SR_EDEVICE, "reading the all-reduce error flag failed");
+  }
+  if (h) {
+    cudaMemset(ph->err, 0, 4);
+    return sr_fail(SR_ETIMEOUT, "a tensor-parallel all-reduce barrier expired (a rank did not join the step)");
+  }
+  return SR_OK;
+}
+
 static int model_create(const sr_model_desc* desc, int device, int tp_rank, int tp_size, const void* nccl_id,
                         sr_model** out) {
   if (!desc || !out) return sr_fail(SR_EINVAL, "null argument");
@@ -303,8 +440,14 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
   {
     const int64_t R = kMaxRows;
     float** bufs[] = {&m->X, &m->N, &m->Q, &m->A, &m->T};
-    for (float** b : bufs)
+    for (float** b : bufs) {
+      if (b == &m->T && tp_size > 1) continue;  // the two all-reduce buffers below
       if ((rc = sr_model_alloc(m, (void**)b, (size_t)(R * d * 4))) != SR_OK) { free_model(m); return rc; }
+    }
+    if (tp_size > 1 && (rc = peer_alloc(m, (size_t)(R * d * 4))) != SR_OK) {
+      free_model(m);
+      return rc;
+    }
     if ((rc = sr_model_alloc(m, (void**)&m->K, (size_t)(R * kd * 4))) != SR_OK ||
         (rc = sr_model_alloc(m, (void**)&m->V, (size_t)(R * kd * 4))) != SR_OK ||
         (rc = sr_model_alloc(m, (void**)&m->G, (size_t)(R * h * 4))) != SR_OK ||
@@ -834,17 +977,45 @@ __global__ void k_add_inplace(float* __restrict__ X, const float* __restrict__ T
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
     X[i] += T[i];
 }
-static int tp_allreduce(sr_model* m, int n) {
-  nccl::Api& api = nccl::api();
+// Sums the ranks' partials in m->T (over peer memory once sr_tp_peer_open has
+// run, else NCCL), sets *sum to the summed buffer and points m->T at the other
+// buffer for the next row-parallel projection.
+static int tp_allreduce(sr_model* m, int n, const float** sum) {
+  PeerHost* ph = (PeerHost*)m->peer;
   const int64_t count = (int64_t)n * m->dm.dim;
-  const int r = api.AllReduce(m->T, m->T, (size_t)count, nccl::kFloat32, nccl::kSum, (nccl::Comm)m->nccl_comm,
-                              m->stream);
-  if (r != nccl::kSuccess) return sr_fail(SR_EDEVICE, std::string("ncclAllReduce: ") + api.GetErrorString(r));
+  float* T = m->T;
+  if (ph->open) {
+    peer::Args a;
+    a.bufs = (float* const*)(ph->tables + (size_t)ph->cur * m->dm.tp_size);
+    a.flags = (int* const*)(ph->tables + (size_t)2 * m->dm.tp_size);
+    a.counter = ph->counter;
+    a.err = ph->err;
+    a.count = count;
+    a.chunk = ((count + m->dm.tp_size - 1) / m->dm.tp_size + 3) / 4 * 4;
+    a.epoch = ++ph->epoch;
+    a.rank = m->dm.tp_rank;
+    a.size = m->dm.tp_size;
+    const int rb = (int)std::min<int64_t>(std::max<int64_t>((a.chunk / 4 + peer::kThreads - 1) / peer::kThreads, 1),
+                                          148 * 2);
+    const int gb = (int)std::min<int64_t>(std::max<int64_t>((count / 4 + peer::kThreads - 1) / peer::kThreads, 1),
+                                          148 * 4);
+    peer::k_peer_reduce<<<rb, peer::kThreads, 0, m->stream>>>(a);
+    peer::k_peer_gather<<<gb, peer::kThreads, 0, m->stream>>>(a);
+    sr_count_launch(m, 2);
+    ph->ran = true;
+  } else {
+    nccl::Api& api = nccl::api();
+    const int r = api.AllReduce(T, T, (size_t)count, nccl::kFloat32, nccl::kSum, (nccl::Comm)m->nccl_comm, m->stream);
+    if (r != nccl::kSuccess) return sr_fail(SR_EDEVICE, std::string("ncclAllReduce: ") + api.GetErrorString(r));
+  }
+  *sum = T;
+  ph->cur ^= 1;
+  m->T = ph->buf[ph->cur];
   return SR_OK;
 }
-static void tp_add(sr_model* m, int n) {
+static void tp_add(sr_model* m, int n, const float* T) {
   const int64_t count = (int64_t)n * m->dm.dim;
-  k_add_inplace<<<(int)std::min<int64_t>((count + 255) / 256, 148 * 8), 256, 0, m->stream>>>(m->X, m->T, count);
+  k_add_inplace<<<(int)std::min<int64_t>((count + 255) / 256, 148 * 8), 256, 0, m->stream>>>(m->X, T, count);
   sr_count_launch(m);
 }
 
@@ -868,7 +1039,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   int rc = SR_OK;
   __nv_bfloat16* xh = tc ? tc_xh(m) : nullptr;
   __nv_bfloat16* xl = tc ? tc_xl(m) : nullptr;
-  bool pending = false;  // tensor parallel: the all-reduced T is still to be added to X
+  const float* pending = nullptr;  // tensor parallel: an all-reduced sum still to be added to X
   for (int l = 0; l < L; l++) {
     if (cancel && *cancel) {
       sr_prof_span_end(m);
@@ -882,12 +1053,12 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     o.ldy = 0;
     o.resid = nullptr;
     o.out_map = nullptr;
-    if (pending && !fast) tp_add(m, n);
+    if (pending && !fast) tp_add(m, n, pending);
     SR_LAUNCH(m, SR_PROF_NORM,
               if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps, xh, xl,
-                                     pending ? m->T : nullptr);
+                                     pending);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps));
-    pending = false;
+    pending = nullptr;
     bool done;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_qkv(m, l, n, true));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
@@ -915,13 +1086,14 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_o(m, l, n, a_split, oy, ores));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->A, n, P[4], o);
+    const float* tsum = nullptr;
     if (tp) {
-      if ((rc = tp_allreduce(m, n)) != SR_OK) return rc;
-      if (!fast) tp_add(m, n);
+      if ((rc = tp_allreduce(m, n, &tsum)) != SR_OK) return rc;
+      if (!fast) tp_add(m, n, tsum);
     }
     SR_LAUNCH(m, SR_PROF_NORM,
               if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps, xh, xl,
-                                     tp ? m->T : nullptr);
+                                     tsum);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps));
     o.resid = nullptr;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_gateup(m, l, n, true));
@@ -938,16 +1110,14 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
               if (tc) k_swiglu_split<<<sw_blocks, 256, 0, s>>>(m->G, m->U, xh, xl, cnt);
               else k_swiglu_exact<<<sw_blocks, 256, 0, s>>>(m->G, m->U, m->H, cnt));
     sr_count_launch(m);
+    oy = tp ? m->T : m->X;  // the all-reduce above moved m->T to the other buffer
     o.y = oy; o.ldy = d; o.resid = ores;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_down(m, l, n, true, oy, ores));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->H, n, P[8], o);
-    if (tp) {
-      if ((rc = tp_allreduce(m, n)) != SR_OK) return rc;
-      pending = true;
-    }
+    if (tp && (rc = tp_allreduce(m, n, &pending)) != SR_OK) return rc;
   }
-  if (pending) tp_add(m, n);  // the final norm below gathers the head rows: a plain add
+  if (pending) tp_add(m, n, pending);  // the final norm below gathers the head rows: a plain add
   // Selected head (M:6420-6448): gather last rows, final norm, LM head into
   // the session's logits row; unselected rows are zero.
   CK(cudaMemsetAsync(m->logits, 0, (size_t)info.sessions * dm.vocab * 4, s));
@@ -994,6 +1164,7 @@ extern "C" int sr_step(sr_model* m, sr_kvpool* pool, const sr_batch* batch, floa
   CK(cudaStreamSynchronize(m->stream));
   sr_prof_resolve(m);
   if (int rc = fast_check(m)) return rc;
+  if (int rc = tp_check(m)) return rc;
   return tc_check(m);
 }
 
@@ -1070,6 +1241,7 @@ int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_o
   CK(cudaStreamSynchronize(m->stream));
   sr_prof_resolve(m);
   if (int rc = fast_check(m)) return rc;
+  if (int rc = tp_check(m)) return rc;
   if (int rc = tc_check(m)) return rc;
   uint8_t* h = (uint8_t*)m->h_stage + m->upload_ints * 4;
   const size_t off_hoff = kSampOffHistOff, off_hist = kSampOffHist, off_rng = kSampOffRng, off_ids = kSampOffIds,

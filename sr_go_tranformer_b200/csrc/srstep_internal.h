@@ -65,6 +65,7 @@ struct sr_model {
   sr_model_desc d;
   std::vector<Shard> shards;  // parallel to params
   void* nccl_comm = nullptr;
+  void* peer = nullptr;  // tensor-parallel peer-memory all-reduce state (tp_peer.cuh)
   int device = 0;
   int mode = SR_MODE_EXACT;
   sr::ModelDims dm;

@@ -105,6 +105,19 @@ class Model:
         except Exception:
             pass
 
+    def tp_peer_handle(self):
+        """This rank's CUDA IPC handle of its all-reduce buffers (bytes)."""
+        buf = C.create_string_buffer(A.SR_TP_PEER_HANDLE_BYTES)
+        A.check(A.lib().sr_tp_peer_handle(self.h, buf))
+        return buf.raw
+
+    def tp_peer_open(self, handles):
+        """Map every rank's buffers (handles in rank order) and all-reduce over
+        NVLink peer memory from now on instead of NCCL."""
+        blob = b"".join(bytes(h) for h in handles)
+        assert len(blob) == A.SR_TP_PEER_HANDLE_BYTES * self.tp_size
+        A.check(A.lib().sr_tp_peer_open(self.h, C.create_string_buffer(blob, len(blob))))
+
     @property
     def page_tokens(self):
         return self.desc.page_tokens

@@ -2,9 +2,14 @@
 
 Each rank holds its shard of the same synthetic model (the counter-based init
 generates every rank's part of one full model) and the step all-reduces the
-o_proj / down_proj partial sums over NCCL.  The summation order of those two
-projections changes, so logits are compared within the fast-path tolerance.
+o_proj / down_proj partial sums, over NCCL or over the library's NVLink
+peer-memory kernels.  The summation order of those two projections changes, so
+logits are compared within the fast-path tolerance; the ranks' logits must be
+identical.
 """
+
+import os
+import time
 
 import numpy as np
 import pytest
@@ -26,12 +31,29 @@ DESC = dict(vocab=2048, dim=1024, hidden=2048, layers=2, heads=8, kv_heads=4, co
             tied=False, weight_format="q8", page_tokens=16)
 
 
-def _run(rank, size, nccl_id, mode, q):
+def exchange_handles(m, rank, size, folder):
+    """Every rank's sr_tp_peer_handle through files in `folder` (bounded wait)."""
+    tmp = os.path.join(folder, f"h{rank}.tmp")
+    with open(tmp, "wb") as f:
+        f.write(m.tp_peer_handle())
+    os.replace(tmp, os.path.join(folder, f"h{rank}.bin"))
+    paths = [os.path.join(folder, f"h{r}.bin") for r in range(size)]
+    t0 = time.time()
+    while not all(os.path.exists(p) for p in paths):
+        assert time.time() - t0 < 120, "peer handles did not arrive"
+        time.sleep(0.05)
+    return [open(p, "rb").read() for p in paths]
+
+
+def _run(rank, size, nccl_id, mode, q, allreduce="nccl", folder=None):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     from sr_go_tranformer_b200 import step as S
     d = S.make_desc(**DESC)
     m = S.Model(d, device=rank, tp_rank=rank, tp_size=size, nccl_id=nccl_id)
     m.init_synthetic(123)
     m.set_mode(mode)
+    if allreduce == "peer":
+        m.tp_peer_open(exchange_handles(m, rank, size, folder))
     pool = S.PagePool(m, 128)
     rng = np.random.default_rng(5)
     prompts = [rng.integers(0, 2048, size=n).tolist() for n in (300, 45, 64, 40)]
@@ -40,16 +62,18 @@ def _run(rank, size, nccl_id, mode, q):
     for _ in range(2):
         toks = [int(np.argmax(x)) for x in outs[-1]]
         outs.append(m.decode_batch(caches, toks))
+    pool.close()
+    m.close()  # every rank: the peer all-reduce's last barrier
     q.put((rank, outs))
 
 
-def _tp_logits(size, mode):
+def _tp_logits(size, mode, allreduce="nccl", folder=None):
     import multiprocessing as mp
     from sr_go_tranformer_b200 import step as S
     nccl_id = S.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_run, args=(r, size, nccl_id, mode, q)) for r in range(size)]
+    procs = [ctx.Process(target=_run, args=(r, size, nccl_id, mode, q, allreduce, folder)) for r in range(size)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in procs)
@@ -71,12 +95,13 @@ def _single_logits(mode):
     return r[1]
 
 
+@pytest.mark.parametrize("allreduce", ["nccl", "peer"])
 @pytest.mark.parametrize("size", [2, 4])
 @pytest.mark.parametrize("mode", ["exact", "fast"])
-def test_tp_matches_single_gpu(mode, size):
+def test_tp_matches_single_gpu(mode, size, allreduce, tmp_path):
     if _gpus() < size:
         pytest.skip(f"needs {size} GPUs")
-    tp = _tp_logits(size, mode)
+    tp = _tp_logits(size, mode, allreduce, str(tmp_path))
     single = _single_logits(mode)
     for step in range(len(single)):
         b = single[step]
@@ -85,3 +110,58 @@ def test_tp_matches_single_gpu(mode, size):
         err = float(np.abs(tp[0][step] - b).max())
         assert err <= ATOL, f"{mode} step {step}: TP{size} logits differ from 1 GPU by {err:.3g}"
         assert (np.argmax(tp[0][step], 1) == np.argmax(b, 1)).mean() >= 0.75
+
+
+def _absent_rank(rank, q, folder, done):
+    """Rank 1 maps the peers but never joins a step; rank 0's step must end with
+    SR_ETIMEOUT from its bounded barrier wait (the flag nothing sets)."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from sr_go_tranformer_b200 import step as S
+    from sr_go_tranformer_b200 import _abi as A
+    d = S.make_desc(**DESC)
+    nccl_id = open(os.path.join(folder, "nccl_id"), "rb").read()
+    m = S.Model(d, device=rank, tp_rank=rank, tp_size=2, nccl_id=nccl_id)
+    m.init_synthetic(123)
+    m.set_mode("fast")
+    m.tp_peer_open(exchange_handles(m, rank, 2, folder))
+    code = None
+    if rank == 0:
+        pool = S.PagePool(m, 16)
+        caches = [m.new_cache(pool)]
+        t0 = time.time()
+        try:
+            m.prefill_selected(caches, [[1, 2, 3]])
+        except A.SRError as e:
+            code = e.code
+        elapsed = time.time() - t0
+        pool.close()
+        done.set()
+        q.put((code, elapsed, caches[0].pos))
+    else:
+        assert done.wait(120)  # stay mapped until rank 0's step has returned
+    m.close()
+
+
+def test_peer_allreduce_absent_rank_times_out(tmp_path):
+    """Failure detection without a GPU fault: a rank that never joins makes the
+    other's barrier wait expire after its bound; the step reports SR_ETIMEOUT
+    and commits nothing."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    from sr_go_tranformer_b200 import step as S
+    from sr_go_tranformer_b200 import _abi as A
+    with open(tmp_path / "nccl_id", "wb") as f:
+        f.write(S.tp_unique_id())
+    ctx = mp.get_context("spawn")
+    q, done = ctx.Queue(), ctx.Event()
+    procs = [ctx.Process(target=_absent_rank, args=(r, q, str(tmp_path), done)) for r in range(2)]
+    for p in procs:
+        p.start()
+    code, elapsed, pos = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert code == A.SR_ETIMEOUT
+    assert elapsed < 30
+    assert pos == 0
