@@ -318,8 +318,9 @@ def main():
     ap.add_argument("--ref-sessions", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"])
-    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
-                    help="tensor-parallel all-reduce: the library's NVLink peer-memory kernels or NCCL")
+    ap.add_argument("--allreduce", default="auto", choices=["auto", "peer", "nccl"],
+                    help="tensor-parallel all-reduce: the library's NVLink peer-memory kernels, NCCL, or auto "
+                         "(peer at 2 ranks, NCCL above: the faster one measured at each size)")
     ap.add_argument("--no-ttft", action="store_true", help="skip the serving run that measures TTFT")
     args = ap.parse_args()
     cfg = dict(CONFIG)
@@ -347,6 +348,8 @@ def main():
             dist.broadcast_object_list(obj, src=0)
             tp_args = (rank, world, obj[0])
     model = make_model(cfg, local, args.mode, tp=tp_args)
+    if args.allreduce == "auto":
+        args.allreduce = "peer" if world == 2 else "nccl"
     if tp and args.allreduce == "peer":
         handles = [None] * world
         dist.all_gather_object(handles, model.tp_peer_handle())
