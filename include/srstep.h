@@ -112,12 +112,13 @@ const char *sr_version(void);
  * RoPE tables (:5034-5043) and the step workspace (decodeWorkspace,
  * :6064-6096; bounded by maxActivationElements, :50). */
 int sr_model_create(const sr_model_desc *desc, int device, sr_model **out);
-/* Tensor-parallel rank `tp_rank` of `tp_size` (SURVEY-style sharding of the
+/* Tensor-parallel rank `tp_rank` of `tp_size` (Megatron-style sharding of the
  * reference model; the reference itself has no multi-GPU path): Q/K/V and
  * gate/up keep a contiguous block of output rows (whole heads / FFN columns),
  * o_proj and down_proj the matching block of input columns, the KV pool holds
  * only this rank's KV heads, and embedding, norms and LM head are replicated.
- * The step all-reduces (NCCL, fp32 sum) after o_proj and down_proj.  nccl_id is
+ * The step all-reduces (fp32 sum; NCCL, or peer memory after
+ * sr_tp_peer_open) after o_proj and down_proj.  nccl_id is
  * the 128-byte id from sr_tp_unique_id on rank 0, shared with every rank;
  * creation blocks until all ranks have joined.  Requires heads, kv_heads and
  * hidden divisible by tp_size (and, for quantized weights, column shards of

@@ -319,7 +319,10 @@ def test_context_limit(tmp_path):
         hf.open_hf_archive(d, 129)
 
 
-REF_TESTDATA = "/root/reference/testdata"
+# A reference checkout: SR_REFERENCE_ROOT, else a "reference" directory beside this repository.
+REF_TESTDATA = os.path.join(os.environ.get("SR_REFERENCE_ROOT") or
+                            os.path.join(os.path.dirname(os.path.dirname(GOLDEN_DIR)), "..", "reference"),
+                            "testdata")
 
 
 @pytest.mark.skipif(not os.path.isdir(REF_TESTDATA), reason="no reference checkout")
