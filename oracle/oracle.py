@@ -26,7 +26,8 @@ class Config(C.Structure):
                 ("rope_theta", C.c_double), ("norm_eps", C.c_double), ("tied", C.c_int32),
                 ("qkv_bias", C.c_int32), ("weight_format", C.c_int32), ("page_tokens", C.c_int32),
                 ("rope_scaling", C.c_int32), ("rope_factor", C.c_double), ("rope_low", C.c_double),
-                ("rope_high", C.c_double), ("rope_original", C.c_int32)]
+                ("rope_high", C.c_double), ("rope_original", C.c_int32), ("gpt2", C.c_int32),
+                ("positions", C.c_int32)]
 
 
 class ParamInfo(C.Structure):
@@ -101,8 +102,19 @@ def _p(a):
 
 
 def config_from_hf(hf, weight_format="f32", page_tokens=32, context=None):
-    """Translate an HF config.json dict the way readHFConfig does (M:253-385)."""
+    """Translate an HF config.json dict the way readHFConfig does (M:253-385),
+    or readGPT2Config (M:446-513) for model_type gpt2."""
     c = Config()
+    if hf.get("model_type") == "gpt2":
+        c.vocab, c.dim, c.layers = hf["vocab_size"], hf["n_embd"], hf["n_layer"]
+        c.hidden = hf.get("n_inner") or 4 * c.dim
+        c.heads = c.kv_heads = hf["n_head"]
+        c.positions = hf["n_positions"]
+        c.context = context or min(c.positions, 2048)
+        c.rope_theta, c.norm_eps = 10000.0, float(hf.get("layer_norm_epsilon", 1e-5))
+        c.tied, c.qkv_bias, c.gpt2 = 1, 0, 1
+        c.weight_format, c.page_tokens = FORMATS[weight_format], page_tokens
+        return c
     c.vocab = hf["vocab_size"]
     c.dim = hf["hidden_size"]
     c.hidden = hf["intermediate_size"]

@@ -281,6 +281,31 @@ void or_rmsnorm(float *y, const float *x, const float *w, int64_t n, int64_t d, 
     }
 }
 
+/* layerNormInto (M:5167-5185): fp64 mean and variance in element order, then
+ * float32((x - mean) * inv) * w + b in float32. */
+void or_layernorm(float *y, const float *x, const float *w, const float *b, int64_t n, int64_t d, double eps) {
+    for (int64_t r = 0; r < n; r++) {
+        const float *xr = x + r * d;
+        double mean = 0, variance = 0;
+        for (int64_t j = 0; j < d; j++) mean += (double)xr[j];
+        mean /= (double)d;
+        for (int64_t j = 0; j < d; j++) {
+            double z = (double)xr[j] - mean;
+            variance += z * z;
+        }
+        double inv = 1 / sqrt(variance / (double)d + eps);
+        for (int64_t j = 0; j < d; j++) y[r * d + j] = (float)(((double)xr[j] - mean) * inv) * w[j] + b[j];
+    }
+}
+
+/* gelu_new as the reference writes it (M:6405-6407), left to right in fp64.
+ * The constant is the double nearest 2/pi (Go folds 2/math.Pi exactly; here
+ * 2.0/M_PI rounds to the same double). */
+float or_gelu_tanh(float v) {
+    double x = (double)v;
+    return (float)(0.5 * x * (1 + tanh(sqrt(0x1.45f306dc9c883p-1) * (x + 0.044715 * x * x * x))));
+}
+
 /* attend (M:5293-5352). */
 double or_attend(const float *q, float *out, float *scores, int64_t hd, int64_t length, const float *const *krows,
                  const float *const *vrows) {
@@ -358,10 +383,11 @@ or_model *or_model_new(const or_config *c) {
         (c->dim / c->heads) % 2 || c->layers < 1 || c->vocab < 1 || c->hidden < 1 || c->context < 1 ||
         c->page_tokens < 1)
         return NULL;
+    if (c->gpt2 && (c->kv_heads != c->heads || !c->tied || c->qkv_bias || c->positions < c->context)) return NULL;
     or_model *m = (or_model *)calloc(1, sizeof(or_model));
     m->c = *c;
     int32_t L = c->layers, d = c->dim, kd = c->dim / c->heads * c->kv_heads, h = c->hidden;
-    m->nparams = 1 + 9 * L + 1 + (c->qkv_bias ? 3 * L : 0) + (c->tied ? 0 : 1);
+    m->nparams = c->gpt2 ? 4 + 16 * L : 1 + 9 * L + 1 + (c->qkv_bias ? 3 * L : 0) + (c->tied ? 0 : 1);
     m->params = (or_param *)calloc((size_t)m->nparams, sizeof(or_param));
     int32_t i = 0;
 #define P(R, C, MAT, EH)                                                                                               \
@@ -371,6 +397,30 @@ or_model *or_model_new(const or_config *c) {
         m->params[i].format = param_format(c, (MAT), (EH));                                                            \
         i++;                                                                                                           \
     } while (0)
+    if (c->gpt2) { /* loadGPT2's parameter order (M:5063-5066, 5114-5122) */
+        P(c->vocab, d, 1, 1);
+        P(c->positions, d, 0, 0);
+        P(1, d, 0, 0);
+        P(1, d, 0, 0);
+        for (int32_t l = 0; l < L; l++) {
+            P(1, d, 0, 0);
+            P(1, d, 0, 0);
+            P(d, d, 1, 0);
+            P(d, d, 1, 0);
+            P(d, d, 1, 0);
+            P(1, d, 0, 0);
+            P(1, d, 0, 0);
+            P(1, d, 0, 0);
+            P(d, d, 1, 0);
+            P(1, d, 0, 0);
+            P(1, d, 0, 0);
+            P(1, d, 0, 0);
+            P(h, d, 1, 0);
+            P(1, h, 0, 0);
+            P(d, h, 1, 0);
+            P(1, d, 0, 0);
+        }
+    } else {
     P(c->vocab, d, 1, 1); /* hfTensorSpecs order (M:407-423) */
     for (int32_t l = 0; l < L; l++) {
         P(1, d, 0, 0);
@@ -391,6 +441,7 @@ or_model *or_model_new(const or_config *c) {
             P(1, kd, 0, 0);
         }
     if (!c->tied) P(c->vocab, d, 1, 1);
+    }
 #undef P
     for (i = 0; i < m->nparams; i++) {
         or_param *p = &m->params[i];
@@ -449,6 +500,7 @@ int or_model_get_param(const or_model *m, int32_t index, void *values, float *sc
 /* One SplitMix64 stream over every matrix and bias element in hfProfileSpecs
  * order; norms are 1 (native convention M:5212-5219 with HF semantics). */
 int or_model_init_synthetic(or_model *m, uint64_t seed, double scale) {
+    if (m->c.gpt2) return 1; /* no native initialisation for the GPT-2 profile */
     uint64_t state = seed;
     int32_t L = m->c.layers;
     for (int32_t i = 0; i < m->nparams; i++) {
@@ -502,6 +554,7 @@ static void synth_rows(void *arg, int64_t lo, int64_t hi) {
     free(tmp);
 }
 int or_model_init_synthetic_mt(or_model *m, uint64_t seed, double scale, int threads) {
+    if (m->c.gpt2) return 1;
     int32_t L = m->c.layers;
     uint64_t e0 = 0;
     for (int32_t i = 0; i < m->nparams; i++) {
@@ -624,6 +677,10 @@ int or_step(or_model *m, float *pool, int64_t num_pages, int32_t sessions, const
             if (positions[r] + 1 > max_pos) max_pos = positions[r] + 1;
             const or_param *E = &m->params[0];
             or_copy_row(E->values, E->scales, E->format, d, tokens[j], X + r * d);
+            if (c->gpt2) { /* absolute position row (M:6369-6371) */
+                const float *wpe = (const float *)m->params[1].values + (int64_t)positions[r] * d;
+                for (int32_t e = 0; e < d; e++) X[r * d + e] += wpe[e];
+            }
             r++;
         }
         last_rows[i] = (int32_t)(r - 1);
@@ -633,21 +690,29 @@ int or_step(or_model *m, float *pool, int64_t num_pages, int32_t sessions, const
     float *scores = (float *)malloc((size_t)(lanes * stride) * 4);
     const float **kr = (const float **)malloc((size_t)(lanes * stride) * sizeof(float *));
     const float **vr = (const float **)malloc((size_t)(lanes * stride) * sizeof(float *));
+#define FV(p) ((const float *)(p).values)
     for (int32_t l = 0; l < L; l++) { /* layer loop (M:6376-6419) */
         const or_param *P = &m->params[1 + 9 * l];
-        or_rmsnorm(N, X, (const float *)P[0].values, n, d, c->norm_eps);
-        linear_p(Q, N, n, &P[1], threads);
-        linear_p(K, N, n, &P[2], threads);
-        linear_p(Vv, N, n, &P[3], threads);
-        if (c->qkv_bias) { /* addBias (M:3933-3940) */
-            const or_param *B = &m->params[2 + 9 * L + 3 * l];
-            for (int64_t e = 0; e < n * d; e++) Q[e] += ((const float *)B[0].values)[e % d];
-            for (int64_t e = 0; e < n * kd; e++) K[e] += ((const float *)B[1].values)[e % kd];
-            for (int64_t e = 0; e < n * kd; e++) Vv[e] += ((const float *)B[2].values)[e % kd];
+        const or_param *G2 = &m->params[4 + 16 * l]; /* GPT-2 block (loadGPT2 order) */
+        const or_param *wq = c->gpt2 ? &G2[2] : &P[1], *wk = c->gpt2 ? &G2[3] : &P[2], *wv = c->gpt2 ? &G2[4] : &P[3];
+        if (c->gpt2)
+            or_layernorm(N, X, FV(G2[0]), FV(G2[1]), n, d, c->norm_eps);
+        else
+            or_rmsnorm(N, X, FV(P[0]), n, d, c->norm_eps);
+        linear_p(Q, N, n, wq, threads);
+        linear_p(K, N, n, wk, threads);
+        linear_p(Vv, N, n, wv, threads);
+        if (c->qkv_bias || c->gpt2) { /* addBias (M:3933-3940) */
+            const or_param *B = c->gpt2 ? &G2[5] : &m->params[2 + 9 * L + 3 * l];
+            for (int64_t e = 0; e < n * d; e++) Q[e] += FV(B[0])[e % d];
+            for (int64_t e = 0; e < n * kd; e++) K[e] += FV(B[1])[e % kd];
+            for (int64_t e = 0; e < n * kd; e++) Vv[e] += FV(B[2])[e % kd];
         }
         for (int64_t i = 0; i < n; i++) { /* RoPE + KV write (M:6384-6396) */
-            rope_row(m, Q + i * d, H, positions[i]);
-            rope_row(m, K + i * kd, Hkv, positions[i]);
+            if (!c->gpt2) {
+                rope_row(m, Q + i * d, H, positions[i]);
+                rope_row(m, K + i * kd, Hkv, positions[i]);
+            }
             int64_t page = page_ids[row_page_base[i] + positions[i] / pt];
             int64_t base = page * pe + (int64_t)l * 2 * pt * kd + (int64_t)(positions[i] % pt) * kd;
             memcpy(pool + base, K + i * kd, (size_t)kd * 4);
@@ -670,9 +735,22 @@ int or_step(or_model *m, float *pool, int64_t num_pages, int32_t sessions, const
         J.vr = vr;
         attn_outer O = {&J, lanes};
         parallel_for(lanes, lanes, attn_lane, &O);
+        if (c->gpt2) { /* O projection + bias + residual, LayerNorm, c_fc + bias, GELU (M:6398-6408) */
+            linear_p(T, A, n, &G2[8], threads);
+            for (int64_t e = 0; e < n * d; e++) T[e] += FV(G2[9])[e % d];
+            for (int64_t e = 0; e < n * d; e++) X[e] += T[e];
+            or_layernorm(N, X, FV(G2[10]), FV(G2[11]), n, d, c->norm_eps);
+            linear_p(G, N, n, &G2[12], threads);
+            for (int64_t e = 0; e < n * hid; e++) G[e] += FV(G2[13])[e % hid];
+            for (int64_t e = 0; e < n * hid; e++) Hh[e] = or_gelu_tanh(G[e]);
+            linear_p(T, Hh, n, &G2[14], threads); /* c_proj + bias + residual (M:6415-6417) */
+            for (int64_t e = 0; e < n * d; e++) T[e] += FV(G2[15])[e % d];
+            for (int64_t e = 0; e < n * d; e++) X[e] += T[e];
+            continue;
+        }
         linear_p(T, A, n, &P[4], threads); /* O projection + residual (M:6398-6400) */
         for (int64_t e = 0; e < n * d; e++) X[e] += T[e];
-        or_rmsnorm(N, X, (const float *)P[5].values, n, d, c->norm_eps);
+        or_rmsnorm(N, X, FV(P[5]), n, d, c->norm_eps);
         linear_p(G, N, n, &P[6], threads);
         linear_p(U, N, n, &P[7], threads);
         for (int64_t e = 0; e < n * hid; e++) /* SwiGLU (M:6410-6413) */
@@ -689,7 +767,10 @@ int or_step(or_model *m, float *pool, int64_t num_pages, int32_t sessions, const
         }
     float *compact = heads ? (float *)malloc((size_t)(heads * V) * 4) : NULL;
     if (heads) {
-        or_rmsnorm(N, T, (const float *)m->params[1 + 9 * L].values, heads, d, c->norm_eps);
+        if (c->gpt2)
+            or_layernorm(N, T, FV(m->params[2]), FV(m->params[3]), heads, d, c->norm_eps);
+        else
+            or_rmsnorm(N, T, FV(m->params[1 + 9 * L]), heads, d, c->norm_eps);
         const or_param *head = c->tied ? &m->params[0] : &m->params[m->nparams - 1];
         linear_p(compact, N, heads, head, threads);
     }
@@ -702,6 +783,7 @@ int or_step(or_model *m, float *pool, int64_t num_pages, int32_t sessions, const
             memset(logits + (int64_t)i * V, 0, (size_t)V * 4);
         }
     }
+#undef FV
     free(compact);
     free(X), free(N), free(Q), free(K), free(Vv), free(A), free(T), free(G), free(U), free(Hh);
     free(positions), free(row_page_base), free(last_rows), free(scores), free(kr), free(vr);

@@ -45,6 +45,15 @@ typedef struct or_config {
     int32_t rope_scaling;
     double rope_factor, rope_low, rope_high;
     int32_t rope_original;
+    /* GPT-2 profile (loadGPT2 M:5052-5165, step branches M:6369-6371, 6389,
+     * 6403-6408): absolute positions (wpe, `positions` rows), affine LayerNorm,
+     * biases on every projection, GELU-tanh MLP, tied head, no RoPE.
+     * Parameters, in loadGPT2's order: wte, wpe, ln_f.weight, ln_f.bias, then
+     * per layer ln_1.weight, ln_1.bias, q, k, v, q bias, k bias, v bias, o, o
+     * bias, ln_2.weight, ln_2.bias, c_fc, c_fc bias, c_proj, c_proj bias, with
+     * every matrix [out, in] (the transposed HF Conv1D). */
+    int32_t gpt2;
+    int32_t positions;
 } or_config;
 
 typedef struct or_param_info {
@@ -76,6 +85,10 @@ void or_linear(float *y, const float *x, int64_t n, int format, const void *valu
                int64_t out, int64_t in, int threads);
 /* rmsInto (M:6182-6194). */
 void or_rmsnorm(float *y, const float *x, const float *w, int64_t n, int64_t d, double eps);
+/* layerNormInto (M:5167-5185). */
+void or_layernorm(float *y, const float *x, const float *w, const float *b, int64_t n, int64_t d, double eps);
+/* GPT-2's gelu_new (M:6405-6407): float32(0.5x(1+tanh(sqrt(2/pi)(x+0.044715x^3)))) in fp64. */
+float or_gelu_tanh(float v);
 /* attend (M:5293-5352) over `length` positions given K/V rows by pointer table. */
 double or_attend(const float *q, float *out, float *scores, int64_t hd, int64_t length, const float *const *krows,
                  const float *const *vrows);

@@ -17,8 +17,15 @@ per fixture next to itself, holding:
   cache_k/v   float32[layers, 37, kv_dim]
   weight_sha256  the fixture's pinned weight digest (checked here)
 
+The GPT-2 fixtures (`testdata/hf-gpt2/{legacy-f32,f16,bf16}`) go to
+`gpt2/hf-gpt2-<variant>.npz` in loadGPT2's parameter order
+(cmd/monolith/monolith.go:5052-5165): the Conv1D weights ([in, out]) are
+transposed to [out, in], c_attn is split into q, k, v and its bias likewise, and
+the legacy causal-mask tensors are checked (ones on and below the diagonal)
+and dropped.  They sit in a subfolder because the device step does not run the
+GPT-2 profile yet.
+
 Usage:  python tests/golden/make_golden.py <reference checkout root>
-GPT-2 fixtures are out of scope and skipped.
 """
 
 import hashlib
@@ -35,6 +42,7 @@ FIXTURES = [
     "hf-qwen2/f32", "hf-qwen2/f16", "hf-qwen2/untied-bf16",
     "hf-mistral/f32", "hf-mistral/f16", "hf-mistral/bf16",
 ]
+GPT2_FIXTURES = ["hf-gpt2/legacy-f32", "hf-gpt2/f16", "hf-gpt2/bf16"]
 
 
 def read_safetensors(path):
@@ -82,6 +90,27 @@ def spec_names(cfg):
     return names
 
 
+def gpt2_params(cfg, tensors):
+    """loadGPT2's parameter order with [out, in] matrices (M:5052-5165)."""
+    t = {k[len("transformer."):] if k.startswith("transformer.") else k: v for k, v in tensors.items()}
+    d, L, ctx = cfg["n_embd"], cfg["n_layer"], cfg["n_positions"]
+    out = [t["wte.weight"], t["wpe.weight"], t["ln_f.weight"], t["ln_f.bias"]]
+    for i in range(L):
+        p = f"h.{i}."
+        mask = t.get(p + "attn.bias")
+        if mask is not None:
+            want = np.tril(np.ones((ctx, ctx), dtype=np.float32)).reshape(1, 1, ctx, ctx)
+            if not np.array_equal(mask, want):
+                raise SystemExit(f"{p}attn.bias: invalid legacy causal mask")
+        w = t[p + "attn.c_attn.weight"].T  # [3d, d]
+        b = t[p + "attn.c_attn.bias"]
+        out += [t[p + "ln_1.weight"], t[p + "ln_1.bias"], w[:d], w[d:2 * d], w[2 * d:], b[:d], b[d:2 * d], b[2 * d:],
+                t[p + "attn.c_proj.weight"].T, t[p + "attn.c_proj.bias"], t[p + "ln_2.weight"], t[p + "ln_2.bias"],
+                t[p + "mlp.c_fc.weight"].T, t[p + "mlp.c_fc.bias"], t[p + "mlp.c_proj.weight"].T,
+                t[p + "mlp.c_proj.bias"]]
+    return out
+
+
 def convert(root, fixture, outdir):
     d = os.path.join(root, "testdata", fixture)
     cfg = json.load(open(os.path.join(d, "config.json")))
@@ -96,8 +125,12 @@ def convert(root, fixture, outdir):
               "logits": np.array(ref["logits"], dtype=np.float32),
               "cache_k": np.array([c["k"] for c in ref["cache"]], dtype=np.float32),
               "cache_v": np.array([c["v"] for c in ref["cache"]], dtype=np.float32)}
-    for i, name in enumerate(spec_names(cfg)):
-        arrays[f"param_{i}"] = np.ascontiguousarray(tensors[name].astype(np.float32))
+    if cfg["model_type"] == "gpt2":
+        for i, a in enumerate(gpt2_params(cfg, tensors)):
+            arrays[f"param_{i}"] = np.ascontiguousarray(a.astype(np.float32))
+    else:
+        for i, name in enumerate(spec_names(cfg)):
+            arrays[f"param_{i}"] = np.ascontiguousarray(tensors[name].astype(np.float32))
     name = fixture.replace("/", "-")
     np.savez_compressed(os.path.join(outdir, name + ".npz"), **arrays)
     return name
@@ -110,6 +143,9 @@ def main():
     outdir = os.path.dirname(os.path.abspath(__file__))
     for f in FIXTURES:
         print("wrote", convert(root, f, outdir))
+    os.makedirs(os.path.join(outdir, "gpt2"), exist_ok=True)
+    for f in GPT2_FIXTURES:
+        print("wrote", convert(root, f, os.path.join(outdir, "gpt2")))
 
 
 if __name__ == "__main__":

@@ -6,10 +6,17 @@ the returned last-row logits and every layer's K/V with the goldens at abs
 tolerance 2e-5; then a ragged two-session prefill + decode batch.
 """
 
+import glob
+import os
+
 import numpy as np
 import pytest
 
-from conftest import GOLDEN
+from conftest import GOLDEN, GOLDEN_DIR
+
+# GPT-2 fixtures (hf-gpt2/{legacy-f32,f16,bf16}): the oracle's GPT-2 profile
+# (loadGPT2 M:5052-5165, step branches M:6369-6408) against the same goldens.
+GPT2 = sorted(glob.glob(os.path.join(GOLDEN_DIR, "gpt2", "*.npz")))
 
 TOL = 2e-5  # hf_inference_test.go: hfNear(..., 2e-5)
 
@@ -21,7 +28,7 @@ def _near(got, want, tol=TOL):
     assert err <= tol, f"max abs error {err:.3g} > {tol}"
 
 
-@pytest.mark.parametrize("path", GOLDEN, ids=lambda p: p.split("/")[-1][:-4])
+@pytest.mark.parametrize("path", GOLDEN + GPT2, ids=lambda p: p.split("/")[-1][:-4])
 def test_oracle_matches_transformers(oracle, path):
     m, z, hf = oracle.load_golden(path)
     ids, ref = z["ids"], z["logits"]
@@ -76,3 +83,20 @@ def test_oracle_selected_rows_zeroed(oracle):
     lg = m.step(pool, [0, 0], [ids[:5], ids[:3]], [[0], [1]], want_logits=[False, True])
     assert not lg[0].any()
     _near(lg[1], z["logits"][2])
+
+
+def test_gpt2_fixtures_present():
+    assert len(GPT2) == 3
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4-mixed"])
+def test_oracle_gpt2_quantized_close(oracle, fmt):
+    """Quantized GPT-2 storage (the same readParam quantizer on the transposed
+    Conv1D matrices, M:5072-5108) stays near the fp32 logits."""
+    m32, z, _ = oracle.load_golden(GPT2[0])
+    mq, _, _ = oracle.load_golden(GPT2[0], weight_format=fmt)
+    ids = z["ids"]
+    a = m32.step(np.zeros(2 * m32.page_elements, np.float32), [0], [ids[:37]], [[0, 1]])
+    b = mq.step(np.zeros(2 * mq.page_elements, np.float32), [0], [ids[:37]], [[0, 1]])
+    err = float(np.abs(a - b).max())
+    assert 0 < err < (0.05 if fmt == "q8" else 0.5), err
