@@ -20,8 +20,13 @@ Llama / Qwen2 / full-attention Mistral profiles the step runs:
                       the reference's block quantizer (readParam M:857-880); a
                       tensor-parallel rank keeps its shard of each full tensor.
 
-Errors raise HFError with the reference's messages.  GPT-2 archives are not
-supported by this build (their step variant is not implemented).
+GPT-2 archives (readGPT2Config M:446-513, gpt2Specs M:515-530) open and read
+the same way; HFArchive.params() gives their tensors in loadGPT2's parameter
+order (M:5052-5165: Conv1D weights transposed to [out, in], c_attn split into
+q, k, v), with the legacy causal masks checked.  The device step does not run
+the GPT-2 profile yet, so load_hf_model refuses them.
+
+Errors raise HFError with the reference's messages.
 """
 
 import json
@@ -32,6 +37,7 @@ import numpy as np
 MAX_HF_HEADER = 4 << 20          # maxHFHeader (M:123)
 MAX_HF_VOCAB = 262144            # maxHFVocab (M:49)
 MAX_HF_PARAMETERS = 8_000_000_000  # maxHFParameters (M:48)
+MAX_ACTIVATION_ELEMENTS = 128 * 1024 * 1024  # maxActivationElements (M:50)
 BASE_VOCAB = 258                 # baseVocab (M:46)
 WIDTH = {"F32": 4, "F16": 2, "BF16": 2}  # hfWidth (M:634-642)
 
@@ -41,6 +47,12 @@ _ALLOWED = ("architectures model_type vocab_size hidden_size intermediate_size n
             "bos_token_id eos_token_id pad_token_id initializer_range is_llama_config torch_dtype dtype "
             "transformers_version transformers.js_config use_cache _name_or_path _attn_implementation").split()
 _ARCH = {"llama": "LlamaForCausalLM", "qwen2": "Qwen2ForCausalLM", "mistral": "MistralForCausalLM"}
+_GPT2_ALLOWED = ("architectures model_type vocab_size n_embd n_inner n_layer n_head n_positions n_ctx "
+                 "layer_norm_epsilon activation_function scale_attn_weights scale_attn_by_inverse_layer_idx "
+                 "reorder_and_upcast_attn add_cross_attention tie_word_embeddings bos_token_id eos_token_id "
+                 "pad_token_id attn_pdrop resid_pdrop embd_pdrop initializer_range torch_dtype dtype "
+                 "transformers_version use_cache _name_or_path _attn_implementation summary_type summary_use_proj "
+                 "summary_activation summary_proj_to_labels summary_first_dropout task_specific_params").split()
 
 
 class HFError(ValueError):
@@ -140,14 +152,17 @@ class HFConfig:
         self.extra_eos = []
         self.rope = None
         self.context = context
+        self.positions = self.max_positions  # wpe rows (GPT-2)
 
     @property
     def kv_dim(self):
         return self.dim // self.heads * self.kv_heads
 
     def parameter_count(self):
-        """hfParameterCount (M:387-398) for the RMSNorm profiles."""
+        """hfParameterCount (M:387-398)."""
         d, h, k, l = self.dim, self.hidden, self.kv_dim, self.layers
+        if self.model_type == "gpt2":
+            return (self.vocab + self.positions) * d + l * (4 * d * d + 2 * d * h + 9 * d + h) + 2 * d
         n = self.vocab * d + l * (2 * d + 2 * d * d + 2 * d * k + 3 * d * h) + d
         if self.model_type == "qwen2":
             n += l * (d + 2 * k)
@@ -156,8 +171,20 @@ class HFConfig:
         return n
 
     def specs(self):
-        """hfProfileSpecs (M:407-442): (name, shape) in parameter order."""
+        """hfProfileSpecs (M:407-442): (name, shape) in parameter order; for
+        GPT-2 the archive's tensors (gpt2Specs, M:515-530)."""
         d, k, h, L = self.dim, self.kv_dim, self.hidden, self.layers
+        if self.model_type == "gpt2":
+            out = [("wte.weight", (self.vocab, d)), ("wpe.weight", (self.positions, d)), ("ln_f.weight", (d,)),
+                   ("ln_f.bias", (d,))]
+            for i in range(L):
+                p = f"h.{i}."
+                out += [(p + "ln_1.weight", (d,)), (p + "ln_1.bias", (d,)), (p + "attn.c_attn.weight", (d, 3 * d)),
+                        (p + "attn.c_attn.bias", (3 * d,)), (p + "attn.c_proj.weight", (d, d)),
+                        (p + "attn.c_proj.bias", (d,)), (p + "ln_2.weight", (d,)), (p + "ln_2.bias", (d,)),
+                        (p + "mlp.c_fc.weight", (d, h)), (p + "mlp.c_fc.bias", (h,)),
+                        (p + "mlp.c_proj.weight", (h, d)), (p + "mlp.c_proj.bias", (d,))]
+            return out
         out = [("model.embed_tokens.weight", (self.vocab, d))]
         for i in range(L):
             p = f"model.layers.{i}."
@@ -175,8 +202,20 @@ class HFConfig:
             out.append(("lm_head.weight", (self.vocab, d)))
         return out
 
+    def optional(self):
+        """Legacy GPT-2 causal masks (M:693-701): accepted, F32 only, when small."""
+        if self.model_type != "gpt2" or self.positions * self.positions * self.layers > MAX_ACTIVATION_ELEMENTS:
+            return {}
+        return {f"h.{i}.attn.bias": (1, 1, self.positions, self.positions) for i in range(self.layers)}
+
+    def canonical(self, name):
+        """GPT-2 archives may prefix every tensor with "transformer." (M:687-692)."""
+        return name[len("transformer."):] if self.model_type == "gpt2" and name.startswith("transformer.") else name
+
     def desc(self, weight_format="f32", page_tokens=32):
         """sr_model_desc of this profile (readHFConfig's Config plus the RoPE scaling)."""
+        if self.model_type == "gpt2":
+            raise HFError("the device step does not run the GPT-2 profile yet")
         from .step import desc_from_hf
         hf = dict(self.raw)
         hf["num_key_value_heads"] = self.kv_heads
@@ -192,7 +231,7 @@ def read_hf_config(path, context_limit=0):
     if not isinstance(mt, str):
         raise HFError("invalid HF model_type")
     if mt == "gpt2":
-        raise HFError("GPT-2 archives are not supported by this build")
+        return read_gpt2_config(raw, context_limit)
     keys = set(_ALLOWED)
     if mt == "qwen2":
         keys |= {"use_sliding_window", "sliding_window", "max_window_layers", "layer_types"}
@@ -288,6 +327,56 @@ def read_hf_config(path, context_limit=0):
     return h
 
 
+def read_gpt2_config(raw, context_limit=0):
+    """readGPT2Config (M:446-513)."""
+    for k, v in raw.items():
+        if k not in _GPT2_ALLOWED:
+            raise HFError(f'unsupported GPT-2 config field "{k}"')
+        if v is None and k not in ("n_inner", "pad_token_id", "summary_activation"):
+            raise HFError(f'null GPT-2 config field "{k}"')
+    f = lambda k, kind, d: _field(raw, k, kind, d)  # noqa: E731
+    h = HFConfig({}, 0)
+    h.raw = raw
+    h.model_type = "gpt2"
+    h.architectures = f("architectures", "strs", [])
+    h.vocab = f("vocab_size", "int", 0)
+    h.tied = f("tie_word_embeddings", "bool", True)
+    h.bos, h.eos = f("bos_token_id", "int", 0), f("eos_token_id", "int", 0)
+    dim, hidden = f("n_embd", "int", 0), f("n_inner", "int", 0)
+    layers, heads, ctx, nctx = f("n_layer", "int", 0), f("n_head", "int", 0), f("n_positions", "int", 0), \
+        f("n_ctx", "int", 0)
+    eps, act = f("layer_norm_epsilon", "float", 1e-5), f("activation_function", "str", "gelu_new")
+    scale, inverse = f("scale_attn_weights", "bool", True), f("scale_attn_by_inverse_layer_idx", "bool", False)
+    upcast, cross = f("reorder_and_upcast_attn", "bool", False), f("add_cross_attention", "bool", False)
+    if (h.architectures != ["GPT2LMHeadModel"] or not h.tied or act != "gelu_new" or not scale or inverse or upcast or
+            cross or (nctx != 0 and nctx != ctx)):
+        raise HFError("unsupported GPT-2 profile: require tied GPT2LMHeadModel, gelu_new and standard scaled causal "
+                      "self-attention")
+    if hidden == 0:
+        hidden = 4 * dim
+    h.dim, h.hidden, h.layers, h.heads, h.kv_heads = dim, hidden, layers, heads, heads
+    h.max_positions = h.positions = ctx
+    h.eps, h.theta = eps, 10000.0
+    if "bos_token_id" not in raw or "eos_token_id" not in raw or not 0 <= h.bos < h.vocab or \
+            not 0 <= h.eos < h.vocab:
+        raise HFError("GPT-2 requires scalar BOS/EOS IDs within vocabulary")
+    if context_limit < 0 or context_limit > ctx or ctx > 32768:
+        raise HFError("invalid GPT-2 context limit")
+    h.context = context_limit if context_limit > 0 else min(ctx, 2048)
+    if (h.vocab < BASE_VOCAB or h.vocab > MAX_HF_VOCAB or h.dim < 2 or h.dim > 8192 or h.hidden < 1 or
+            h.hidden > 32768 or h.layers < 1 or h.layers > 128 or h.heads < 1 or h.heads > h.dim or
+            h.context < 1 or h.context > 32768):
+        raise HFError("invalid model dimensions (see README limits)")
+    if h.dim % h.heads or (h.dim // h.heads) % 2:
+        raise HFError("dim must be divisible by heads with an even head dimension; heads must be divisible by "
+                      "kv_heads")
+    if not np.isfinite(h.eps) or h.eps < 1e-12 or h.eps > 1:
+        raise HFError("invalid RoPE theta or RMS epsilon")
+    if h.parameter_count() > MAX_HF_PARAMETERS:
+        raise HFError("GPT-2 exceeds HF parameter limit")
+    return h
+
+
 # --------------------------------------------------------------- archive --
 def half_float(bits):
     """halfFloat (M:834-847) over an array of IEEE half bit patterns: exact fp32."""
@@ -339,11 +428,47 @@ class HFArchive:
             raise HFError(f"non-finite HF weight in {name}")
         return out.reshape(t.shape)
 
+    def params(self):
+        """The parameters in the model's order as fp32 arrays: hfProfileSpecs
+        order, or loadGPT2's (M:5052-5165) with Conv1D weights transposed to
+        [out, in] and c_attn split into q, k, v; GPT-2 legacy causal masks are
+        checked (M:5146-5160) and not returned."""
+        h = self.config
+        if h.model_type != "gpt2":
+            for name, _ in h.specs():
+                yield self.read_tensor(name)
+            return
+        d = h.dim
+        for name in ("wte.weight", "wpe.weight", "ln_f.weight", "ln_f.bias"):
+            yield self.read_tensor(name)
+        for i in range(h.layers):
+            p = f"h.{i}."
+            w = self.read_tensor(p + "attn.c_attn.weight").T
+            b = self.read_tensor(p + "attn.c_attn.bias")
+            yield self.read_tensor(p + "ln_1.weight")
+            yield self.read_tensor(p + "ln_1.bias")
+            for part in (w[:d], w[d:2 * d], w[2 * d:], b[:d], b[d:2 * d], b[2 * d:]):
+                yield np.ascontiguousarray(part)
+            yield np.ascontiguousarray(self.read_tensor(p + "attn.c_proj.weight").T)
+            yield self.read_tensor(p + "attn.c_proj.bias")
+            yield self.read_tensor(p + "ln_2.weight")
+            yield self.read_tensor(p + "ln_2.bias")
+            yield np.ascontiguousarray(self.read_tensor(p + "mlp.c_fc.weight").T)
+            yield self.read_tensor(p + "mlp.c_fc.bias")
+            yield np.ascontiguousarray(self.read_tensor(p + "mlp.c_proj.weight").T)
+            yield self.read_tensor(p + "mlp.c_proj.bias")
+            mask = p + "attn.bias"
+            if mask in self.tensors:
+                P = h.positions
+                want = np.tril(np.ones((P, P), dtype=np.float32)).reshape(1, 1, P, P)
+                if not np.array_equal(self.read_tensor(mask), want):
+                    raise HFError("invalid GPT-2 legacy causal mask values")
+
     def load_into(self, model):
         """Every tensor, in parameter order, through sr_model_load_param_f32 (the
         device quantizer restates readParam, M:857-880)."""
-        for i, (name, _) in enumerate(self.config.specs()):
-            model.load_param_f32(i, self.read_tensor(name))
+        for i, values in enumerate(self.params()):
+            model.load_param_f32(i, values)
 
 
 def open_hf_archive(path, context_limit=0):
@@ -352,6 +477,8 @@ def open_hf_archive(path, context_limit=0):
     h = read_hf_config(path, context_limit)
     params = h.parameter_count()
     expected = dict(h.specs())
+    optional = h.optional()
+    aux = sum(int(np.prod(s)) * 4 for s in optional.values())
     index = None
     shards = set()
     ipath = os.path.join(path, "model.safetensors.index.json")
@@ -360,11 +487,13 @@ def open_hf_archive(path, context_limit=0):
         wm = raw.get("weight_map") if isinstance(raw, dict) else None
         if not isinstance(wm, dict):
             wm = {}
-        if len(wm) < len(expected) or len(wm) > len(expected):
+        if len(wm) < len(expected) or len(wm) > len(expected) + len(optional):
             raise HFError("HF shard index tensor count mismatch")
         index = {}
         for name, file in wm.items():
-            if (name not in expected or name in index or not isinstance(file, str) or not file or
+            name = h.canonical(name)
+            if ((name not in expected and name not in optional) or name in index or not isinstance(file, str) or
+                    not file or
                     os.path.basename(file) != file or "/" in file or "\\" in file or not file.endswith(".safetensors")):
                 raise HFError("unsupported HF shard index name/path")
             index[name] = file
@@ -379,7 +508,7 @@ def open_hf_archive(path, context_limit=0):
         if not os.path.isfile(fpath):
             raise HFError(f"open {name}: no such file")
         size = os.path.getsize(fpath)
-        if size < 10 or size > params * 4 + MAX_HF_HEADER + 8:
+        if size < 10 or size > params * 4 + aux + MAX_HF_HEADER + 8:
             raise HFError("Safetensors file size/type limit")
         with open(fpath, "rb") as f:
             n = int.from_bytes(f.read(8), "little")
@@ -396,23 +525,27 @@ def open_hf_archive(path, context_limit=0):
                 if not isinstance(value, dict) or not all(isinstance(v, str) for v in value.values()):
                     raise HFError("invalid Safetensors metadata")
                 continue
-            if key not in expected or key in tensors or (index is not None and index.get(key) != name):
+            key = h.canonical(key)
+            shape_of = expected.get(key, optional.get(key))
+            if shape_of is None or key in tensors or (index is not None and index.get(key) != name):
                 raise HFError(f'unexpected or duplicate HF tensor "{key}"')
             if not isinstance(value, dict) or set(value) - {"dtype", "shape", "data_offsets"}:
                 raise HFError(f"invalid HF tensor header: {key}")
             shape = value.get("shape")
-            if not isinstance(shape, list) or len(shape) != len(expected[key]):
+            if not isinstance(shape, list) or len(shape) != len(shape_of):
                 raise HFError(f"HF tensor shape mismatch: {key}")
-            if any(not _is_int(a) or a != b for a, b in zip(shape, expected[key])):
+            if any(not _is_int(a) or a != b for a, b in zip(shape, shape_of)):
                 raise HFError(f"HF tensor shape mismatch: {key}")
-            count = int(np.prod(expected[key]))
+            count = int(np.prod(shape_of))
             dt = value.get("dtype")
             w = WIDTH.get(dt, 0) if isinstance(dt, str) else 0
+            if key in optional and dt != "F32":
+                raise HFError("GPT-2 legacy causal masks must be F32")
             off = value.get("data_offsets")
             if (w == 0 or not isinstance(off, list) or len(off) != 2 or not all(_is_int(o) for o in off) or
                     off[0] < 0 or off[1] < off[0] or off[1] > body or off[1] - off[0] != count * w):
                 raise HFError(f"invalid HF tensor dtype/extent: {key}")
-            tensors[key] = _Tensor(fpath, 8 + n + off[0], dt, tuple(expected[key]), count)
+            tensors[key] = _Tensor(fpath, 8 + n + off[0], dt, tuple(shape_of), count)
             ordered.append(off)
         end = 0
         for lo, hi in sorted(ordered):

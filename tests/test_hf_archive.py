@@ -337,3 +337,101 @@ def test_reference_fixture_directories(npz):
     for i, (name, _) in enumerate(a.config.specs()):
         assert np.array_equal(a.read_tensor(name).reshape(-1).view(np.uint32),
                               z[f"param_{i}"].reshape(-1).view(np.uint32)), name
+
+
+# ------------------------------------------------------------------ GPT-2 --
+GPT2_NPZ = sorted(glob.glob(os.path.join(GOLDEN_DIR, "gpt2", "*.npz")))
+
+
+def make_gpt2_checkpoint(d, npz_path, prefix=True, masks=False, dtype=None):
+    """The inverse of loadGPT2's parameter order: HF Conv1D layout ([in, out]),
+    c_attn concatenated, optional "transformer." prefix and legacy masks."""
+    z = np.load(npz_path)
+    cfg = json.loads(str(z["config"]))
+    dt = dtype or DT[os.path.basename(npz_path)[:-4].split("-")[-1]]
+    L = cfg["n_layer"]
+    P = [z[f"param_{i}"] for i in range(4 + 16 * L)]
+    pre = "transformer." if prefix else ""
+    t = {pre + "wte.weight": P[0], pre + "wpe.weight": P[1], pre + "ln_f.weight": P[2].reshape(-1),
+         pre + "ln_f.bias": P[3].reshape(-1)}
+    for i in range(L):
+        q = P[4 + 16 * i:4 + 16 * (i + 1)]
+        p = f"{pre}h.{i}."
+        t[p + "ln_1.weight"], t[p + "ln_1.bias"] = q[0].reshape(-1), q[1].reshape(-1)
+        t[p + "attn.c_attn.weight"] = np.concatenate([q[2], q[3], q[4]], 0).T.copy()
+        t[p + "attn.c_attn.bias"] = np.concatenate([q[5].reshape(-1), q[6].reshape(-1), q[7].reshape(-1)])
+        t[p + "attn.c_proj.weight"], t[p + "attn.c_proj.bias"] = q[8].T.copy(), q[9].reshape(-1)
+        t[p + "ln_2.weight"], t[p + "ln_2.bias"] = q[10].reshape(-1), q[11].reshape(-1)
+        t[p + "mlp.c_fc.weight"], t[p + "mlp.c_fc.bias"] = q[12].T.copy(), q[13].reshape(-1)
+        t[p + "mlp.c_proj.weight"], t[p + "mlp.c_proj.bias"] = q[14].T.copy(), q[15].reshape(-1)
+    tensors = {k: (v, dt) for k, v in t.items()}
+    if masks:
+        n = cfg["n_positions"]
+        for i in range(L):
+            tensors[f"{pre}h.{i}.attn.bias"] = (np.tril(np.ones((n, n), np.float32)).reshape(1, 1, n, n), "F32")
+    os.makedirs(d, exist_ok=True)
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    names = list(tensors)
+    np.random.default_rng(3).shuffle(names)
+    write_safetensors(os.path.join(d, "model.safetensors"), tensors, order=names)
+    return cfg, tensors, z
+
+
+def _params_equal(a, z):
+    got = list(a.params())
+    assert len(got) == len([k for k in z.files if k.startswith("param_")])
+    for i, g in enumerate(got):
+        assert np.array_equal(g.reshape(-1).view(np.uint32), z[f"param_{i}"].reshape(-1).view(np.uint32)), i
+
+
+@pytest.mark.parametrize("npz", GPT2_NPZ, ids=lambda p: os.path.basename(p)[:-4])
+@pytest.mark.parametrize("prefix,masks", [(True, False), (False, True)])
+def test_gpt2_archive_params_in_loadgpt2_order(tmp_path, npz, prefix, masks):
+    _, _, z = make_gpt2_checkpoint(str(tmp_path), npz, prefix, masks)
+    a = hf.open_hf_archive(str(tmp_path))
+    assert a.config.model_type == "gpt2" and a.config.kv_heads == a.config.heads
+    _params_equal(a, z)
+    with pytest.raises(hf.HFError, match="GPT-2 profile yet"):
+        a.config.desc()
+
+
+def test_gpt2_rejects_bad_mask(tmp_path):
+    d = str(tmp_path)
+    cfg, t, z = make_gpt2_checkpoint(d, GPT2_NPZ[0], prefix=False, masks=True)
+    n = cfg["n_positions"]
+    t["h.0.attn.bias"] = (np.ones((1, 1, n, n), np.float32), "F32")
+    write_safetensors(os.path.join(d, "model.safetensors"), t)
+    a = hf.open_hf_archive(d)
+    with pytest.raises(hf.HFError, match="legacy causal mask values"):
+        list(a.params())
+    t["h.0.attn.bias"] = (np.tril(np.ones((n, n), np.float32)).reshape(1, 1, n, n), "F16")
+    write_safetensors(os.path.join(d, "model.safetensors"), t)
+    with pytest.raises(hf.HFError, match="masks must be F32"):
+        hf.open_hf_archive(d)
+
+
+@pytest.mark.parametrize("edit,msg", [
+    (lambda c: c.update(activation_function="gelu"), "unsupported GPT-2 profile"),
+    (lambda c: c.update(n_ctx=32), "unsupported GPT-2 profile"),
+    (lambda c: c.update(tie_word_embeddings=False), "unsupported GPT-2 profile"),
+    (lambda c: c.update(scale_attn_by_inverse_layer_idx=True), "unsupported GPT-2 profile"),
+    (lambda c: c.update(rotary_dim=8), "unsupported GPT-2 config field"),
+    (lambda c: c.update(n_head=None), "null GPT-2 config field"),
+    (lambda c: c.update(eos_token_id=300), "BOS/EOS"),
+])
+def test_gpt2_config_checks(tmp_path, edit, msg):
+    d = str(tmp_path)
+    cfg, _, _ = make_gpt2_checkpoint(d, GPT2_NPZ[0])
+    edit(cfg)
+    _rewrite_config(d, cfg)
+    with pytest.raises(hf.HFError, match=msg):
+        hf.open_hf_archive(d)
+
+
+@pytest.mark.skipif(not os.path.isdir(REF_TESTDATA), reason="no reference checkout")
+@pytest.mark.parametrize("npz", GPT2_NPZ, ids=lambda p: os.path.basename(p)[:-4])
+def test_reference_gpt2_directories(npz):
+    var = os.path.basename(npz)[:-4].split("-", 2)[2]
+    a = hf.open_hf_archive(os.path.join(REF_TESTDATA, "hf-gpt2", var))
+    _params_equal(a, np.load(npz))
