@@ -320,6 +320,35 @@ int sr_engine_session_pages(const sr_engine *e, int32_t i, int32_t *pages, int32
  * borrows them (prefixSnapshot.clear, :5915-5921). */
 int sr_engine_clear_prefix(sr_engine *e);
 
+/* ---------------------------------------------------------------- text */
+/* Streaming detokenization (incrementalText, :7649-7780, and the Mistral
+ * PushToken, :2132-2161): feed each sampled token's piece (the tokenizer's
+ * bytes for that id) and receive the text that is final so far, so that the
+ * concatenated deltas equal the whole-string decode even when a piece ends
+ * inside a UTF-8 sequence, a byte-fallback run or a cleanup pattern.  Host
+ * only; needs no GPU.  Flags mirror newTextDecoder (:7662-7668):
+ *   0                 plain decoder (strings.ToValidUTF8 across pieces);
+ *   SR_TEXT_HF        HF ByteLevel lossy UTF-8 (pushHF, :7737-7780);
+ *   SR_TEXT_CLEANUP   with SR_TEXT_HF: Transformers' cleanup cascade (:7672-7701);
+ *   SR_TEXT_MISTRAL   byte-fallback runs decode atomically and the first text
+ *                     loses one leading space; `fallback` flags the vocab's
+ *                     <0xNN> ids (vocab entries). */
+#define SR_TEXT_HF 1
+#define SR_TEXT_CLEANUP 2
+#define SR_TEXT_MISTRAL 4
+typedef struct sr_text_decoder sr_text_decoder;
+int sr_text_decoder_create(int32_t flags, const uint8_t *fallback, int32_t vocab, sr_text_decoder **out);
+int sr_text_decoder_destroy(sr_text_decoder *d);
+/* incrementalText.Push of n bytes (final: end of the stream).  Up to cap bytes of
+ * text (whole characters) go to out, *n_out receives their count and *queued
+ * (may be NULL) how many bytes still wait; call again with n = 0 to drain. */
+int sr_text_decoder_push(sr_text_decoder *d, const uint8_t *bytes, int64_t n, int32_t final, char *out,
+                         int64_t cap, int64_t *n_out, int64_t *queued);
+/* PushToken (:2132-2161) for token `id` with its piece; other decoders treat it
+ * as sr_text_decoder_push of the piece. */
+int sr_text_decoder_push_token(sr_text_decoder *d, int32_t id, const uint8_t *piece, int64_t n, int32_t final,
+                               char *out, int64_t cap, int64_t *n_out, int64_t *queued);
+
 #ifdef __cplusplus
 }
 #endif
