@@ -268,7 +268,7 @@ def cpu_baseline(cfg, sample_sessions, threads, steps=1):
     pos = [int(prompts[i] + offsets[i]) for i in idx]
     tables, nxt = [], 0
     for p in pos:
-        k = (p + 1 + pt - 1) // pt
+        k = (p + steps + pt - 1) // pt  # pages for every timed step's position
         tables.append(list(range(nxt, nxt + k)))
         nxt += k
     pool = np.zeros(nxt * m.page_elements, dtype=np.float32)
@@ -285,20 +285,34 @@ def cpu_baseline(cfg, sample_sessions, threads, steps=1):
             "step_s": t}
 
 
+def bench_config(cfg, args, world, tp):
+    """The `config` object of the JSON line (both arms report the same one)."""
+    return {"workload": cfg["name"], "sessions": cfg["sessions"], "layers": cfg["layers"],
+            "page_tokens": cfg["page_tokens"], "weights": "q8 (64-col blocks, fp32 scales)",
+            "mode": args.mode, "parallelism": f"tp{world}" if tp else f"replicas{world}",
+            "allreduce": (args.allreduce if tp else None),
+            "kv_state": "synthetic prefilled pages (prompt + decode offset)",
+            "l2": "inputs larger than L2 (KV pool > 100 GB)",
+            "sampling": "T0.8 k40 p0.95 penalty1.1, SplitMix64"}
+
+
 def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
     W, K = args.warmup, args.steps
+    tp = args.gpus > 1 and args.parallel == "tp"
+    if args.allreduce == "auto":
+        args.allreduce = "peer" if args.gpus == 2 else "nccl"
     from oracle import oracle as O
     O.build()
     # bounded sample: 8 sessions per step (about 10 s of CPU work per step on 32+ cores)
     res = cpu_baseline(cfg, args.ref_sessions, threads, steps=max(1, min(K, 3)))
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "output tok/s", "n_gpus": args.gpus,
             "steps": K, "warmup": W, "ms_per_step": res["step_s"] * 1000.0, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": cfg["name"], "sessions_sampled": args.ref_sessions, "page_tokens": 16},
+            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": dict(bench_config(cfg, args, args.gpus, tp), sessions_sampled=args.ref_sessions),
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": "output tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -417,13 +431,7 @@ def main():
             "ms_per_step": span_max / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
-            "config": {"workload": cfg["name"], "sessions": cfg["sessions"], "layers": cfg["layers"],
-                       "page_tokens": cfg["page_tokens"], "weights": "q8 (64-col blocks, fp32 scales)",
-                       "mode": args.mode, "parallelism": f"tp{world}" if tp else f"replicas{world}",
-                       "allreduce": (args.allreduce if tp else None),
-                       "kv_state": "synthetic prefilled pages (prompt + decode offset)",
-                       "l2": "inputs larger than L2 (KV pool > 100 GB)",
-                       "sampling": "T0.8 k40 p0.95 penalty1.1, SplitMix64"},
+            "config": bench_config(cfg, args, world, tp),
             "itl_p50_ms": span_max / K, "ttft_p50_ms": ttft["ttft_p50_ms"] if ttft else None,
             "hbm_gbs_step": step_bytes / (span_max / K / 1000.0) / 1e9,
             "algorithmic_bytes_per_step": step_bytes,
