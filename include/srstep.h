@@ -66,7 +66,18 @@ typedef struct sr_model_desc {
     int32_t rope_scaling;  /* 1: llama3 frequency scaling (:4961-4977) */
     double rope_factor, rope_low_freq_factor, rope_high_freq_factor;
     int32_t rope_original_max_positions;
+    /* SR_ARCH_GPT2: GPT-2 profile (loadGPT2 :5052-5165): absolute position
+     * table of `positions` rows (>= context), affine LayerNorm (norm_eps is
+     * layer_norm_epsilon), biases on every projection, GELU-tanh MLP (`hidden`
+     * = n_inner), tied head, kv_heads == heads, no RoPE.  Parameters follow
+     * loadGPT2's order with [out, in] matrices: wte, wpe, ln_f.weight,
+     * ln_f.bias, then per layer ln_1 w/b, q, k, v, q/k/v biases, o, o bias, ln_2
+     * w/b, c_fc, c_fc bias, c_proj, c_proj bias.  Exact mode only, one GPU. */
+    int32_t arch;          /* SR_ARCH_LLAMA (0) or SR_ARCH_GPT2 (1) */
+    int32_t positions;     /* GPT-2 position-table rows (n_positions) */
 } sr_model_desc;
+#define SR_ARCH_LLAMA 0
+#define SR_ARCH_GPT2 1
 
 typedef struct sr_param_info {
     int32_t rows, cols, format; /* SR_PARAM_* */

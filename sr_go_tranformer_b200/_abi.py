@@ -16,6 +16,7 @@ SR_PARAM_F32, SR_PARAM_Q8, SR_PARAM_Q4 = range(3)
 SR_MODE_EXACT, SR_MODE_FAST = 0, 1
 SR_TP_PEER_HANDLE_BYTES = 64
 SR_TEXT_HF, SR_TEXT_CLEANUP, SR_TEXT_MISTRAL = 1, 2, 4
+SR_ARCH_LLAMA, SR_ARCH_GPT2 = 0, 1
 FORMATS = {"f32": SR_FMT_F32, "q8": SR_FMT_Q8, "q4": SR_FMT_Q4, "q4-mixed": SR_FMT_Q4_MIXED}
 
 # Every symbol include/srstep.h declares (checked by tests/test_abi.py).
@@ -39,7 +40,8 @@ class ModelDesc(C.Structure):
                 ("rope_theta", C.c_double), ("norm_eps", C.c_double), ("tied", C.c_int32),
                 ("qkv_bias", C.c_int32), ("weight_format", C.c_int32), ("page_tokens", C.c_int32),
                 ("rope_scaling", C.c_int32), ("rope_factor", C.c_double), ("rope_low_freq_factor", C.c_double),
-                ("rope_high_freq_factor", C.c_double), ("rope_original_max_positions", C.c_int32)]
+                ("rope_high_freq_factor", C.c_double), ("rope_original_max_positions", C.c_int32),
+                ("arch", C.c_int32), ("positions", C.c_int32)]
 
 
 class ParamInfo(C.Structure):

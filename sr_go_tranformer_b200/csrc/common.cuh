@@ -24,6 +24,7 @@ __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b)
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ double dmul(double a, double b) { return __dmul_rn(a, b); }
 __device__ __forceinline__ double dadd(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ double dsub(double a, double b) { return __dsub_rn(a, b); }
 
 // q4Pairs (monolith.go:3811-3817): sign-extended low / high nibble of a byte.
 __device__ __forceinline__ float q4_lo(uint32_t b) { return (float)((int32_t)(b << 28) >> 28); }

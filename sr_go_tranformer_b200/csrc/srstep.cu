@@ -21,6 +21,7 @@
 #include "srstep_internal.h"
 #include "nccl_dl.h"
 #include "tp_peer.cuh"
+#include "gpt2_kernels.cuh"
 
 using namespace sr;
 
@@ -120,6 +121,14 @@ static int validate_desc(const sr_model_desc& c, int tp_size) {
   if (group * hd / 4 > 1024) return sr_fail(SR_EUNSUPPORTED, "query heads per KV head x head_dim exceeds 4096");
   if (c.rope_scaling && (c.rope_low_freq_factor <= 0 || c.rope_high_freq_factor <= c.rope_low_freq_factor))
     return sr_fail(SR_EINVAL, "invalid llama3 rope scaling");
+  if (c.arch != SR_ARCH_LLAMA && c.arch != SR_ARCH_GPT2) return sr_fail(SR_EINVAL, "invalid model architecture");
+  if (c.arch == SR_ARCH_GPT2) {  // readGPT2Config's profile (M:446-513)
+    if (c.kv_heads != c.heads || !c.tied || c.qkv_bias || c.rope_scaling)
+      return sr_fail(SR_EINVAL, "GPT-2 needs kv_heads == heads, a tied head, no q/k/v bias flag and no RoPE scaling");
+    if (c.positions < c.context || c.positions > 32768)
+      return sr_fail(SR_EINVAL, "GPT-2 position table must cover the context (at most 32768 rows)");
+    if (tp_size != 1) return sr_fail(SR_EUNSUPPORTED, "the GPT-2 profile runs on one GPU");
+  }
   if (tp_size < 1 || tp_size > 64) return sr_fail(SR_EINVAL, "tensor-parallel size must be 1..64");
   if (tp_size > 1) {
     if (c.heads % tp_size || c.kv_heads % tp_size || c.hidden % tp_size)
@@ -157,6 +166,27 @@ int sr_param_table(const sr_model_desc& c, int rank, int size, std::vector<Param
     shards->push_back(sh);
   };
   const int L = c.layers, d = c.dim, h = c.hidden;
+  if (c.arch == SR_ARCH_GPT2) {  // loadGPT2's parameter order (M:5063-5066, 5114-5122)
+    add(c.vocab, d, true, true, 0);
+    add(c.positions, d, false, false, 0);
+    add(1, d, false, false, 0);
+    add(1, d, false, false, 0);
+    for (int l = 0; l < L; l++) {
+      add(1, d, false, false, 0);
+      add(1, d, false, false, 0);
+      for (int k = 0; k < 3; k++) add(d, d, true, false, 0);
+      for (int k = 0; k < 3; k++) add(1, d, false, false, 0);
+      add(d, d, true, false, 0);
+      add(1, d, false, false, 0);
+      add(1, d, false, false, 0);
+      add(1, d, false, false, 0);
+      add(h, d, true, false, 0);
+      add(1, h, false, false, 0);
+      add(d, h, true, false, 0);
+      add(1, d, false, false, 0);
+    }
+    return SR_OK;
+  }
   add(c.vocab, d, true, true, 0);
   for (int l = 0; l < L; l++) {
     add(1, d, false, false, 0);
@@ -659,6 +689,7 @@ __global__ void k_init_param(Param p, uint64_t seed, uint64_t e0, double scale, 
 
 extern "C" int sr_model_init_synthetic(sr_model* m, uint64_t seed, double scale) {
   if (!m) return sr_fail(SR_EINVAL, "null model");
+  if (m->d.arch == SR_ARCH_GPT2) return sr_fail(SR_EUNSUPPORTED, "no synthetic initialisation for the GPT-2 profile");
   CK(cudaSetDevice(m->device));
   const int L = m->d.layers;
   uint64_t e0 = 0;
@@ -719,6 +750,8 @@ extern "C" int sr_model_load_param_f32(sr_model* m, int32_t index, const float* 
 extern "C" int sr_model_set_mode(sr_model* m, int32_t mode) {
   if (!m) return sr_fail(SR_EINVAL, "null model");
   if (mode != SR_MODE_EXACT && mode != SR_MODE_FAST) return sr_fail(SR_EINVAL, "invalid mode");
+  if (mode == SR_MODE_FAST && m->d.arch == SR_ARCH_GPT2)
+    return sr_fail(SR_EUNSUPPORTED, "the GPT-2 profile runs in the exact mode only");
   m->mode = mode;
   return SR_OK;
 }
@@ -1019,8 +1052,94 @@ static void tp_add(sr_model* m, int n, const float* T) {
   sr_count_launch(m);
 }
 
+// The GPT-2 profile's step (prefillSelected's GPT-2 branches, M:6369-6371,
+// 6389, 6403-6408), exact order on every kernel: embedding + position row,
+// then per layer LayerNorm, Q/K/V with bias, K/V write without RoPE,
+// attention, O with bias + residual, LayerNorm, c_fc with bias, GELU-tanh,
+// c_proj with bias + residual; the selected head is LayerNorm + tied wte.
+static int gpt2_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel) {
+  const ModelDims& dm = m->dm;
+  const int n = info.rows, d = dm.dim, L = dm.layers;
+  const double eps = m->d.norm_eps;
+  cudaStream_t s = m->stream;
+  auto fv = [&](int i) { return (const float*)m->params[i].values; };
+  sr_prof_span_begin(m);
+  SR_LAUNCH(m, SR_PROF_META, k_meta<<<1, 1024, 0, s>>>(m->meta, info.sessions, n));
+  SR_LAUNCH(m, SR_PROF_EMBED, k_embed<<<n, 256, 0, s>>>(m->params[0], m->meta.tokens, m->X, d);
+            k_add_position<<<n, 256, 0, s>>>(m->X, fv(1), m->meta, d));
+  sr_count_launch(m, 3);
+  const int norm_blocks = (n + kNormWarps - 1) / kNormWarps;
+  for (int l = 0; l < L; l++) {
+    if (cancel && *cancel) {
+      sr_prof_span_end(m);
+      cudaStreamSynchronize(s);
+      sr_prof_resolve(m);
+      return sr_fail(SR_ECANCELED, "step canceled between layers");
+    }
+    const int b = 4 + 16 * l;
+    const Param* P = &m->params[b];
+    SR_LAUNCH(m, SR_PROF_NORM,
+              k_layernorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, fv(b), fv(b + 1), m->N, n, d,
+                                                                          eps));
+    LinearOut o;
+    o.resid = nullptr;
+    o.out_map = nullptr;
+    float* qkv[3] = {m->Q, m->K, m->V};
+    for (int k = 0; k < 3; k++) {
+      o.y = qkv[k];
+      o.ldy = d;
+      o.bias = fv(b + 5 + k);  // addBias after the projection (M:6384-6386)
+      SR_LAUNCH(m, SR_PROF_LINEAR, launch_linear_exact(m, m->N, n, P[2 + k], o));
+    }
+    SR_LAUNCH(m, SR_PROF_ROPE_KV,
+              k_kv_write_exact<<<n, 128, 0, s>>>(m->K, m->V, m->meta, pool->data, dm, l));
+    sr_count_launch(m, 5);  // norm, q, k, v, kv write
+    SR_LAUNCH(m, SR_PROF_ATTENTION, launch_attention_exact(m, pool, n, info.max_len, l));
+    o.y = m->X;  // Tmp = O(a) + bias; X += Tmp (M:6398-6400)
+    o.ldy = d;
+    o.bias = fv(b + 9);
+    o.resid = m->X;
+    SR_LAUNCH(m, SR_PROF_LINEAR, launch_linear_exact(m, m->A, n, P[8], o));
+    SR_LAUNCH(m, SR_PROF_NORM,
+              k_layernorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, fv(b + 10), fv(b + 11), m->N, n,
+                                                                          d, eps));
+    o.y = m->G;
+    o.ldy = dm.hidden;
+    o.bias = fv(b + 13);
+    o.resid = nullptr;
+    SR_LAUNCH(m, SR_PROF_LINEAR, launch_linear_exact(m, m->N, n, P[12], o));
+    const int64_t cnt = (int64_t)n * dm.hidden;
+    SR_LAUNCH(m, SR_PROF_SWIGLU,
+              k_gelu_exact<<<(int)std::min<int64_t>((cnt + 255) / 256, 148 * 16), 256, 0, s>>>(m->G, m->H, cnt));
+    o.y = m->X;  // X += c_proj(h) + bias (M:6415-6417)
+    o.ldy = d;
+    o.bias = fv(b + 15);
+    o.resid = m->X;
+    SR_LAUNCH(m, SR_PROF_LINEAR, launch_linear_exact(m, m->H, n, P[14], o));
+    sr_count_launch(m, 5);  // o, norm, c_fc, gelu, c_proj
+  }
+  CK(cudaMemsetAsync(m->logits, 0, (size_t)info.sessions * dm.vocab * 4, s));
+  if (info.heads > 0) {
+    const int hb = (info.heads + kNormWarps - 1) / kNormWarps;
+    SR_LAUNCH(m, SR_PROF_HEAD,
+              k_layernorm_exact<<<hb, kNormWarps * 32, 0, s>>>(m->X, m->meta.head_src, fv(2), fv(3), m->N, info.heads,
+                                                               d, eps));
+    LinearOut o;
+    o.y = m->logits;
+    o.ldy = dm.vocab;
+    o.bias = nullptr;
+    o.resid = nullptr;
+    o.out_map = m->meta.head_dst;
+    SR_LAUNCH(m, SR_PROF_HEAD, launch_linear_exact(m, m->N, info.heads, m->params[0], o));
+    sr_count_launch(m, 2);
+  }
+  CK(cudaGetLastError());
+  return SR_OK;
+}
+
 int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel,
                     const StepScratch* scratch) {
+  if (m->d.arch == SR_ARCH_GPT2) return gpt2_step_enqueue(m, pool, info, cancel);
   const ModelDims& dm = m->dm;
   const int n = info.rows, d = dm.dim, kd = dm.kvd, L = dm.layers;
   const double eps = m->d.norm_eps;
@@ -1414,6 +1533,7 @@ extern "C" int sr_step_noalloc(sr_model* m, sr_kvpool* pool, const sr_batch* bat
   BatchInfo info;
   int rc = sr_validate_batch(m, pool, batch, &info);
   if (rc != SR_OK) return rc;
+  if (m->d.arch == SR_ARCH_GPT2) return sr_fail(SR_EUNSUPPORTED, "the allocation-free step runs the RMSNorm profiles");
   if (!fast_attention_supported(m->dm))
     return sr_fail(SR_EUNSUPPORTED, "the allocation-free step needs head_dim 64 or 128 and at most 8 query heads per KV head");
   if (m->dm.tp_size > 1)

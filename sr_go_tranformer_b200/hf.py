@@ -23,8 +23,8 @@ Llama / Qwen2 / full-attention Mistral profiles the step runs:
 GPT-2 archives (readGPT2Config M:446-513, gpt2Specs M:515-530) open and read
 the same way; HFArchive.params() gives their tensors in loadGPT2's parameter
 order (M:5052-5165: Conv1D weights transposed to [out, in], c_attn split into
-q, k, v), with the legacy causal masks checked.  The device step does not run
-the GPT-2 profile yet, so load_hf_model refuses them.
+q, k, v), with the legacy causal masks checked.  The device runs GPT-2 in the
+exact mode only.
 
 Errors raise HFError with the reference's messages.
 """
@@ -213,10 +213,11 @@ class HFConfig:
         return name[len("transformer."):] if self.model_type == "gpt2" and name.startswith("transformer.") else name
 
     def desc(self, weight_format="f32", page_tokens=32):
-        """sr_model_desc of this profile (readHFConfig's Config plus the RoPE scaling)."""
-        if self.model_type == "gpt2":
-            raise HFError("the device step does not run the GPT-2 profile yet")
+        """sr_model_desc of this profile (readHFConfig's Config plus the RoPE scaling;
+        for GPT-2 the position table, exact mode only on the device)."""
         from .step import desc_from_hf
+        if self.model_type == "gpt2":
+            return desc_from_hf(self.raw, weight_format, page_tokens, context=self.context)
         hf = dict(self.raw)
         hf["num_key_value_heads"] = self.kv_heads
         return desc_from_hf(hf, weight_format, page_tokens, context=self.context)

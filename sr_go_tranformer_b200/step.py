@@ -22,8 +22,20 @@ def _p(a):
 
 
 def desc_from_hf(hf, weight_format="f32", page_tokens=32, context=None):
-    """sr_model_desc from an HF config.json dict (readHFConfig, M:253-385)."""
+    """sr_model_desc from an HF config.json dict (readHFConfig, M:253-385;
+    readGPT2Config, M:446-513, for model_type gpt2)."""
     d = A.ModelDesc()
+    if hf.get("model_type") == "gpt2":
+        d.vocab, d.dim, d.layers = hf["vocab_size"], hf["n_embd"], hf["n_layer"]
+        d.hidden = hf.get("n_inner") or 4 * d.dim
+        d.heads = d.kv_heads = hf["n_head"]
+        d.positions = hf["n_positions"]
+        d.context = context or min(d.positions, 2048)
+        d.rope_theta, d.norm_eps = 10000.0, float(hf.get("layer_norm_epsilon", 1e-5))
+        d.tied, d.qkv_bias, d.arch = 1, 0, A.SR_ARCH_GPT2
+        d.weight_format = A.FORMATS[weight_format]
+        d.page_tokens = page_tokens
+        return d
     d.vocab = hf["vocab_size"]
     d.dim = hf["hidden_size"]
     d.hidden = hf["intermediate_size"]

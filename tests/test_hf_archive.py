@@ -392,8 +392,10 @@ def test_gpt2_archive_params_in_loadgpt2_order(tmp_path, npz, prefix, masks):
     a = hf.open_hf_archive(str(tmp_path))
     assert a.config.model_type == "gpt2" and a.config.kv_heads == a.config.heads
     _params_equal(a, z)
-    with pytest.raises(hf.HFError, match="GPT-2 profile yet"):
-        a.config.desc()
+    d = a.config.desc("q8", 32)
+    cfg = json.loads(str(z["config"]))
+    assert (d.arch, d.dim, d.heads, d.kv_heads, d.positions, d.tied) == (1, cfg["n_embd"], cfg["n_head"],
+                                                                         cfg["n_head"], cfg["n_positions"], 1)
 
 
 def test_gpt2_rejects_bad_mask(tmp_path):

@@ -184,3 +184,26 @@ def test_two_rank_gloo_forward_matches_single_rank(srlib):
     assert np.abs(got[0] - ref).max() < 1e-9
     # and against the Transformers golden (fp32 reference) within 2e-5
     assert np.abs(got[0] - z["logits"][19]).max() < 2e-5
+
+
+def test_gpt2_parameter_table_matches_oracle(oracle):
+    """The device's GPT-2 parameter table (loadGPT2 order, M:5052-5165) has the
+    oracle's shapes, parameter by parameter."""
+    import glob
+    import json
+    import os
+    import numpy as np
+    from conftest import GOLDEN_DIR
+    from sr_go_tranformer_b200 import step as S
+    for path in sorted(glob.glob(os.path.join(GOLDEN_DIR, "gpt2", "*.npz"))):
+        hf = json.loads(str(np.load(path)["config"]))
+        desc = S.desc_from_hf(hf, "q8", 32)
+        om = oracle.Model(oracle.config_from_hf(hf, "q8", 32))
+        for i in range(om.nparams):
+            info = om.param_info(i)
+            row0, rows, col0, cols = S.tp_shard(desc, 0, 1, i)
+            assert (row0, col0, rows, cols) == (0, 0, info.rows, info.cols), i
+        with pytest.raises(Exception):
+            S.tp_shard(desc, 0, 1, om.nparams)
+        with pytest.raises(Exception):  # one GPU only
+            S.tp_shard(desc, 0, 2, 0)
