@@ -195,7 +195,7 @@ __device__ __forceinline__ void warp_tile8(const float* kt, const float* vt, int
 // grid: the step's single-row items (rows of 1-token chunks) x KV heads
 template <int G>
 __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
-  constexpr int HD = 128, MT = kWpMT, GP = WarpSmem<G>::GP;
+  constexpr int HD = 128, MT = kWpMT;
   constexpr int ROUNDS = (G + 3) / 4;  // softmax passes: 4 heads x 8 positions per pass
   extern __shared__ __align__(16) float fsm[];
   const int rs = a.meta.single_rs[blockIdx.x], kh = blockIdx.y;

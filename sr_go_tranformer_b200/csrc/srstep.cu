@@ -419,7 +419,7 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
   dm.page_tokens = c.page_tokens;
   dm.page_elems = 2LL * c.page_tokens * dm.kvd * c.layers;
   sr_param_table(c, tp_rank, tp_size, &m->params, &m->shards);
-  const int L = c.layers, d = c.dim, kd = dm.kvd, h = dm.hidden;
+  const int d = c.dim, kd = dm.kvd, h = dm.hidden;
   if (tp_size > 1) {
     nccl::Api& api = nccl::api();
     if (!api.ok) {
@@ -1363,8 +1363,7 @@ int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_o
   if (int rc = tp_check(m)) return rc;
   if (int rc = tc_check(m)) return rc;
   uint8_t* h = (uint8_t*)m->h_stage + m->upload_ints * 4;
-  const size_t off_hoff = kSampOffHistOff, off_hist = kSampOffHist, off_rng = kSampOffRng, off_ids = kSampOffIds,
-               off_status = kSampOffStatus;
+  const size_t off_rng = kSampOffRng, off_ids = kSampOffIds, off_status = kSampOffStatus;
   const int32_t* ids = (const int32_t*)(h + off_ids);
   const int32_t* status = (const int32_t*)(h + off_status);
   memcpy(ids_out, ids, (size_t)n * 4);
