@@ -332,9 +332,10 @@ def main():
     ap.add_argument("--ref-sessions", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"])
-    ap.add_argument("--allreduce", default="auto", choices=["auto", "peer", "nccl"],
-                    help="tensor-parallel all-reduce: the library's NVLink peer-memory kernels, NCCL, or auto "
-                         "(peer at 2 ranks, NCCL above: the faster one measured at each size)")
+    ap.add_argument("--allreduce", default="auto", choices=["auto", "peer", "peer-ll", "nccl"],
+                    help="tensor-parallel all-reduce: the library's NVLink peer-memory kernels (flag barriers, or "
+                         "peer-ll: flags inside the data, one kernel), NCCL, or auto (peer at 2 ranks, NCCL above: the "
+                         "faster one measured at each size)")
     ap.add_argument("--no-ttft", action="store_true", help="skip the serving run that measures TTFT")
     args = ap.parse_args()
     cfg = dict(CONFIG)
@@ -364,10 +365,12 @@ def main():
     model = make_model(cfg, local, args.mode, tp=tp_args)
     if args.allreduce == "auto":
         args.allreduce = "peer" if world == 2 else "nccl"
-    if tp and args.allreduce == "peer":
+    if tp and args.allreduce in ("peer", "peer-ll"):
         handles = [None] * world
         dist.all_gather_object(handles, model.tp_peer_handle())
         model.tp_peer_open(handles)
+        if args.allreduce == "peer-ll":
+            model.tp_peer_set_protocol("ll")
     st = DecodeState(cfg, model, W, workload_rank=0 if tp else rank)
     for _ in range(W):
         st.step()

@@ -154,6 +154,19 @@ int sr_tp_shard(const sr_model_desc *desc, int32_t rank, int32_t size, int32_t i
 #define SR_TP_PEER_HANDLE_BYTES 64
 int sr_tp_peer_handle(sr_model *m, void *handle_out);
 int sr_tp_peer_open(sr_model *m, const void *handles);
+/* Protocol of the peer-memory all-reduce (after sr_tp_peer_open; every rank
+ * the same):
+ *   SR_PEER_BARRIER  two kernels, reduce-scatter then gather, with a flag
+ *                    barrier before each (the default);
+ *   SR_PEER_LL       one kernel: every 16-byte line carries two values and
+ *                    the all-reduce's epoch twice, each chunk is pushed to its
+ *                    owner, summed there in rank order as its lines arrive and
+ *                    pushed to every rank; the next RMSNorm (or the residual
+ *                    add) waits on the lines it reads.  Same sums, bit for bit,
+ *                    as SR_PEER_BARRIER.  Not yet run on a GPU. */
+#define SR_PEER_BARRIER 0
+#define SR_PEER_LL 1
+int sr_tp_peer_set_protocol(sr_model *m, int32_t protocol);
 int sr_model_destroy(sr_model *m);
 int sr_model_param_count(const sr_model *m, int32_t *count);
 int sr_model_param_info(const sr_model *m, int32_t index, sr_param_info *out);

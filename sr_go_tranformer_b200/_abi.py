@@ -17,6 +17,7 @@ SR_MODE_EXACT, SR_MODE_FAST = 0, 1
 SR_TP_PEER_HANDLE_BYTES = 64
 SR_TEXT_HF, SR_TEXT_CLEANUP, SR_TEXT_MISTRAL = 1, 2, 4
 SR_ARCH_LLAMA, SR_ARCH_GPT2 = 0, 1
+SR_PEER_BARRIER, SR_PEER_LL = 0, 1
 FORMATS = {"f32": SR_FMT_F32, "q8": SR_FMT_Q8, "q4": SR_FMT_Q4, "q4-mixed": SR_FMT_Q4_MIXED}
 
 # Every symbol include/srstep.h declares (checked by tests/test_abi.py).
@@ -30,6 +31,7 @@ EXPORTED = [
     "sr_step_noalloc", "sr_model_create_tp", "sr_tp_unique_id", "sr_tp_shard", "sr_engine_latency",
     "sr_kvpool_copy_rows", "sr_engine_clear_prefix", "sr_tp_peer_handle", "sr_tp_peer_open",
     "sr_text_decoder_create", "sr_text_decoder_destroy", "sr_text_decoder_push", "sr_text_decoder_push_token",
+    "sr_tp_peer_set_protocol",
 ]
 PROF_CLASSES = ["meta", "embed", "norm", "linear", "rope_kv", "attention", "swiglu", "head", "sample"]
 
@@ -123,6 +125,7 @@ def lib():
         "sr_tp_shard": (C.c_int, [C.POINTER(ModelDesc), I32, I32, I32, P]),
         "sr_tp_peer_handle": (C.c_int, [P, P]),
         "sr_tp_peer_open": (C.c_int, [P, P]),
+        "sr_tp_peer_set_protocol": (C.c_int, [P, I32]),
         "sr_text_decoder_create": (C.c_int, [I32, P, I32, C.POINTER(P)]),
         "sr_text_decoder_destroy": (C.c_int, [P]),
         "sr_text_decoder_push": (C.c_int, [P, P, I64, I32, P, I64, C.POINTER(I64), C.POINTER(I64)]),

@@ -9,6 +9,7 @@
 #include "exact_kernels.cuh"
 #include "fast_attention.cuh"
 #include "srstep_internal.h"
+#include "tp_peer.cuh"
 
 namespace sr {
 
@@ -65,7 +66,8 @@ inline int fast_check(sr_model* m) {
 __global__ void __launch_bounds__(128)
 k_rmsnorm_fast(float* __restrict__ X, const int32_t* __restrict__ src_map, const float* __restrict__ w,
                float* __restrict__ Y, int rows, int d, double eps, __nv_bfloat16* __restrict__ yh,
-               __nv_bfloat16* __restrict__ yl, const float* __restrict__ T) {
+               __nv_bfloat16* __restrict__ yl, const float* __restrict__ T, const uint4* __restrict__ Tll,
+               uint32_t epoch, int* err) {
   __shared__ double red[4];
   const int r = blockIdx.x;
   const int srow = src_map ? src_map[r] : r;
@@ -74,6 +76,15 @@ k_rmsnorm_fast(float* __restrict__ X, const int32_t* __restrict__ src_map, const
   if (T) {
     const float* t = T + (int64_t)srow * d;
     for (int j = threadIdx.x; j < d; j += 128) x[j] += t[j];
+    __syncthreads();
+  } else if (Tll) {  // the LL all-reduce's sums, waited for line by line (peer::k_peer_ll)
+    const uint4* t = Tll + (int64_t)srow * d / 2;
+    bool ok = true;
+    for (int j = threadIdx.x; j < d / 2; j += 128) {
+      const uint4 v = peer::wait_line(t + j, epoch, err, ok);
+      x[2 * j] += __uint_as_float(v.x);
+      x[2 * j + 1] += __uint_as_float(v.z);
+    }
     __syncthreads();
   }
   double ss = 0.0;
@@ -119,8 +130,9 @@ k_rmsnorm_fast(float* __restrict__ X, const int32_t* __restrict__ src_map, const
 
 inline void fast_rmsnorm(sr_model* m, float* X, const int32_t* src_map, const float* w, float* Y, int rows, int d,
                          double eps, __nv_bfloat16* yh = nullptr, __nv_bfloat16* yl = nullptr,
-                         const float* T = nullptr) {
-  k_rmsnorm_fast<<<rows, 128, 0, m->stream>>>(X, src_map, w, Y, rows, d, eps, yh, yl, T);
+                         const float* T = nullptr, const uint4* Tll = nullptr, uint32_t epoch = 0,
+                         int* err = nullptr) {
+  k_rmsnorm_fast<<<rows, 128, 0, m->stream>>>(X, src_map, w, Y, rows, d, eps, yh, yl, T, Tll, epoch, err);
 }
 
 // SwiGLU h = g/(1+exp(-g)) * u in fp32 (M:6410-6413 reordered), written as the

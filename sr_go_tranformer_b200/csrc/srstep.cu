@@ -253,11 +253,15 @@ extern "C" int sr_model_create_tp(const sr_model_desc* desc, int device, int32_t
 
 // ------------------------------------------------- tensor-parallel peer memory --
 // One exported allocation per rank: the two all-reduce buffers, the barrier
-// slots and the finished-CTA counter (tp_peer.cuh).  tables (device) holds
-// every rank's buffer 0, buffer 1 and slot pointers once the peers are open.
+// slots and the finished-CTA counter, then the LL protocol's two reduce and
+// two gather buffers (tp_peer.cuh).  tables (device) holds, once the peers are
+// open, every rank's buffer 0, buffer 1, slots, reduce 0, reduce 1, gather 0
+// and gather 1 pointers (7 x size).
 struct PeerHost {
   uint8_t* base = nullptr;
-  size_t buf_bytes = 0;
+  size_t buf_bytes = 0, rb_bytes = 0, gb_bytes = 0;
+  int protocol = SR_PEER_BARRIER;
+  int ll_parity = 0;
   float* buf[2] = {};
   int* slots = nullptr;
   int* counter = nullptr;
@@ -276,7 +280,13 @@ static int peer_alloc(sr_model* m, size_t buf_bytes) {
   PeerHost* ph = new PeerHost();
   m->peer = ph;
   ph->buf_bytes = buf_bytes;
-  int rc = sr_model_alloc(m, (void**)&ph->base, 2 * buf_bytes + kPeerTail);
+  // LL buffers: 16-byte lines of two values (8 bytes per value), every rank's
+  // chunk slot of the reduce buffer sized for the largest step
+  const int64_t count_max = (int64_t)(buf_bytes / 4), size = m->dm.tp_size;
+  const int64_t chunk_max = ((count_max + size - 1) / size + 3) / 4 * 4;
+  ph->rb_bytes = (size_t)(size * chunk_max * 8);
+  ph->gb_bytes = (size_t)(count_max * 8);
+  int rc = sr_model_alloc(m, (void**)&ph->base, 2 * buf_bytes + kPeerTail + 2 * ph->rb_bytes + 2 * ph->gb_bytes);
   if (rc != SR_OK) return rc;
   ph->buf[0] = (float*)ph->base;
   ph->buf[1] = (float*)(ph->base + buf_bytes);
@@ -287,7 +297,11 @@ static int peer_alloc(sr_model* m, size_t buf_bytes) {
     cudaGetLastError();
     return sr_fail(SR_EDEVICE, "clearing the all-reduce barrier slots failed");
   }
-  if ((rc = sr_model_alloc(m, (void**)&ph->tables, (size_t)3 * m->dm.tp_size * sizeof(void*))) != SR_OK) return rc;
+  if (cudaMemset(ph->base + 2 * buf_bytes + kPeerTail, 0, 2 * ph->rb_bytes + 2 * ph->gb_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return sr_fail(SR_EDEVICE, "clearing the LL all-reduce buffers failed");
+  }
+  if ((rc = sr_model_alloc(m, (void**)&ph->tables, (size_t)7 * m->dm.tp_size * sizeof(void*))) != SR_OK) return rc;
   m->T = ph->buf[0];
   return SR_OK;
 }
@@ -341,7 +355,7 @@ extern "C" int sr_tp_peer_open(sr_model* m, const void* handles) {
   if (size > peer::kMaxRanks) return sr_fail(SR_EUNSUPPORTED, "peer all-reduce supports at most 64 ranks");
   if (m->dm.dim % 4) return sr_fail(SR_EUNSUPPORTED, "peer all-reduce needs a model width divisible by 4");
   CK(cudaSetDevice(m->device));
-  std::vector<void*> host((size_t)3 * size);
+  std::vector<void*> host((size_t)7 * size);
   for (int q = 0; q < size; q++) {
     uint8_t* b = ph->base;
     if (q != rank) {
@@ -361,9 +375,23 @@ extern "C" int sr_tp_peer_open(sr_model* m, const void* handles) {
     host[q] = b;
     host[size + q] = b + ph->buf_bytes;
     host[2 * size + q] = b + 2 * ph->buf_bytes;
+    uint8_t* ll = b + 2 * ph->buf_bytes + kPeerTail;
+    host[3 * size + q] = ll;
+    host[4 * size + q] = ll + ph->rb_bytes;
+    host[5 * size + q] = ll + 2 * ph->rb_bytes;
+    host[6 * size + q] = ll + 2 * ph->rb_bytes + ph->gb_bytes;
   }
   CK(cudaMemcpy(ph->tables, host.data(), host.size() * sizeof(void*), cudaMemcpyHostToDevice));
   ph->open = true;
+  return SR_OK;
+}
+
+extern "C" int sr_tp_peer_set_protocol(sr_model* m, int32_t protocol) {
+  if (!m) return sr_fail(SR_EINVAL, "null model");
+  PeerHost* ph = (PeerHost*)m->peer;
+  if (!ph || !ph->open) return sr_fail(SR_EINVAL, "peer memory is not open (sr_tp_peer_open)");
+  if (protocol != SR_PEER_BARRIER && protocol != SR_PEER_LL) return sr_fail(SR_EINVAL, "unknown peer protocol");
+  ph->protocol = protocol;
   return SR_OK;
 }
 
@@ -1010,14 +1038,44 @@ __global__ void k_add_inplace(float* __restrict__ X, const float* __restrict__ T
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
     X[i] += T[i];
 }
+// An all-reduced sum as its consumer reads it: a plain buffer, or the LL
+// protocol's gather buffer of this rank with the all-reduce's epoch.
+struct TpSum {
+  const float* plain = nullptr;
+  const uint4* ll = nullptr;
+  uint32_t epoch = 0;
+  explicit operator bool() const { return plain || ll; }
+};
+
 // Sums the ranks' partials in m->T (over peer memory once sr_tp_peer_open has
-// run, else NCCL), sets *sum to the summed buffer and points m->T at the other
-// buffer for the next row-parallel projection.
-static int tp_allreduce(sr_model* m, int n, const float** sum) {
+// run, else NCCL), sets *sum to where the sums are and points m->T at the
+// other buffer for the next row-parallel projection.
+static int tp_allreduce(sr_model* m, int n, TpSum* sum) {
   PeerHost* ph = (PeerHost*)m->peer;
   const int64_t count = (int64_t)n * m->dm.dim;
   float* T = m->T;
-  if (ph->open) {
+  *sum = TpSum();
+  if (ph->open && ph->protocol == SR_PEER_LL) {
+    const int size = m->dm.tp_size, par = ph->ll_parity;
+    peer::LLArgs a;
+    a.part = T;
+    a.rb = (uint4* const*)(ph->tables + (size_t)(3 + par) * size);
+    a.gb = (uint4* const*)(ph->tables + (size_t)(5 + par) * size);
+    a.err = ph->err;
+    a.count = count;
+    a.chunk = ((count + size - 1) / size + 3) / 4 * 4;
+    a.epoch = ++ph->epoch;
+    a.rank = m->dm.tp_rank;
+    a.size = size;
+    const int grid = (int)std::min<int64_t>(std::max<int64_t>((a.chunk / 2 + peer::kThreads - 1) / peer::kThreads, 1),
+                                            148 * 2);
+    peer::k_peer_ll<<<grid, peer::kThreads, 0, m->stream>>>(a);
+    sr_count_launch(m);
+    ph->ran = true;
+    sum->ll = (const uint4*)(ph->base + 2 * ph->buf_bytes + kPeerTail + 2 * ph->rb_bytes + (size_t)par * ph->gb_bytes);
+    sum->epoch = a.epoch;
+    ph->ll_parity ^= 1;
+  } else if (ph->open) {
     peer::Args a;
     a.bufs = (float* const*)(ph->tables + (size_t)ph->cur * m->dm.tp_size);
     a.flags = (int* const*)(ph->tables + (size_t)2 * m->dm.tp_size);
@@ -1036,19 +1094,24 @@ static int tp_allreduce(sr_model* m, int n, const float** sum) {
     peer::k_peer_gather<<<gb, peer::kThreads, 0, m->stream>>>(a);
     sr_count_launch(m, 2);
     ph->ran = true;
+    sum->plain = T;
   } else {
     nccl::Api& api = nccl::api();
     const int r = api.AllReduce(T, T, (size_t)count, nccl::kFloat32, nccl::kSum, (nccl::Comm)m->nccl_comm, m->stream);
     if (r != nccl::kSuccess) return sr_fail(SR_EDEVICE, std::string("ncclAllReduce: ") + api.GetErrorString(r));
+    sum->plain = T;
   }
-  *sum = T;
   ph->cur ^= 1;
   m->T = ph->buf[ph->cur];
   return SR_OK;
 }
-static void tp_add(sr_model* m, int n, const float* T) {
+static void tp_add(sr_model* m, int n, const TpSum& t) {
   const int64_t count = (int64_t)n * m->dm.dim;
-  k_add_inplace<<<(int)std::min<int64_t>((count + 255) / 256, 148 * 8), 256, 0, m->stream>>>(m->X, T, count);
+  if (t.ll)
+    peer::k_add_ll<<<(int)std::min<int64_t>((count / 2 + 255) / 256, 148 * 8), 256, 0, m->stream>>>(
+        m->X, t.ll, t.epoch, ((PeerHost*)m->peer)->err, count);
+  else
+    k_add_inplace<<<(int)std::min<int64_t>((count + 255) / 256, 148 * 8), 256, 0, m->stream>>>(m->X, t.plain, count);
   sr_count_launch(m);
 }
 
@@ -1158,7 +1221,8 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   int rc = SR_OK;
   __nv_bfloat16* xh = tc ? tc_xh(m) : nullptr;
   __nv_bfloat16* xl = tc ? tc_xl(m) : nullptr;
-  const float* pending = nullptr;  // tensor parallel: an all-reduced sum still to be added to X
+  TpSum pending;  // tensor parallel: an all-reduced sum still to be added to X
+  int* tp_err = m->peer ? ((PeerHost*)m->peer)->err : nullptr;
   for (int l = 0; l < L; l++) {
     if (cancel && *cancel) {
       sr_prof_span_end(m);
@@ -1175,9 +1239,9 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     if (pending && !fast) tp_add(m, n, pending);
     SR_LAUNCH(m, SR_PROF_NORM,
               if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps, xh, xl,
-                                     pending);
+                                     pending.plain, pending.ll, pending.epoch, tp_err);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[0].values, m->N, n, d, eps));
-    pending = nullptr;
+    pending = TpSum();
     bool done;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_qkv(m, l, n, true));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
@@ -1205,14 +1269,14 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_o(m, l, n, a_split, oy, ores));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->A, n, P[4], o);
-    const float* tsum = nullptr;
+    TpSum tsum;
     if (tp) {
       if ((rc = tp_allreduce(m, n, &tsum)) != SR_OK) return rc;
       if (!fast) tp_add(m, n, tsum);
     }
     SR_LAUNCH(m, SR_PROF_NORM,
               if (fast) fast_rmsnorm(m, m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps, xh, xl,
-                                     tsum);
+                                     tsum.plain, tsum.ll, tsum.epoch, tp_err);
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps));
     o.resid = nullptr;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_gateup(m, l, n, true));

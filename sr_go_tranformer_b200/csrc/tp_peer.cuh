@@ -130,5 +130,109 @@ __global__ void __launch_bounds__(kThreads) k_peer_gather(Args a) {
   }
 }
 
+// ------------------------------------------------------------ LL protocol --
+// The flags travel with the data: a 16-byte line holds two values, each next
+// to the all-reduce's epoch ({v0, e, v1, e}), written by one 16-byte store
+// and read by one 16-byte load, so a reader that sees both flags equal to the
+// epoch also sees both values (the word-level flag scheme of NCCL's LL
+// protocol).  No separate barrier: every consumer waits on the lines it reads.
+__device__ __forceinline__ void st_line(uint4* p, uint4 v) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_line(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+// Bounded wait for a line of epoch e.  After an expiry (here or anywhere:
+// *err) the caller's ok turns false and no further line is waited for.
+__device__ __forceinline__ uint4 wait_line(const uint4* p, uint32_t e, int* err, bool& ok) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; it++) {
+    const uint4 v = ld_line(p);
+    if ((v.y == e && v.w == e) || !ok) return v;
+    if ((it & 63) == 0) {
+      if (*(volatile int*)err) {
+        ok = false;
+        return v;
+      }
+      const uint64_t now = tc::globaltimer();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > tc::kWaitNs) {
+        atomicExch(err, 1);
+        ok = false;
+        return v;
+      }
+    }
+  }
+}
+
+struct LLArgs {
+  const float* part;  // this rank's partial sums, count floats
+  uint4* const* rb;   // [size] every rank's reduce buffer: [size source slots][chunk/2 lines]
+  uint4* const* gb;   // [size] every rank's gather buffer: [count/2 lines]
+  int* err;
+  int64_t count, chunk;  // floats; both multiples of 4
+  uint32_t epoch;
+  int rank, size;
+};
+
+// The whole all-reduce in one kernel.  Line L of chunk q of this rank's
+// partials goes to rank q's reduce buffer (slot = this rank); then this rank's
+// own chunk is summed line by line over the slots in rank order (q = 0, 1, ...,
+// the same order as k_peer_reduce) as the lines arrive, and each sum line goes
+// to every rank's gather buffer.  A CTA pushes before it waits and every rank
+// runs the same grid over the same lines, so no CTA waits on another CTA of its
+// own GPU.  grid <= the resident CTAs (256 threads, no shared memory).
+__global__ void __launch_bounds__(kThreads) k_peer_ll(LLArgs a) {
+  const int64_t cl = a.chunk / 2;
+  const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int q = 0; q < a.size; q++) {
+    const int64_t lo = (int64_t)q * a.chunk;
+    const int64_t nl = (min(a.count, lo + a.chunk) - lo) / 2;
+    uint4* dst = a.rb[q] + (int64_t)a.rank * cl;
+    for (int64_t L = t0; L < nl; L += stride) {
+      const float2 v = *(const float2*)(a.part + lo + 2 * L);
+      st_line(dst + L, make_uint4(__float_as_uint(v.x), a.epoch, __float_as_uint(v.y), a.epoch));
+    }
+  }
+  const int64_t lo = (int64_t)a.rank * a.chunk;
+  const int64_t nl = (min(a.count, lo + a.chunk) - lo) / 2;
+  const uint4* src = a.rb[a.rank];
+  bool ok = true;
+  for (int64_t L = t0; L < nl; L += stride) {
+    float s0 = 0.f, s1 = 0.f;
+    for (int q = 0; q < a.size; q++) {
+      const uint4 w = wait_line(src + (int64_t)q * cl + L, a.epoch, a.err, ok);
+      if (q == 0) {
+        s0 = __uint_as_float(w.x);
+        s1 = __uint_as_float(w.z);
+      } else {
+        s0 += __uint_as_float(w.x);
+        s1 += __uint_as_float(w.z);
+      }
+    }
+    const uint4 line = make_uint4(__float_as_uint(s0), a.epoch, __float_as_uint(s1), a.epoch);
+    for (int p = 0; p < a.size; p++) st_line(a.gb[p] + lo / 2 + L, line);
+  }
+}
+
+// X += the all-reduced sums read from this rank's gather buffer (tp_add for
+// the LL protocol: exact mode, and the last layer before the final norm).
+__global__ void k_add_ll(float* __restrict__ X, const uint4* __restrict__ G, uint32_t epoch, int* err,
+                         int64_t count) {
+  bool ok = true;
+  for (int64_t L = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; L < count / 2; L += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 w = wait_line(G + L, epoch, err, ok);
+    X[2 * L] += __uint_as_float(w.x);
+    X[2 * L + 1] += __uint_as_float(w.z);
+  }
+}
+
 }  // namespace peer
 }  // namespace sr

@@ -130,6 +130,11 @@ class Model:
         assert len(blob) == A.SR_TP_PEER_HANDLE_BYTES * self.tp_size
         A.check(A.lib().sr_tp_peer_open(self.h, C.create_string_buffer(blob, len(blob))))
 
+    def tp_peer_set_protocol(self, protocol):
+        """"barrier" (two kernels with flag barriers) or "ll" (one kernel, flags
+        inside every 16-byte line); after tp_peer_open, the same on every rank."""
+        A.check(A.lib().sr_tp_peer_set_protocol(self.h, {"barrier": A.SR_PEER_BARRIER, "ll": A.SR_PEER_LL}[protocol]))
+
     @property
     def page_tokens(self):
         return self.desc.page_tokens

@@ -52,8 +52,10 @@ def _run(rank, size, nccl_id, mode, q, allreduce="nccl", folder=None):
     m = S.Model(d, device=rank, tp_rank=rank, tp_size=size, nccl_id=nccl_id)
     m.init_synthetic(123)
     m.set_mode(mode)
-    if allreduce == "peer":
+    if allreduce in ("peer", "peer-ll"):
         m.tp_peer_open(exchange_handles(m, rank, size, folder))
+        if allreduce == "peer-ll":
+            m.tp_peer_set_protocol("ll")
     pool = S.PagePool(m, 128)
     rng = np.random.default_rng(5)
     prompts = [rng.integers(0, 2048, size=n).tolist() for n in (300, 45, 64, 40)]
@@ -165,3 +167,21 @@ def test_peer_allreduce_absent_rank_times_out(tmp_path):
     assert code == A.SR_ETIMEOUT
     assert elapsed < 30
     assert pos == 0
+
+
+@pytest.mark.skipif(os.environ.get("SR_GPU_PEER_LL") != "1",
+                    reason="the LL peer protocol has not yet run on a GPU (set SR_GPU_PEER_LL=1)")
+@pytest.mark.parametrize("size", [2, 4])
+@pytest.mark.parametrize("mode", ["exact", "fast"])
+def test_peer_ll_protocol_equals_barrier_protocol(mode, size, tmp_path):
+    """SR_PEER_LL sums each chunk in the same rank order as SR_PEER_BARRIER, so
+    the logits of every rank must be bit-identical between the two protocols."""
+    if _gpus() < size:
+        pytest.skip(f"needs {size} GPUs")
+    (tmp_path / "a").mkdir()
+    (tmp_path / "b").mkdir()
+    ll = _tp_logits(size, mode, "peer-ll", str(tmp_path / "a"))
+    barrier = _tp_logits(size, mode, "peer", str(tmp_path / "b"))
+    for step in range(len(barrier[0])):
+        for r in range(size):
+            assert np.array_equal(ll[r][step], barrier[r][step]), (step, r)
