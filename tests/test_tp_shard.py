@@ -207,3 +207,18 @@ def test_gpt2_parameter_table_matches_oracle(oracle):
             S.tp_shard(desc, 0, 1, om.nparams)
         with pytest.raises(Exception):  # one GPU only
             S.tp_shard(desc, 0, 2, 0)
+
+
+def test_gpt2_description_checks():
+    """validate_desc's GPT-2 rules (readGPT2Config's profile, M:446-513): one
+    KV head per query head, a tied head, a position table covering the
+    context, one GPU; an unknown architecture is refused."""
+    from sr_go_tranformer_b200 import step as S
+    hf = dict(model_type="gpt2", vocab_size=258, n_embd=24, n_inner=40, n_layer=2, n_head=6, n_positions=64)
+    good = S.desc_from_hf(hf, "q8", 32)
+    assert S.tp_shard(good, 0, 1, 1) == (0, 64, 0, 24)  # wpe: n_positions rows
+    for field, value in (("kv_heads", 2), ("tied", 0), ("qkv_bias", 1), ("positions", 32), ("arch", 7)):
+        d = S.desc_from_hf(hf, "q8", 32)
+        setattr(d, field, value)
+        with pytest.raises(Exception):
+            S.tp_shard(d, 0, 1, 0)
