@@ -159,3 +159,34 @@ def test_errors(srlib):
     assert A.lib().sr_text_decoder_create(A.SR_TEXT_CLEANUP, None, 0, C.byref(h)) == A.SR_EINVAL
     assert A.lib().sr_text_decoder_create(64, None, 0, C.byref(h)) == A.SR_EINVAL
     assert A.lib().sr_text_decoder_create(A.SR_TEXT_MISTRAL, None, 10, C.byref(h)) == A.SR_EINVAL
+
+
+def _random_pieces(rng, data):
+    cuts = sorted(rng.choice(len(data) + 1, size=min(len(data), int(rng.integers(0, 8))), replace=False)) if data else []
+    out, prev = [], 0
+    for c in list(cuts) + [len(data)]:
+        out.append(data[prev:c])
+        prev = c
+    return out
+
+
+def test_random_streams_split_anywhere(srlib):
+    """Property check over seeded random byte streams (ASCII, multi-byte
+    sequences, truncated and invalid bytes, cleanup patterns): pieces cut at
+    random points decode to the same text as the whole stream, for the plain,
+    HF and HF+cleanup decoders; the plain decoder equals ToValidUTF8."""
+    import numpy as np
+    TD = _td()
+    rng = np.random.default_rng(2024)
+    alphabet = [b"a", b" ", b".", b"'", b"s", b"n't", b"\xc3\xa9", b"\xe2\x82\xac", b"\xf0\x9f\x8c\x80", b"\xe2\x82",
+                b"\xf0\x9f", b"\xff", b"\x80", b"\xc0", b"\xed\xa0\x80", b" 're", b" ,", b" !"]
+    for _ in range(300):
+        data = b"".join(alphabet[int(i)] for i in rng.integers(0, len(alphabet), size=int(rng.integers(0, 24))))
+        pieces = _random_pieces(rng, data)
+        for kw in (dict(), dict(hf=True), dict(hf=True, cleanup=True)):
+            whole = TD(**kw).push(data, True)
+            d = TD(**kw)
+            got = "".join(d.push(p, False) for p in pieces) + d.push(b"", True)
+            assert got == whole, (kw, data, pieces)
+        assert TD().push(data, True) == to_valid_utf8(data), data
+        assert TD(hf=True).push(data, True) == data.decode("utf-8", "replace"), data
