@@ -77,3 +77,30 @@ def test_prefix_limit_caps_snapshot_pages(oracle):
     assert got == base
     assert st["prefix_pages"] == 1
     assert st["prefix_tokens"] == (len(reqs) - 1) * m.cfg.page_tokens
+
+
+def test_prefix_cache_random_scenarios(oracle):
+    """Seeded random request mixes (several shared system prompts, random
+    suffixes, output lengths, batch sizes, snapshot limits, tail reuse): the
+    simulated engine with the prefix cache always returns exactly the outputs
+    of the engine without it, and never reuses more tokens than a prompt holds."""
+    m = _model(oracle)
+    rng = np.random.default_rng(77)
+    for scenario in range(5):
+        heads = [rng.integers(0, 300, size=int(rng.integers(10, 50))).tolist() for _ in range(2)]
+        reqs = []
+        for i in range(int(rng.integers(3, 7))):
+            head = heads[int(rng.integers(0, 2))]
+            tail = rng.integers(0, 300, size=int(rng.integers(1, 10))).tolist()
+            r = dict(ids=head + tail, max_tokens=int(rng.integers(1, 5)), seed=int(rng.integers(1, 1000)))
+            if rng.random() < 0.5:
+                r.update(temperature=0.9, top_k=30, top_p=0.9, penalty=1.05)
+            reqs.append(r)
+        mb = int(rng.integers(1, 4))
+        limit, plimit, tail = 28, int(rng.integers(1, 5)), bool(rng.random() < 0.5)
+        base, _ = simulate(m, reqs, limit, mb, 16, 8, 1)
+        st = {}
+        got, _ = simulate(m, reqs, limit, mb, 16, 8, 1, prefix_limit=plimit, prefix_tail=tail, stats=st)
+        assert got == base, scenario
+        assert st["prefix_tokens"] <= sum(len(r["ids"]) - 1 for r in reqs)
+        assert st["prefix_pages"] <= plimit
