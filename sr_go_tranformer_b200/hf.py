@@ -574,3 +574,63 @@ def load_hf_model(path, weight_format="q8", context_limit=0, page_tokens=32, dev
         m.close()
         raise
     return m, a
+
+
+def _bench(dim=2048, hidden=8192, layers=8, vocab=32000, shards=2, seed=0):
+    """Host throughput of the import: a temporary Llama-shaped BF16 checkpoint
+    (seeded values, `shards` files with an index) is validated and every tensor
+    widened to fp32 in parameter order (the device upload is not included)."""
+    import shutil
+    import tempfile
+    import time
+    cfg = {"architectures": ["LlamaForCausalLM"], "model_type": "llama", "vocab_size": vocab, "hidden_size": dim,
+           "intermediate_size": hidden, "num_hidden_layers": layers, "num_attention_heads": dim // 64,
+           "num_key_value_heads": dim // 256, "max_position_embeddings": 4096, "rope_theta": 5e5,
+           "rms_norm_eps": 1e-5, "hidden_act": "silu", "tie_word_embeddings": False, "bos_token_id": 1,
+           "eos_token_id": 2}
+    h = HFConfig(cfg, 0)
+    h.model_type = "llama"
+    specs = h.specs()
+    rng = np.random.default_rng(seed)
+    d = tempfile.mkdtemp(prefix="sr_hf_bench_")
+    try:
+        with open(os.path.join(d, "config.json"), "w") as f:
+            json.dump(cfg, f)
+        parts = np.array_split(np.arange(len(specs)), shards)
+        wm, total = {}, 0
+        for k, idx in enumerate(parts):
+            fn = f"model-{k + 1:05d}-of-{shards:05d}.safetensors"
+            header, off = {}, 0
+            for i in idx:
+                name, shape = specs[i]
+                n = int(np.prod(shape)) * 2
+                header[name] = {"dtype": "BF16", "shape": list(shape), "data_offsets": [off, off + n]}
+                off += n
+                wm[name] = fn
+            hb = json.dumps(header).encode()
+            with open(os.path.join(d, fn), "wb") as f:
+                f.write(len(hb).to_bytes(8, "little"))
+                f.write(hb)
+                for i in idx:
+                    count = int(np.prod(specs[i][1]))
+                    f.write((rng.standard_normal(count, dtype=np.float32) * 0.02).view(np.uint32).__rshift__(16)
+                            .astype("<u2").tobytes())
+            total += off
+        with open(os.path.join(d, "model.safetensors.index.json"), "w") as f:
+            json.dump({"weight_map": wm}, f)
+        t0 = time.perf_counter()
+        a = open_hf_archive(d)
+        t1 = time.perf_counter()
+        n = sum(p.size for p in a.params())
+        t2 = time.perf_counter()
+        print(f"{h.parameter_count():,} parameters, {total / 1e9:.2f} GB BF16 in {shards} shards: "
+              f"headers checked in {(t1 - t0) * 1e3:.1f} ms; values read and widened at {total / (t2 - t1) / 1e9:.2f} "
+              f"GB/s of checkpoint ({n / (t2 - t1) / 1e6:.0f} M values/s), one host thread")
+    finally:
+        shutil.rmtree(d)
+
+
+if __name__ == "__main__":
+    import sys
+    if "--bench" in sys.argv:
+        _bench()

@@ -59,3 +59,27 @@ class TextDecoder:
         """PushToken for one sampled token and its piece."""
         b = bytes(piece)
         return self._call(A.lib().sr_text_decoder_push_token, (self.h, int(token_id), b, len(b), int(final)), len(b))
+
+
+def _bench(tokens=200_000, seed=0):
+    """Host throughput of PushToken on a seeded stream of ByteLevel-like pieces
+    (1-4 bytes, some multi-byte characters split across tokens)."""
+    import time
+    rng = np.random.default_rng(seed)
+    text = "".join(rng.choice(list("abcde fghij.,'é€🌀日本")) for _ in range(tokens * 2)).encode()
+    cuts = np.sort(rng.choice(len(text), size=tokens - 1, replace=False))
+    pieces = [text[a:b] for a, b in zip(np.r_[0, cuts], np.r_[cuts, len(text)])]
+    for name, kw in (("plain", {}), ("hf", dict(hf=True)), ("hf+cleanup", dict(hf=True, cleanup=True))):
+        d = TextDecoder(**kw)
+        t0 = time.perf_counter()
+        out = [d.push_token(i, p, i == len(pieces) - 1) for i, p in enumerate(pieces)]
+        dt = time.perf_counter() - t0
+        assert "".join(out) == TextDecoder(**kw).push(text, True)
+        print(f"{name:11s} {len(pieces) / dt:12,.0f} tokens/s  ({dt * 1e6 / len(pieces):.2f} us per token, "
+              f"{len(text) / dt / 1e6:.1f} MB/s, Python call included)")
+
+
+if __name__ == "__main__":
+    import sys
+    if "--bench" in sys.argv:
+        _bench()
