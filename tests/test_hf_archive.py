@@ -437,3 +437,42 @@ def test_reference_gpt2_directories(npz):
     var = os.path.basename(npz)[:-4].split("-", 2)[2]
     a = hf.open_hf_archive(os.path.join(REF_TESTDATA, "hf-gpt2", var))
     _params_equal(a, np.load(npz))
+
+
+@pytest.mark.parametrize("dtype", ["BF16", "F16", "F32"])
+def test_threaded_widening_matches_one_thread(tmp_path, dtype):
+    """read_tensor widens large tensors in slices on several threads: the
+    values equal the one-thread widening bit for bit, and a non-finite value in
+    a late slice is still refused."""
+    d = str(tmp_path)
+    cfg = {"architectures": ["LlamaForCausalLM"], "model_type": "llama", "vocab_size": 70000, "hidden_size": 128,
+           "intermediate_size": 64, "num_hidden_layers": 1, "num_attention_heads": 2, "num_key_value_heads": 1,
+           "max_position_embeddings": 64, "rope_theta": 1e4, "rms_norm_eps": 1e-5, "hidden_act": "silu",
+           "tie_word_embeddings": True, "bos_token_id": 1, "eos_token_id": 2}
+    h = hf.HFConfig(cfg, 0)
+    h.model_type = "llama"
+    rng = np.random.default_rng(5)
+    tensors = {}
+    for name, shape in h.specs():
+        a = (rng.standard_normal(int(np.prod(shape)), dtype=np.float32) * 0.02).reshape(shape)
+        if dtype == "BF16":
+            a = (a.view(np.uint32) & 0xFFFF0000).view(np.float32)
+        elif dtype == "F16":
+            a = a.astype(np.float16).astype(np.float32)
+        tensors[name] = (a, dtype)
+    os.makedirs(d, exist_ok=True)
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    write_safetensors(os.path.join(d, "model.safetensors"), tensors)
+    a = hf.open_hf_archive(d)
+    big = "model.embed_tokens.weight"  # 70000 x 128 = 8.96 M values: three slices
+    one = a.read_tensor(big, threads=1)
+    many = a.read_tensor(big, threads=4)
+    assert np.array_equal(one.view(np.uint32), many.view(np.uint32))
+    assert np.array_equal(one, tensors[big][0])
+    bad = tensors[big][0].copy()
+    bad.reshape(-1)[-5] = np.inf
+    tensors[big] = (bad, dtype)
+    write_safetensors(os.path.join(d, "model.safetensors"), tensors)
+    with pytest.raises(hf.HFError, match="non-finite"):
+        hf.open_hf_archive(d).read_tensor(big, threads=4)
