@@ -484,9 +484,20 @@ class HFArchive:
 
     def load_into(self, model):
         """Every tensor, in parameter order, through sr_model_load_param_f32 (the
-        device quantizer restates readParam, M:857-880)."""
-        for i, values in enumerate(self.params()):
-            model.load_param_f32(i, values)
+        device quantizer restates readParam, M:857-880).  The next tensor is read
+        and widened on a host thread while the current one uploads."""
+        from concurrent.futures import ThreadPoolExecutor
+        it = self.params()
+        with ThreadPoolExecutor(1) as ex:
+            pending = ex.submit(next, it, None)
+            i = 0
+            while True:
+                values = pending.result()
+                if values is None:
+                    break
+                pending = ex.submit(next, it, None)
+                model.load_param_f32(i, values)
+                i += 1
 
 
 def open_hf_archive(path, context_limit=0):

@@ -476,3 +476,26 @@ def test_threaded_widening_matches_one_thread(tmp_path, dtype):
     write_safetensors(os.path.join(d, "model.safetensors"), tensors)
     with pytest.raises(hf.HFError, match="non-finite"):
         hf.open_hf_archive(d).read_tensor(big, threads=4)
+
+
+@pytest.mark.parametrize("npz", [FIXTURES[0], GPT2_NPZ[1]], ids=["llama", "gpt2"])
+def test_load_into_uploads_every_parameter_in_order(tmp_path, npz):
+    """load_into (reading ahead on a host thread) hands sr_model_load_param_f32
+    every parameter exactly once, in parameter order, with the right values."""
+    class Recorder:
+        def __init__(self):
+            self.calls = []
+
+        def load_param_f32(self, i, values):
+            self.calls.append((i, np.array(values, copy=True)))
+
+    if "gpt2" in npz:
+        _, _, z = make_gpt2_checkpoint(str(tmp_path), npz)
+    else:
+        _, _, z, _ = make_checkpoint(str(tmp_path), npz, shards=2)
+    rec = Recorder()
+    hf.open_hf_archive(str(tmp_path)).load_into(rec)
+    n = len([k for k in z.files if k.startswith("param_")])
+    assert [i for i, _ in rec.calls] == list(range(n))
+    for i, v in rec.calls:
+        assert np.array_equal(v.reshape(-1).view(np.uint32), z[f"param_{i}"].reshape(-1).view(np.uint32)), i
