@@ -124,14 +124,40 @@ def traffic_per_position():
         return None
 
 
+def advance_sessions(pos, hist, hoff, ids, prompts, outs):
+    """Host bookkeeping after one decode step: each session's sampled id joins
+    its history and its position advances.  A session that has used its whole
+    output budget (prompt + outs positions) restarts decoding right after its
+    prompt, as a fresh request in its slot would, so the step keeps its shape
+    and its pages for any number of steps.  Returns (pos, hist, hoff)."""
+    hist = np.insert(hist, hoff[1:], ids)  # append each session's new id
+    hoff = hoff + np.arange(len(hoff), dtype=np.int32)
+    pos = pos + 1
+    done = np.nonzero(pos >= prompts + outs)[0]
+    if done.size:
+        keep = np.ones(hist.size, dtype=bool)
+        for i in done:
+            keep[hoff[i] + int(prompts[i]):hoff[i + 1]] = False
+        lens = np.diff(hoff)
+        lens[done] = prompts[done]
+        hist = hist[keep]
+        hoff = np.zeros_like(hoff)
+        hoff[1:] = np.cumsum(lens)
+        pos = pos.copy()
+        pos[done] = prompts[done]
+    return pos.astype(np.int32), hist, hoff.astype(np.int32)
+
+
 class DecodeState:
     """256 sessions in steady decode over one device model and page pool."""
 
-    def __init__(self, cfg, model, warmup, workload_rank=0):
+    def __init__(self, cfg, model, warmup, workload_rank=0, steps=0):
+        """steps: the decode steps that follow the warm-up; the sessions' starting
+        offsets leave room for all of them where the output budget allows."""
         from sr_go_tranformer_b200 import _abi as A
         from sr_go_tranformer_b200 import step as S
         self.A, self.S, self.cfg = A, S, cfg
-        prompts, outs, offsets, rng = workload(cfg, workload_rank, warmup)
+        prompts, outs, offsets, rng = workload(cfg, workload_rank, warmup + steps)
         self.prompts, self.outs = prompts, outs
         n = cfg["sessions"]
         pt = cfg["page_tokens"]
@@ -182,9 +208,7 @@ class DecodeState:
         # bytes crossing the host boundary this step (sr_upload_batch + sampler staging)
         self.h2d_bytes += 4 * (1864 + pids.size) + n * 32 + 4 * (n + 1) + 4 * hist.size + 8 * n
         self.d2h_bytes += 8 * n + 4 * n + 4 * n
-        self.hist = np.insert(hist, hoff[1:], self.ids)  # append each session's new id
-        self.hoff = hoff + np.arange(n + 1, dtype=np.int32)
-        self.pos += 1
+        self.pos, self.hist, self.hoff = advance_sessions(self.pos, hist, hoff, self.ids, self.prompts, self.outs)
         self.last[:] = self.ids
 
     def profile(self, reset=False):
@@ -371,7 +395,7 @@ def main():
         model.tp_peer_open(handles)
         if args.allreduce == "peer-ll":
             model.tp_peer_set_protocol("ll")
-    st = DecodeState(cfg, model, W, workload_rank=0 if tp else rank)
+    st = DecodeState(cfg, model, W, workload_rank=0 if tp else rank, steps=K + 1)  # + the profiled step
     for _ in range(W):
         st.step()
     ext = torch.cuda.ExternalStream(st.stream())
