@@ -373,6 +373,21 @@ int sr_text_decoder_push(sr_text_decoder *d, const uint8_t *bytes, int64_t n, in
 int sr_text_decoder_push_token(sr_text_decoder *d, int32_t id, const uint8_t *piece, int64_t n, int32_t final,
                                char *out, int64_t cap, int64_t *n_out, int64_t *queued);
 
+/* The engine's token events (TokenEvent, :7643-7647, sent at :8451-8462): with
+ * the tokenizer's pieces table (bytes of every id concatenated, offsets[vocab+1])
+ * and the decoder flags, every sampled token yields an event holding its id and
+ * the text it completes (PushToken, final on the request's last token).  Set
+ * only while no session is active; vocab 0 turns events off (the default).
+ * The queue is unbounded: the reference's slow-consumer cut-off (:8460-8462)
+ * is the caller's policy. */
+int sr_engine_set_pieces(sr_engine *e, const uint8_t *pieces, const int64_t *offsets, int32_t vocab, int32_t flags,
+                         const uint8_t *fallback);
+/* Pop the oldest token event: request id (-1 when none), token id, the text
+ * (*n_text bytes into text; if cap is smaller, SR_EINVAL with *n_text set and
+ * the event kept), and whether it was the request's last token. */
+int sr_engine_poll_token(sr_engine *e, int64_t *request_id, int32_t *token_id, char *text, int32_t cap,
+                         int32_t *n_text, int32_t *final);
+
 #ifdef __cplusplus
 }
 #endif

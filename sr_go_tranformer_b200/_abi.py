@@ -31,7 +31,7 @@ EXPORTED = [
     "sr_step_noalloc", "sr_model_create_tp", "sr_tp_unique_id", "sr_tp_shard", "sr_engine_latency",
     "sr_kvpool_copy_rows", "sr_engine_clear_prefix", "sr_tp_peer_handle", "sr_tp_peer_open",
     "sr_text_decoder_create", "sr_text_decoder_destroy", "sr_text_decoder_push", "sr_text_decoder_push_token",
-    "sr_tp_peer_set_protocol",
+    "sr_tp_peer_set_protocol", "sr_engine_set_pieces", "sr_engine_poll_token",
 ]
 PROF_CLASSES = ["meta", "embed", "norm", "linear", "rope_kv", "attention", "swiglu", "head", "sample"]
 
@@ -126,6 +126,9 @@ def lib():
         "sr_tp_peer_handle": (C.c_int, [P, P]),
         "sr_tp_peer_open": (C.c_int, [P, P]),
         "sr_tp_peer_set_protocol": (C.c_int, [P, I32]),
+        "sr_engine_set_pieces": (C.c_int, [P, P, P, I32, I32, P]),
+        "sr_engine_poll_token": (C.c_int, [P, C.POINTER(I64), C.POINTER(I32), P, I32, C.POINTER(I32),
+                                           C.POINTER(I32)]),
         "sr_text_decoder_create": (C.c_int, [I32, P, I32, C.POINTER(P)]),
         "sr_text_decoder_destroy": (C.c_int, [P]),
         "sr_text_decoder_push": (C.c_int, [P, P, I64, I32, P, I64, C.POINTER(I64), C.POINTER(I64)]),

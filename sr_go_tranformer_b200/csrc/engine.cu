@@ -10,6 +10,7 @@
 // restatement.
 #include <algorithm>
 #include <chrono>
+#include <cstring>
 #include <deque>
 #include <string>
 #include <vector>
@@ -43,6 +44,15 @@ struct EngSession {
   uint64_t rng = 0;            // engineSession.RNG
   Clock::time_point last_token;  // engineSession.LastToken
   bool has_token = false;
+  sr_text_decoder* text = nullptr;  // engineSession.Text (token events only)
+};
+
+// TokenEvent (M:7643-7647): one sampled token and the text it completes.
+struct TextEvent {
+  int64_t request_id;
+  int32_t token_id;
+  std::string text;
+  int32_t final;
 };
 
 struct Finished {
@@ -80,6 +90,14 @@ struct sr_engine {
   int32_t rotation = 0;
   int64_t next_id = 0;
   std::deque<Finished> finished;
+  // Token events (M:8451-8462): the pieces table (bytes of every id) and the
+  // decoder flags newTextDecoder would pick; off until sr_engine_set_pieces.
+  bool text_on = false;
+  int32_t text_flags = 0;
+  std::string pieces;
+  std::vector<int64_t> piece_off;
+  std::vector<uint8_t> fallback;
+  std::deque<TextEvent> events;
   sr_engine_stats st{};
   std::vector<int32_t> last_counts;
   // firstTokenLatency / tokenGap observations (M:8441-8447), in seconds
@@ -114,6 +132,10 @@ static void close_session(sr_engine* e, EngSession& s) {
   }
   s.pages.clear();
   s.shared_pages = 0;
+  if (s.text) {
+    sr_text_decoder_destroy(s.text);
+    s.text = nullptr;
+  }
 }
 
 static int32_t snapshot_page(const sr_engine* e, int32_t i) { return (int32_t)(e->limit + i); }
@@ -270,6 +292,8 @@ extern "C" int sr_engine_create(sr_model* m, const sr_engine_config* cfg, sr_eng
 
 extern "C" int sr_engine_destroy(sr_engine* e) {
   if (!e) return sr_fail(SR_EINVAL, "null engine");
+  for (auto& s : e->sessions)
+    if (s.text) sr_text_decoder_destroy(s.text);
   if (e->pool) sr_kvpool_destroy(e->pool);
   delete e;
   return SR_OK;
@@ -338,6 +362,9 @@ extern "C" int sr_engine_tick(sr_engine* e, int32_t* rows) {
       e->st.prefix_tokens += s.pos;
     }
     s.cursor = s.pos;  // engineSession.Cursor = cache.Pos
+    if (e->text_on)  // newTextDecoder (M:8363)
+      sr_text_decoder_create(e->text_flags, e->fallback.empty() ? nullptr : e->fallback.data(),
+                             (int32_t)e->fallback.size(), &s.text);
     e->sessions.push_back(std::move(s));
     e->st.active++;
     account(e);
@@ -431,6 +458,22 @@ extern "C" int sr_engine_tick(sr_engine* e, int32_t* rows) {
     int32_t reason = -1;
     if (e->c.eos_id >= 0 && id == e->c.eos_id) reason = 1;
     else if ((int32_t)s.output.size() == s.req.max_tokens) reason = 0;
+    if (s.text) {  // TokenEvent{id, Text.PushToken(id, pieces[id], final)} (M:8458-8459)
+      const bool in_vocab = id >= 0 && (size_t)id + 1 < e->piece_off.size();
+      const int64_t lo = in_vocab ? e->piece_off[id] : 0, len = in_vocab ? e->piece_off[id + 1] - lo : 0;
+      std::string out((size_t)(3 * len + 4096), '\0');
+      int64_t n_out = 0, queued = 0;
+      sr_text_decoder_push_token(s.text, id, (const uint8_t*)e->pieces.data() + lo, len, reason >= 0, &out[0],
+                                 (int64_t)out.size(), &n_out, &queued);
+      out.resize((size_t)n_out);
+      while (queued > 0) {
+        std::string more((size_t)queued + 16, '\0');
+        int64_t m = 0;
+        sr_text_decoder_push(s.text, nullptr, 0, 0, &more[0], (int64_t)more.size(), &m, &queued);
+        out.append(more, 0, (size_t)m);
+      }
+      e->events.push_back(TextEvent{s.req.id, id, std::move(out), reason >= 0 ? 1 : 0});
+    }
     if (reason >= 0) finish(e, s, reason);
     else alive.push_back(std::move(s));
   }
@@ -511,5 +554,55 @@ extern "C" int sr_engine_session_pages(const sr_engine* e, int32_t i, int32_t* p
   const auto& p = e->sessions[i].pages;
   *n_pages = (int32_t)p.size();
   if (pages) std::copy(p.begin(), p.begin() + std::min<size_t>(p.size(), (size_t)std::max(cap, 0)), pages);
+  return SR_OK;
+}
+
+extern "C" int sr_engine_set_pieces(sr_engine* e, const uint8_t* pieces, const int64_t* offsets, int32_t vocab,
+                                    int32_t flags, const uint8_t* fallback) {
+  if (!e || (vocab > 0 && !offsets)) return sr_fail(SR_EINVAL, "null argument");
+  if (!e->sessions.empty()) return sr_fail(SR_EINVAL, "token text can be configured only while no session is active");
+  if (vocab <= 0) {  // off
+    e->text_on = false;
+    e->pieces.clear();
+    e->piece_off.clear();
+    e->fallback.clear();
+    return SR_OK;
+  }
+  if (offsets[0] != 0) return sr_fail(SR_EINVAL, "piece offsets must start at 0");
+  for (int32_t i = 0; i < vocab; i++)
+    if (offsets[i + 1] < offsets[i]) return sr_fail(SR_EINVAL, "piece offsets must not decrease");
+  if (offsets[vocab] > 0 && !pieces) return sr_fail(SR_EINVAL, "null pieces");
+  sr_text_decoder* probe = nullptr;  // checks the flags and the fallback table
+  int rc = sr_text_decoder_create(flags, fallback, (flags & SR_TEXT_MISTRAL) ? vocab : 0, &probe);
+  if (rc != SR_OK) return rc;
+  sr_text_decoder_destroy(probe);
+  e->pieces.assign((const char*)pieces, (size_t)offsets[vocab]);
+  e->piece_off.assign(offsets, offsets + vocab + 1);
+  e->fallback.clear();
+  if ((flags & SR_TEXT_MISTRAL) && fallback) e->fallback.assign(fallback, fallback + vocab);
+  e->text_flags = flags;
+  e->text_on = true;
+  return SR_OK;
+}
+
+extern "C" int sr_engine_poll_token(sr_engine* e, int64_t* request_id, int32_t* token_id, char* text, int32_t cap,
+                                    int32_t* n_text, int32_t* final) {
+  if (!e || !request_id || !token_id || !n_text || !final) return sr_fail(SR_EINVAL, "null argument");
+  if (e->events.empty()) {
+    *request_id = -1;
+    *token_id = -1;
+    *n_text = 0;
+    *final = 0;
+    return SR_OK;
+  }
+  const TextEvent& ev = e->events.front();
+  *n_text = (int32_t)ev.text.size();
+  if ((int64_t)ev.text.size() > (int64_t)std::max(cap, 0) || (!text && !ev.text.empty()))
+    return sr_fail(SR_EINVAL, "text buffer too small: *n_text bytes needed");  // the event stays queued
+  *request_id = ev.request_id;
+  *token_id = ev.token_id;
+  *final = ev.final;
+  if (!ev.text.empty()) memcpy(text, ev.text.data(), ev.text.size());
+  e->events.pop_front();
   return SR_OK;
 }

@@ -70,6 +70,36 @@ class Engine:
         A.check(A.lib().sr_engine_latency(self.h, C.byref(t), C.byref(g), C.byref(nt), C.byref(ng)))
         return {"ttft_p50_ms": t.value, "itl_p50_ms": g.value, "first_tokens": nt.value, "gaps": ng.value}
 
+    def set_pieces(self, pieces, hf=False, cleanup=False, mistral=False, fallback=None):
+        """Token events with text (TokenEvent, M:8451-8462): pieces[i] is the bytes
+        of token i; the flags are the decoder's (newTextDecoder).  Call while idle."""
+        blob = b"".join(bytes(p) for p in pieces)
+        off = np.zeros(len(pieces) + 1, dtype=np.int64)
+        off[1:] = np.cumsum([len(p) for p in pieces])
+        flags = (A.SR_TEXT_HF if hf else 0) | (A.SR_TEXT_CLEANUP if cleanup else 0) | \
+            (A.SR_TEXT_MISTRAL if mistral else 0)
+        fb = None if fallback is None else np.ascontiguousarray(fallback, dtype=np.uint8)
+        self._pieces = (blob, off, fb)  # kept alive for the call
+        A.check(A.lib().sr_engine_set_pieces(self.h, C.create_string_buffer(blob, max(len(blob), 1)),
+                                             off.ctypes.data_as(C.c_void_p), len(pieces), flags,
+                                             None if fb is None else fb.ctypes.data_as(C.c_void_p)))
+
+    def poll_token(self):
+        """(request id, token id, text, final) of the oldest token event, or None."""
+        rid, tid, n, fin = C.c_int64(), C.c_int32(), C.c_int32(), C.c_int32()
+        cap = 4096
+        while True:
+            buf = C.create_string_buffer(cap)
+            rc = A.lib().sr_engine_poll_token(self.h, C.byref(rid), C.byref(tid), buf, cap, C.byref(n), C.byref(fin))
+            if rc == A.SR_EINVAL and n.value > cap:
+                cap = n.value
+                continue
+            A.check(rc)
+            break
+        if rid.value < 0:
+            return None
+        return rid.value, tid.value, buf.raw[:n.value].decode("utf-8"), bool(fin.value)
+
     def clear_prefix(self):
         """Drop the prefix snapshot (clearPrefix, M:8236-8241); applied once the engine is idle."""
         A.check(A.lib().sr_engine_clear_prefix(self.h))

@@ -415,3 +415,38 @@ def test_engine_prefix_config_errors(oracle, srlib):
     e = Engine(dm, max_batch=2, cache_bytes=8 * pb, prefix_cache_bytes=3 * pb)
     assert e.stats()["pool_limit"] == 5
     e.close()
+
+
+@pytest.mark.skipif(__import__("os").environ.get("SR_GPU_ENGINE_TEXT") != "1",
+                    reason="engine token events have not yet run on a GPU (set SR_GPU_ENGINE_TEXT=1)")
+def test_engine_token_events(oracle, srlib):
+    """TokenEvent (M:8451-8462): one event per sampled token, in order, whose
+    texts concatenate to the decoder's text of the request's pieces; the last
+    is final."""
+    from sr_go_tranformer_b200.engine import Engine
+    from sr_go_tranformer_b200.text import TextDecoder
+    om, dm = synthetic_pair(oracle, srlib, "q8", 16, vocab=300)
+    euro = "€".encode()
+    pieces = [bytes([97 + i % 26]) if i % 7 else euro[:2] if i % 2 else euro[2:] for i in range(300)]
+    eng = Engine(dm, max_batch=2, token_budget=16, prefill_chunk=8, mixed_prefill_chunk=1,
+                 cache_bytes=24 * om.page_elements * 4)
+    eng.set_pieces(pieces, hf=True)
+    rng = np.random.default_rng(3)
+    rids = [eng.submit(rng.integers(0, 300, size=int(rng.integers(2, 20))).tolist(), int(rng.integers(2, 9)),
+                       0.9, 20, 0.9, 1.0, 11 + i) for i in range(3)]
+    done = eng.run_to_completion()
+    events = {}
+    while True:
+        ev = eng.poll_token()
+        if ev is None:
+            break
+        events.setdefault(ev[0], []).append(ev[1:])
+    for rid in rids:
+        out, _ = done[rid]
+        evs = events[rid]
+        assert [t for t, _, _ in evs] == out
+        assert [f for _, _, f in evs] == [False] * (len(out) - 1) + [True]
+        d = TextDecoder(hf=True)
+        want = "".join(d.push_token(t, pieces[t], k == len(out) - 1) for k, t in enumerate(out))
+        assert "".join(x for _, x, _ in evs) == want
+    eng.close()
