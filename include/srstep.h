@@ -230,14 +230,24 @@ int sr_step(sr_model *m, sr_kvpool *pool, const sr_batch *batch, float *logits_h
  * arguments, validation and outputs as sr_step (without the cancel flag); the
  * projections and norms run in the exact order, attention runs as split-K
  * flash-decoding whose partial results use a 16 MiB scratch array compiled into
- * the library (resident on every GPU that loads it).  A batch needing more
- * scratch -- rows x kv_heads x ceil(max context / 256) x group x (head_dim+2)
- * floats -- is rejected with SR_EINVAL; head_dim must be 64 or 128 and at most
- * 8 query heads may share a KV head (SR_EUNSUPPORTED otherwise).  The first
+ * the library (resident on every GPU that loads it).  Row r of the batch
+ * attends to c_r = pos + (r's index in its chunk) + 1 positions, cut into
+ * splits of 512 positions; a batch whose scratch,
+ *   sum over rows of ceil(c_r / 512) x kv_heads x group x (head_dim + 2)
+ * floats, exceeds 16 MiB is rejected with SR_EINVAL; head_dim must be 64 or
+ * 128 and at most 8 query heads may share a KV head (SR_EUNSUPPORTED
+ * otherwise).  The first
  * call on each device resolves the array's address; make it before any stream
  * capture.  Calls that overlap on one device race on the shared array.  Never
  * calls cudaMalloc or cudaFree. */
 int sr_step_noalloc(sr_model *m, sr_kvpool *pool, const sr_batch *batch, float *logits_host);
+/* One projection of a loaded matrix parameter: y[rows x out] = x[rows x in]
+ * W^T, as linearIntoWithExecutor computes it (:3942-3968) -- FP32 sequential
+ * dots, Q8/Q4 4-strided partials per 64-column block (:4074-4780) in
+ * SR_MODE_EXACT, the step's fast kernels in SR_MODE_FAST.  x and y are host
+ * fp32 arrays, rows 1..1024.  For kernel-level parity checks and diagnostics
+ * (allocates its device copies per call). */
+int sr_linear(sr_model *m, int32_t index, int32_t rows, const float *x, float *y);
 /* Device pointer of the last step's logits [n_sessions x vocab]. */
 int sr_step_logits(sr_model *m, const float **device_logits);
 
@@ -246,11 +256,21 @@ int sr_step_logits(sr_model *m, const float **device_logits);
  * history: per session the prompt+output ids (history_offsets[n+1]).
  * rng_state: per session, advanced exactly as RNG.Float64 does (one draw per
  * sampled, non-greedy token).  blocked: id never sampled (-1 for HF models).
- * Supports top_k in 1..256 or temperature 0; other settings return
- * SR_EUNSUPPORTED.  ids_out[i] receives the token; a nonfinite logit or empty
- * distribution returns SR_EINVAL naming the session. */
+ * Every setting Sampling.Validate accepts (:7264-7269) is supported: top_k 0
+ * (every candidate) and top_k above 256 sort the whole eligible vocabulary on
+ * the device (scratch of 24 bytes per vocabulary entry for up to 32 sessions,
+ * allocated on first use).  ids_out[i] receives the token; a nonfinite logit
+ * or empty distribution returns SR_EINVAL naming the session. */
 int sr_sample(sr_model *m, int32_t n_sessions, const sr_sampling *settings, const int32_t *history_offsets,
               const int32_t *history, uint64_t *rng_state, int32_t blocked, int32_t *ids_out);
+/* sampleWithBlocked(logits, history, s, rng, blocked) (:7320) over logits the
+ * caller passes: host fp32 [n_sessions x vocab] (vocab 1..262144), every
+ * session sampled, the rest as sr_sample.  The model's last-step logits are
+ * left as they were (the rows go to a separate device buffer, allocated on
+ * first use). */
+int sr_sample_logits(sr_model *m, int32_t n_sessions, int32_t vocab, const float *logits, const sr_sampling *settings,
+                     const int32_t *history_offsets, const int32_t *history, uint64_t *rng_state, int32_t blocked,
+                     int32_t *ids_out);
 
 /* Step + sample in one call (one host round trip per engine tick). */
 int sr_step_sample(sr_model *m, sr_kvpool *pool, const sr_batch *batch, const sr_sampling *settings,

@@ -31,7 +31,8 @@ EXPORTED = [
     "sr_step_noalloc", "sr_model_create_tp", "sr_tp_unique_id", "sr_tp_shard", "sr_engine_latency",
     "sr_kvpool_copy_rows", "sr_engine_clear_prefix", "sr_tp_peer_handle", "sr_tp_peer_open",
     "sr_text_decoder_create", "sr_text_decoder_destroy", "sr_text_decoder_push", "sr_text_decoder_push_token",
-    "sr_tp_peer_set_protocol", "sr_engine_set_pieces", "sr_engine_poll_token",
+    "sr_tp_peer_set_protocol", "sr_engine_set_pieces", "sr_engine_poll_token", "sr_sample_logits",
+    "sr_linear",
 ]
 PROF_CLASSES = ["meta", "embed", "norm", "linear", "rope_kv", "attention", "swiglu", "head", "sample"]
 
@@ -134,6 +135,8 @@ def lib():
         "sr_text_decoder_push": (C.c_int, [P, P, I64, I32, P, I64, C.POINTER(I64), C.POINTER(I64)]),
         "sr_text_decoder_push_token": (C.c_int, [P, I32, P, I64, I32, P, I64, C.POINTER(I64), C.POINTER(I64)]),
         "sr_sample": (C.c_int, [P, I32, P, P, P, P, I32, P]),
+        "sr_sample_logits": (C.c_int, [P, I32, I32, P, P, P, P, P, I32, P]),
+        "sr_linear": (C.c_int, [P, I32, I32, P, P]),
         "sr_step_sample": (C.c_int, [P, P, C.POINTER(Batch), P, P, P, P, I32, P]),
         "sr_engine_create": (C.c_int, [P, C.POINTER(EngineConfig), C.POINTER(P)]),
         "sr_engine_destroy": (C.c_int, [P]),

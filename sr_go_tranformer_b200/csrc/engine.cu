@@ -362,9 +362,19 @@ extern "C" int sr_engine_tick(sr_engine* e, int32_t* rows) {
       e->st.prefix_tokens += s.pos;
     }
     s.cursor = s.pos;  // engineSession.Cursor = cache.Pos
-    if (e->text_on)  // newTextDecoder (M:8363)
-      sr_text_decoder_create(e->text_flags, e->fallback.empty() ? nullptr : e->fallback.data(),
-                             (int32_t)e->fallback.size(), &s.text);
+    if (e->text_on) {  // newTextDecoder (M:8363)
+      rc = sr_text_decoder_create(e->text_flags, e->fallback.empty() ? nullptr : e->fallback.data(),
+                                  (int32_t)e->fallback.size(), &s.text);
+      if (rc != SR_OK) {  // the request fails as a whole, like a failed prefix restore
+        std::string msg = sr_last_error();
+        close_session(e, s);
+        e->st.failed++;
+        e->finished.push_back(Finished{s.req.id, {}, 2});
+        account(e);
+        sr_fail(rc, msg);
+        return rc;
+      }
+    }
     e->sessions.push_back(std::move(s));
     e->st.active++;
     account(e);
@@ -568,6 +578,8 @@ extern "C" int sr_engine_set_pieces(sr_engine* e, const uint8_t* pieces, const i
     e->fallback.clear();
     return SR_OK;
   }
+  if (vocab < e->m->dm.vocab)  // e.pieces[id] must exist for every id the sampler can return
+    return sr_fail(SR_EINVAL, "the pieces table must cover the model's vocabulary");
   if (offsets[0] != 0) return sr_fail(SR_EINVAL, "piece offsets must start at 0");
   for (int32_t i = 0; i < vocab; i++)
     if (offsets[i + 1] < offsets[i]) return sr_fail(SR_EINVAL, "piece offsets must not decrease");

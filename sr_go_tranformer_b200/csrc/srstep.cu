@@ -87,6 +87,8 @@ static void free_model(sr_model* m) {
   if (m->nccl_comm) nccl::api().CommDestroy((nccl::Comm)m->nccl_comm);
   for (void* p : m->allocs) cudaFree(p);
   if (m->h_stage) cudaFreeHost(m->h_stage);
+  if (m->samp_full) cudaFree(m->samp_full);
+  if (m->samp_logits) cudaFree(m->samp_logits);
   if (m->stream) cudaStreamDestroy(m->stream);
   for (auto& f : m->fast_free) f();
   delete m;
@@ -562,6 +564,7 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
   }
   cudaFuncSetAttribute(k_attention_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+  cudaFuncSetAttribute(k_sample_full, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
   if ((rc = fast_init(m)) != SR_OK) { free_model(m); return rc; }
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
@@ -1351,6 +1354,44 @@ extern "C" int sr_step(sr_model* m, sr_kvpool* pool, const sr_batch* batch, floa
   return tc_check(m);
 }
 
+// linearIntoWithExecutor (M:3942-3968) for one loaded matrix: Y = X W^T in
+// the model's mode (exact: the reference's reduction order).  Host buffers;
+// the device copies are allocated per call (a diagnostic path).
+extern "C" int sr_linear(sr_model* m, int32_t index, int32_t rows, const float* x, float* y) {
+  if (!m || !x || !y) return sr_fail(SR_EINVAL, "null argument");
+  if (index < 0 || index >= (int32_t)m->params.size()) return sr_fail(SR_EINVAL, "parameter index out of range");
+  const Param& W = m->params[index];
+  if (W.rows < 1 || W.cols < 1 || (W.format == kF32 && W.rows == 1))
+    return sr_fail(SR_EINVAL, "parameter is not a matrix");
+  if (rows < 1 || rows > kMaxRows) return sr_fail(SR_EINVAL, "rows must be 1..1024");
+  CK(cudaSetDevice(m->device));
+  const size_t xb = (size_t)rows * W.cols * 4, yb = (size_t)rows * W.rows * 4;
+  float *xd = nullptr, *yd = nullptr;
+  if (cudaMalloc((void**)&xd, xb) != cudaSuccess || cudaMalloc((void**)&yd, yb) != cudaSuccess) {
+    cudaGetLastError();
+    if (xd) cudaFree(xd);
+    return sr_fail(SR_ENOMEM, "linear buffers");
+  }
+  cudaError_t e = cudaMemcpyAsync(xd, x, xb, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) {
+    LinearOut o;
+    o.y = yd;
+    o.ldy = W.rows;
+    o.bias = nullptr;
+    o.resid = nullptr;
+    o.out_map = nullptr;
+    sr_launch_linear(m, xd, rows, W, o);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(y, yd, yb, cudaMemcpyDeviceToHost, m->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  cudaFree(xd);
+  cudaFree(yd);
+  if (e != cudaSuccess) return sr_fail(SR_EDEVICE, std::string("linear: ") + cudaGetErrorString(e));
+  sr_prof_resolve(m);
+  return SR_OK;
+}
+
 extern "C" int sr_step_logits(sr_model* m, const float** device_logits) {
   if (!m || !device_logits) return sr_fail(SR_EINVAL, "null argument");
   *device_logits = m->logits;
@@ -1358,26 +1399,50 @@ extern "C" int sr_step_logits(sr_model* m, const float** device_logits) {
 }
 
 // ------------------------------------------------------------------ sampler --
+// Grow-only device buffer owned by the model (freed with it).
+static int grow_buffer(sr_model* m, void** p, size_t* have, size_t need, const char* what) {
+  if (*have >= need) return SR_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *have = 0;
+  cudaError_t e = cudaMalloc(p, need);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *p = nullptr;
+    return sr_fail(SR_ENOMEM, std::string(what) + ": cudaMalloc(" + std::to_string(need) + ") failed");
+  }
+  *have = need;
+  return SR_OK;
+}
+
 int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const int32_t* history_offsets,
-                      const int32_t* history, const uint64_t* rng_state, int32_t blocked) {
-  if (n != m->last_sessions) return sr_fail(SR_EINVAL, "session count differs from the last step");
+                      const int32_t* history, const uint64_t* rng_state, int32_t blocked, const float* logits,
+                      int32_t V, bool all) {
+  if (!all && n != m->last_sessions) return sr_fail(SR_EINVAL, "session count differs from the last step");
+  if (n < 1 || n > kMaxSessions) return sr_fail(SR_EINVAL, "sampling needs 1..256 sessions");
   if (!settings || !history_offsets || !rng_state) return sr_fail(SR_EINVAL, "null argument");
   if (history_offsets[0] != 0) return sr_fail(SR_EINVAL, "history offsets must start at 0");
   const int64_t nh = history_offsets[n];
   if (nh < 0 || nh > kSampleHistCap) return sr_fail(SR_EINVAL, "history exceeds the device staging capacity");
   if (nh > 0 && !history) return sr_fail(SR_EINVAL, "null history");
+  int32_t* list = (int32_t*)((uint8_t*)m->h_stage + m->upload_ints * 4 + kSampOffList);
+  int n_full = 0;
   for (int i = 0; i < n; i++) {
     if (history_offsets[i + 1] < history_offsets[i]) return sr_fail(SR_EINVAL, "history offsets must be nondecreasing");
-    if (!m->last_want[i]) continue;
+    if (!all && !m->last_want[i]) continue;
     const sr_sampling& s = settings[i];
     if (!std::isfinite(s.temperature) || s.temperature < 0 || s.temperature > 100 || !std::isfinite(s.top_p) ||
         s.top_p <= 0 || s.top_p > 1 || !std::isfinite(s.repeat_penalty) || s.repeat_penalty < 1 ||
         s.repeat_penalty > 100 || s.top_k < 0)
       return sr_fail(SR_EINVAL, "invalid sampling settings");  // Sampling.Validate (M:7264-7269)
-    if (s.temperature != 0 && (s.top_k < 1 || s.top_k > kMaxTopK))
-      return sr_fail(SR_EUNSUPPORTED, "device sampler supports top_k 1..256 when temperature > 0");
+    if (s.temperature != 0 && (s.top_k == 0 || s.top_k > kMaxTopK)) list[n_full++] = i;
   }
-  // Staging: settings | hist_off | hist | rng
+  if (n_full) {
+    const size_t need = (size_t)std::min(n_full, kSampleWave) * (size_t)sample_full_stride(V);
+    int rc = grow_buffer(m, (void**)&m->samp_full, &m->samp_full_bytes, need, "full-vocabulary sampler scratch");
+    if (rc != SR_OK) return rc;
+  }
+  // Staging: settings | hist_off | hist | rng | ids | status | list
   uint8_t* h = (uint8_t*)m->h_stage + m->upload_ints * 4;
   SampleSetting* hs = (SampleSetting*)h;
   for (int i = 0; i < n; i++) {
@@ -1397,22 +1462,35 @@ int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const
   CK(cudaMemcpyAsync(dv + off_hoff, h + off_hoff, (size_t)(n + 1) * 4, cudaMemcpyHostToDevice, m->stream));
   if (nh) CK(cudaMemcpyAsync(dv + off_hist, h + off_hist, (size_t)nh * 4, cudaMemcpyHostToDevice, m->stream));
   CK(cudaMemcpyAsync(dv + off_rng, h + off_rng, (size_t)n * 8, cudaMemcpyHostToDevice, m->stream));
+  if (n_full)
+    CK(cudaMemcpyAsync(dv + kSampOffList, h + kSampOffList, (size_t)n_full * 4, cudaMemcpyHostToDevice, m->stream));
   SampleArgs a;
-  a.logits = m->logits;
-  a.V = m->dm.vocab;
+  a.logits = logits;
+  a.V = V;
   a.n = n;
   a.blocked = blocked;
-  a.want = m->meta.want;
+  a.want = all ? nullptr : m->meta.want;
   a.settings = (const SampleSetting*)dv;
   a.hist_off = (const int32_t*)(dv + off_hoff);
   a.hist = (const int32_t*)(dv + off_hist);
   a.rng = (uint64_t*)(dv + off_rng);
   a.ids = (int32_t*)(dv + off_ids);
   a.status = (int32_t*)(dv + off_status);
-  size_t smem = (size_t)((m->dm.vocab + 31) / 32) * 4;
+  size_t smem = (size_t)((V + 31) / 32) * 4;
   SR_LAUNCH(m, SR_PROF_SAMPLE, k_sample<<<n, kSampleThreads, smem, m->stream>>>(a));
   sr_count_launch(m);
   CK(cudaGetLastError());
+  if (n_full) {
+    const size_t fsmem = (((size_t)(V + 31) / 32) * 4 + 15) / 16 * 16 + (size_t)kSampleFullStage * 8;
+    for (int w0 = 0; w0 < n_full; w0 += kSampleWave) {
+      const int wn = std::min(kSampleWave, n_full - w0);
+      SR_LAUNCH(m, SR_PROF_SAMPLE,
+                k_sample_full<<<wn, kSampleFullThreads, fsmem, m->stream>>>(
+                    a, (const int32_t*)(dv + kSampOffList) + w0, m->samp_full));
+      sr_count_launch(m);
+      CK(cudaGetLastError());
+    }
+  }
   sr_prof_span_end(m);
   // results: rng | ids | status are contiguous -> one copy back
   CK(cudaMemcpyAsync(h + off_rng, dv + off_rng, off_status + (size_t)kMaxSessions * 4 - off_rng, cudaMemcpyDeviceToHost,
@@ -1420,7 +1498,7 @@ int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const
   return SR_OK;
 }
 
-int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_out) {
+int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_out, bool all) {
   CK(cudaStreamSynchronize(m->stream));
   sr_prof_resolve(m);
   if (int rc = fast_check(m)) return rc;
@@ -1432,7 +1510,7 @@ int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_o
   const int32_t* status = (const int32_t*)(h + off_status);
   memcpy(ids_out, ids, (size_t)n * 4);
   for (int i = 0; i < n; i++) {
-    if (!m->last_want[i]) continue;
+    if (!all && !m->last_want[i]) continue;
     if (status[i] == 1) return sr_fail(SR_EINVAL, "nonfinite sampling logit (session " + std::to_string(i) + ")");
     if (status[i] == 2) return sr_fail(SR_EINVAL, "empty sampling distribution (session " + std::to_string(i) + ")");
     if (status[i] == 3) return sr_fail(SR_EUNSUPPORTED, "unsupported sampling settings (session " + std::to_string(i) + ")");
@@ -1446,9 +1524,33 @@ extern "C" int sr_sample(sr_model* m, int32_t n_sessions, const sr_sampling* set
   if (!m || !ids_out || !rng_state) return sr_fail(SR_EINVAL, "null argument");
   CK(cudaSetDevice(m->device));
   sr_prof_span_begin(m);
-  int rc = sr_sample_enqueue(m, n_sessions, settings, history_offsets, history, rng_state, blocked);
+  int rc = sr_sample_enqueue(m, n_sessions, settings, history_offsets, history, rng_state, blocked, m->logits,
+                             m->dm.vocab, false);
   if (rc != SR_OK) return rc;
-  return sr_sample_finish(m, n_sessions, rng_state, ids_out);
+  return sr_sample_finish(m, n_sessions, rng_state, ids_out, false);
+}
+
+extern "C" int sr_sample_logits(sr_model* m, int32_t n_sessions, int32_t vocab, const float* logits,
+                                const sr_sampling* settings, const int32_t* history_offsets, const int32_t* history,
+                                uint64_t* rng_state, int32_t blocked, int32_t* ids_out) {
+  if (!m || !logits || !ids_out || !rng_state) return sr_fail(SR_EINVAL, "null argument");
+  if (vocab < 1 || vocab > 262144) return sr_fail(SR_EINVAL, "empty sampling distribution or vocabulary above 262144");
+  if (n_sessions < 1 || n_sessions > kMaxSessions) return sr_fail(SR_EINVAL, "sampling needs 1..256 sessions");
+  CK(cudaSetDevice(m->device));
+  const size_t bytes = (size_t)n_sessions * vocab * 4;
+  int rc = grow_buffer(m, (void**)&m->samp_logits, &m->samp_logits_bytes, bytes, "sampling logits buffer");
+  if (rc != SR_OK) return rc;
+  CK(cudaMemcpyAsync(m->samp_logits, logits, bytes, cudaMemcpyHostToDevice, m->stream));
+  sr_prof_span_begin(m);
+  rc = sr_sample_enqueue(m, n_sessions, settings, history_offsets, history, rng_state, blocked, m->samp_logits, vocab,
+                         true);
+  if (rc != SR_OK) {
+    sr_prof_span_end(m);
+    cudaStreamSynchronize(m->stream);
+    sr_prof_resolve(m);
+    return rc;
+  }
+  return sr_sample_finish(m, n_sessions, rng_state, ids_out, true);
 }
 
 extern "C" int sr_step_sample(sr_model* m, sr_kvpool* pool, const sr_batch* batch, const sr_sampling* settings,
@@ -1462,13 +1564,14 @@ extern "C" int sr_step_sample(sr_model* m, sr_kvpool* pool, const sr_batch* batc
   CK(cudaSetDevice(m->device));
   if ((rc = sr_upload_batch(m, batch, info)) != SR_OK) return rc;
   if ((rc = sr_step_enqueue(m, pool, info, nullptr)) != SR_OK) return rc;
-  if ((rc = sr_sample_enqueue(m, batch->n_sessions, settings, history_offsets, history, rng_state, blocked)) != SR_OK) {
+  if ((rc = sr_sample_enqueue(m, batch->n_sessions, settings, history_offsets, history, rng_state, blocked, m->logits,
+                              m->dm.vocab, false)) != SR_OK) {
     sr_prof_span_end(m);
     cudaStreamSynchronize(m->stream);
     sr_prof_resolve(m);
     return rc;
   }
-  return sr_sample_finish(m, batch->n_sessions, rng_state, ids_out);
+  return sr_sample_finish(m, batch->n_sessions, rng_state, ids_out, false);
 }
 
 // Fast-mode attention: split-K kernels when the shape is covered (returns true

@@ -29,7 +29,8 @@ constexpr size_t kSampOffHist = sr_align16(kSampOffHistOff + 257 * 4);
 constexpr size_t kSampOffRng = sr_align16(kSampOffHist + (size_t)kSampleHistCap * 4);
 constexpr size_t kSampOffIds = sr_align16(kSampOffRng + 256 * 8);
 constexpr size_t kSampOffStatus = sr_align16(kSampOffIds + 256 * 4);
-constexpr size_t kSampleStageBytes = sr_align16(kSampOffStatus + 256 * 4);
+constexpr size_t kSampOffList = sr_align16(kSampOffStatus + 256 * 4);  // sessions of the full-vocabulary path
+constexpr size_t kSampleStageBytes = sr_align16(kSampOffList + 256 * 4);
 static_assert(kSampOffRng % 16 == 0, "RNG states must be 8-byte aligned");
 
 struct BatchInfo {
@@ -81,6 +82,12 @@ struct sr_model {
   int64_t max_pages_per_session = 0, page_cap = 0, upload_ints = 0;
   void* h_stage = nullptr;
   void* samp_dev = nullptr;
+  // k_sample_full scratch (kSampleWave sessions x sample_full_stride(V)) and the
+  // logits buffer of sr_sample_logits; both allocated on first use, grow-only
+  uint8_t* samp_full = nullptr;
+  size_t samp_full_bytes = 0;
+  float* samp_logits = nullptr;
+  size_t samp_logits_bytes = 0;
   cudaStream_t stream = nullptr;
   int last_sessions = 0;
   std::vector<uint8_t> last_want;
@@ -154,6 +161,9 @@ struct StepScratch {
 };
 int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel,
                     const StepScratch* scratch = nullptr);
+// Samples sessions 0..n-1 of logits [n x V] (device): the last step's rows
+// (all == false: only the sessions the step selected) or every row (all).
 int sr_sample_enqueue(sr_model* m, int32_t n, const sr_sampling* settings, const int32_t* history_offsets,
-                      const int32_t* history, const uint64_t* rng_state, int32_t blocked);
-int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_out);
+                      const int32_t* history, const uint64_t* rng_state, int32_t blocked, const float* logits,
+                      int32_t V, bool all);
+int sr_sample_finish(sr_model* m, int32_t n, uint64_t* rng_state, int32_t* ids_out, bool all);

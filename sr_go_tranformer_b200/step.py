@@ -176,6 +176,17 @@ class Model:
         A.check(A.lib().sr_model_read_param(self.h, i, _p(vals), vals.nbytes, _p(sc), sc.size))
         return vals, sc
 
+    def linear(self, index, x):
+        """y = x W^T for matrix parameter `index` in the model's mode
+        (linearIntoWithExecutor, M:3942); x [rows, in] -> y [rows, out]."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        info = self.param_info(index)
+        if x.ndim != 2 or x.shape[1] != info.cols:
+            raise A.SRError(A.SR_EINVAL, "x must be [rows, in]")
+        y = np.zeros((x.shape[0], info.rows), dtype=np.float32)
+        A.check(A.lib().sr_linear(self.h, index, x.shape[0], _p(x), _p(y)))
+        return y
+
     def init_synthetic(self, seed, scale=0.02):
         A.check(A.lib().sr_model_init_synthetic(self.h, seed, scale))
 
@@ -253,9 +264,8 @@ class Model:
     def step(self, cache, token):
         return self.decode_batch([cache], [token])[0]
 
-    def sample(self, settings, histories, rng_states, blocked=-1):
-        """Device sampleWithBlocked over the last step's selected rows.
-        settings: list of (temperature, top_k, top_p, penalty); returns ids, rng."""
+    @staticmethod
+    def _sample_args(settings, histories, rng_states):
         S = len(settings)
         arr = (A.Sampling * S)()
         for i, (t, k, p, pen) in enumerate(settings):
@@ -265,7 +275,24 @@ class Model:
         hist = np.concatenate([np.asarray(h, dtype=np.int32) for h in histories] + [np.zeros(1, np.int32)])
         rng = np.asarray(rng_states, dtype=np.uint64).copy()
         ids = np.full(S, -1, dtype=np.int32)
+        return S, arr, hoff, hist, rng, ids
+
+    def sample(self, settings, histories, rng_states, blocked=-1):
+        """Device sampleWithBlocked over the last step's selected rows.
+        settings: list of (temperature, top_k, top_p, penalty); returns ids, rng."""
+        S, arr, hoff, hist, rng, ids = self._sample_args(settings, histories, rng_states)
         A.check(A.lib().sr_sample(self.h, S, C.cast(arr, C.c_void_p), _p(hoff), _p(hist), _p(rng), blocked, _p(ids)))
+        return ids, rng
+
+    def sample_logits(self, logits, settings, histories, rng_states, blocked=-1):
+        """Device sampleWithBlocked(logits, history, s, rng, blocked) over the
+        caller's logits [sessions, vocab] (M:7320); returns ids, rng."""
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        S, arr, hoff, hist, rng, ids = self._sample_args(settings, histories, rng_states)
+        if lg.ndim != 2 or lg.shape[0] != S:
+            raise A.SRError(A.SR_EINVAL, "logits must be [sessions, vocab]")
+        A.check(A.lib().sr_sample_logits(self.h, S, lg.shape[1], _p(lg), C.cast(arr, C.c_void_p), _p(hoff),
+                                          _p(hist), _p(rng), blocked, _p(ids)))
         return ids, rng
 
 

@@ -6,10 +6,6 @@ the first 35 ids in chunks of 1/4/16/35, decode ids 35 and 36; logits and every
 K/V row bit-exact with the oracle, logits within 2e-5 of Transformers.  Also the
 quantized storages against the quantized oracle, and the checkpoint path
 through hf.py.
-
-The GPT-2 device step has not yet run on a GPU, so these tests run only when
-SR_GPU_GPT2=1; they stay out of the default GPU suite until they have passed
-there once.
 """
 
 import glob
@@ -21,9 +17,7 @@ import pytest
 from conftest import GOLDEN_DIR
 from test_gpu_step import assert_same, compare_cache_rows
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("SR_GPU_GPT2") != "1",
-                                 reason="GPT-2 device step not yet validated on a GPU (set SR_GPU_GPT2=1)")]
+pytestmark = pytest.mark.gpu
 
 GPT2 = sorted(glob.glob(os.path.join(GOLDEN_DIR, "gpt2", "*.npz")))
 

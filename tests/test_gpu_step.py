@@ -417,8 +417,6 @@ def test_engine_prefix_config_errors(oracle, srlib):
     e.close()
 
 
-@pytest.mark.skipif(__import__("os").environ.get("SR_GPU_ENGINE_TEXT") != "1",
-                    reason="engine token events have not yet run on a GPU (set SR_GPU_ENGINE_TEXT=1)")
 def test_engine_token_events(oracle, srlib):
     """TokenEvent (M:8451-8462): one event per sampled token, in order, whose
     texts concatenate to the decoder's text of the request's pieces; the last
