@@ -8,6 +8,7 @@
 #include "common.cuh"
 #include "exact_kernels.cuh"
 #include "fast_attention.cuh"
+#include "gemv.cuh"
 #include "srstep_internal.h"
 #include "tp_peer.cuh"
 
@@ -17,6 +18,10 @@ struct FastState {
   float* part_o = nullptr;
   float* part_ml = nullptr;
   size_t items_cap = 0;
+  float* gv_part = nullptr;  // decode GEMV split-K partials (grow-only)
+  size_t gv_part_floats = 0;
+  int* gv_count = nullptr;   // decode GEMV row-group counters (zeroed, reset by the kernel)
+  size_t gv_count_cap = 0;
   int* err = nullptr;    // device flag raised by an expired bounded wait
   int* h_err = nullptr;  // pinned host copy
   bool ran = false;      // a kernel that can raise the flag ran since the last check
@@ -30,6 +35,8 @@ inline int fast_init(sr_model* m) {
   m->fast_free.push_back([st]() {
     if (st->part_o) cudaFree(st->part_o);
     if (st->part_ml) cudaFree(st->part_ml);
+    if (st->gv_part) cudaFree(st->gv_part);
+    if (st->gv_count) cudaFree(st->gv_count);
     if (st->err) cudaFree(st->err);
     if (st->h_err) cudaFreeHost(st->h_err);
     delete st;
@@ -267,5 +274,107 @@ inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, const
 // ------------------------------------------------------------------- linear --
 // Returns true when a fast projection kernel handled the call.
 bool fast_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O);
+
+// ------------------------------------------------------------- decode GEMV --
+// Whether the decode GEMV covers matrix W for n step rows: Q8 rows of a
+// multiple of 16 columns, Q4 of 32 (16-byte aligned rows of codes).
+inline bool gemv_covers(const Param& W, int n) {
+  if (n < 1 || n > gv::kMaxRows) return false;
+  if (W.format == kQ8) return W.cols % 16 == 0;
+  if (W.format == kQ4) return W.cols % 32 == 0;
+  return false;
+}
+
+template <int NR>
+inline void gemv_launch(const gv::Args& a, dim3 grid, cudaStream_t s) {
+  if (a.fmt == kQ8) gv::k_gemv<kQ8, NR><<<grid, gv::kThreads, 0, s>>>(a);
+  else gv::k_gemv<kQ4, NR><<<grid, gv::kThreads, 0, s>>>(a);
+}
+
+// Y = X W^T for up to 3 matrices sharing X (same format and width), each with
+// its own output.  Returns false when the shapes are not covered or scratch
+// cannot be allocated (the caller then runs the exact kernels).
+inline bool gemv_run(sr_model* m, const float* X, int n, const Param* const* W, const LinearOut* O, int nseg) {
+  if (nseg < 1 || nseg > gv::kMaxSeg) return false;
+  for (int i = 0; i < nseg; i++)
+    if (!gemv_covers(*W[i], n) || W[i]->format != W[0]->format || W[i]->cols != W[0]->cols ||
+        (O[i].out_map != O[0].out_map))
+      return false;
+  FastState* st = fast_state(m);
+  const int nr = n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8;
+  gv::Args a;
+  a.x = X;
+  a.n = n;
+  a.in = W[0]->cols;
+  a.fmt = W[0]->format;
+  a.groups = (a.in + kQBlock - 1) / kQBlock;
+  a.rb = a.fmt == kQ8 ? a.in : (a.in + 1) / 2;
+  a.nseg = nseg;
+  a.out_map = O[0].out_map;
+  int tiles = 0;
+  const int rpc = gv::rows_per_cta(nr);
+  for (int i = 0; i < nseg; i++) {
+    gv::Seg& g = a.seg[i];
+    g.rows = W[i]->rows;
+    g.tiles = (g.rows + rpc - 1) / rpc;
+    g.w = (const uint8_t*)W[i]->values;
+    g.scales = W[i]->scales;
+    g.y = O[i].y;
+    g.ldy = O[i].ldy;
+    g.bias = O[i].bias;
+    g.resid = O[i].resid;
+    tiles += g.tiles;
+  }
+  for (int i = nseg; i < gv::kMaxSeg; i++) a.seg[i] = a.seg[0];
+  a.total_tiles = tiles;
+  // K splits: at least enough that a CTA's columns fit its staged chunk, more
+  // (down to one warp span each) until the launch has about 4 CTAs per SM.
+  const int chunk = gv::chunk_for(nr), span = gv::span_for(a.fmt);
+  const int min_split = (a.in + chunk - 1) / chunk, max_split = std::max(min_split, (a.in + span - 1) / span);
+  const int ksplit = std::max(min_split, std::min(max_split, (148 * 4 + tiles - 1) / tiles));
+  a.kper = ((a.in + ksplit - 1) / ksplit + span - 1) / span * span;
+  a.ksplit = (a.in + a.kper - 1) / a.kper;
+  a.part = nullptr;
+  a.counters = nullptr;
+  if (a.ksplit > 1) {
+    const size_t need = (size_t)a.ksplit * tiles * rpc * nr;
+    if (need > st->gv_part_floats) {
+      if (st->gv_part) cudaFree(st->gv_part);
+      st->gv_part = nullptr;
+      st->gv_part_floats = 0;
+      const size_t cap = std::max(need, (size_t)1 << 20);
+      if (cudaMalloc((void**)&st->gv_part, cap * 4) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+      }
+      st->gv_part_floats = cap;
+    }
+    if ((size_t)tiles > st->gv_count_cap) {
+      if (st->gv_count) cudaFree(st->gv_count);
+      st->gv_count = nullptr;
+      st->gv_count_cap = 0;
+      const size_t cap = std::max((size_t)tiles, (size_t)4096);
+      if (cudaMalloc((void**)&st->gv_count, cap * 4) != cudaSuccess ||
+          cudaMemsetAsync(st->gv_count, 0, cap * 4, m->stream) != cudaSuccess) {
+        cudaGetLastError();
+        if (st->gv_count) cudaFree(st->gv_count);
+        st->gv_count = nullptr;
+        return false;
+      }
+      st->gv_count_cap = cap;
+    }
+    a.part = st->gv_part;
+    a.counters = st->gv_count;
+  }
+  const dim3 grid(tiles, a.ksplit);
+  switch (nr) {
+    case 1: gemv_launch<1>(a, grid, m->stream); break;
+    case 2: gemv_launch<2>(a, grid, m->stream); break;
+    case 4: gemv_launch<4>(a, grid, m->stream); break;
+    default: gemv_launch<8>(a, grid, m->stream); break;
+  }
+  sr_count_launch(m);
+  return true;
+}
 
 }  // namespace sr

@@ -1248,6 +1248,14 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     bool done;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_qkv(m, l, n, true));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
+    if (!done && fast) {  // decode GEMV: Q|K|V in one launch
+      const Param* w3[3] = {&P[1], &P[2], &P[3]};
+      LinearOut o3[3] = {o, o, o};
+      o3[0].y = m->Q; o3[0].ldy = dm.qd; o3[0].bias = B ? (const float*)B[0].values : nullptr;
+      o3[1].y = m->K; o3[1].ldy = kd; o3[1].bias = B ? (const float*)B[1].values : nullptr;
+      o3[2].y = m->V; o3[2].ldy = kd; o3[2].bias = B ? (const float*)B[2].values : nullptr;
+      SR_LAUNCH(m, SR_PROF_LINEAR, done = gemv_run(m, m->N, n, w3, o3, 3));
+    }
     if (!done) {
       o.y = m->Q; o.ldy = dm.qd; o.bias = B ? (const float*)B[0].values : nullptr;
       sr_launch_linear(m, m->N, n, P[1], o);
@@ -1284,6 +1292,13 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     o.resid = nullptr;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_gateup(m, l, n, true));
     if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
+    if (!done && fast) {  // decode GEMV: gate|up in one launch
+      const Param* w2[2] = {&P[6], &P[7]};
+      LinearOut o2[2] = {o, o};
+      o2[0].y = m->G; o2[0].ldy = dm.hidden; o2[0].bias = nullptr;
+      o2[1].y = m->U; o2[1].ldy = dm.hidden; o2[1].bias = nullptr;
+      SR_LAUNCH(m, SR_PROF_LINEAR, done = gemv_run(m, m->N, n, w2, o2, 2));
+    }
     if (!done) {
       o.y = m->G; o.ldy = dm.hidden;
       sr_launch_linear(m, m->N, n, P[6], o);
@@ -1584,11 +1599,12 @@ static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, const BatchInfo&
   return false;
 }
 
-// Per-call fast projection hook.  The step's fast projections go through the
-// tensor-core path (fast_gemm.cuh) directly; other callers use the exact kernels.
+// Per-call fast projection hook: the decode GEMV for steps of a few rows
+// (gemv.cuh); larger steps go through the tensor-core path (fast_gemm.cuh)
+// directly, and shapes neither covers run the exact kernels.
 bool sr::fast_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O) {
-  (void)m, (void)X, (void)n, (void)W, (void)O;
-  return false;
+  const Param* w = &W;
+  return gemv_run(m, X, n, &w, &O, 1);
 }
 
 // ---------------------------------------------------------------- profiling --

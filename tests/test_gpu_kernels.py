@@ -167,3 +167,46 @@ def test_linear_tails_rows_exact(oracle, srlib, fmt, cols):
         want = oracle.linear(x, f, vals, sc if sc is not None else np.zeros(1, np.float32), 64, cols)
         bits_equal(got, want.reshape(got.shape), f"{fmt} cols {cols} rows {rows}")
     dm.close()
+
+
+def dequant(vals, sc, fmt, rows, cols):
+    """Dense fp64 weights from Q8 / Q4 storage (copyRow, M:3900-3921)."""
+    g = (cols + 63) // 64
+    if fmt == "q8":
+        q = vals.view(np.int8).reshape(rows, cols).astype(np.float64)
+    else:
+        b = vals.view(np.uint8).reshape(rows, (cols + 1) // 2).astype(np.int64)
+        nib = np.zeros((rows, 2 * b.shape[1]), dtype=np.int64)
+        nib[:, 0::2], nib[:, 1::2] = b & 15, b >> 4
+        q = np.where(nib >= 8, nib - 16, nib)[:, :cols].astype(np.float64)
+    s = np.repeat(sc.reshape(rows, g).astype(np.float64), 64, axis=1)[:, :cols]
+    return q * s
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+@pytest.mark.parametrize("cols", [64, 576, 4096, 14336])
+def test_fast_decode_gemv(oracle, srlib, fmt, cols):
+    """SR_MODE_FAST projections of 1..8 rows run the decode GEMV (128-bit code
+    loads, dequantisation in registers): down_proj [64, cols] splits K over
+    CTAs (the split-K reduction), gate [cols, 64] and the embedding as a head
+    [256, 64] do not.  Each output must be within 1e-5 of sum_j |x_j w_j| of
+    the exact-order oracle result (fast mode reorders the fp32 sums)."""
+    dm = model(hidden=cols, fmt=fmt)
+    rng = np.random.default_rng(cols + (fmt == "q4"))
+    for index, (rows_w, cols_w) in ((DOWN, (64, cols)), (7, (cols, 64)), (EMB, (256, 64))):
+        w = (rng.standard_normal((rows_w, cols_w)) * 0.05).astype(np.float32)
+        vals, sc = oracle.quantize(w, Q8 if fmt == "q8" else Q4)
+        dm.load_param(index, vals, sc)
+        wd = np.abs(dequant(vals, sc, fmt, rows_w, cols_w))
+        for n in range(1, 9):
+            x = rng.standard_normal((n, cols_w)).astype(np.float32)
+            dm.set_mode("exact")
+            exact = dm.linear(index, x)
+            dm.set_mode("fast")
+            got = dm.linear(index, x)
+            want = oracle.linear(x, Q8 if fmt == "q8" else Q4, vals, sc, rows_w, cols_w).reshape(got.shape)
+            bits_equal(exact, want, f"exact {fmt} param {index} rows {n}")
+            bound = np.abs(x).astype(np.float64) @ wd.T
+            err = np.abs(got.astype(np.float64) - want) / np.maximum(bound, 1e-30)
+            assert err.max() <= 1e-5, (fmt, cols, index, n, float(err.max()))
+    dm.close()
