@@ -194,6 +194,18 @@ int sr_model_read_param(const sr_model *m, int32_t index, void *values, size_t v
 int sr_model_init_synthetic(sr_model *m, uint64_t seed, double scale);
 /* Select SR_MODE_EXACT (default) or SR_MODE_FAST for subsequent steps. */
 int sr_model_set_mode(sr_model *m, int32_t mode);
+/* Fast-mode code cache (no counterpart in the reference, which reads the
+ * codes as stored).  enabled = 1 (the default): the tensor-core projections
+ * also keep every Q8/Q4 matrix's codes as bf16 in tile order, 2 bytes per
+ * weight (about 1.9x the Q8 payload, 3.8x Q4), built on the first fast step
+ * of 32+ rows; each weight tile is then one bulk copy.  enabled = 0, or when
+ * the copy does not fit in device memory: the projections read the reference
+ * codes as stored and widen them to bf16 in shared memory, which uses no
+ * extra device memory but more shared-memory bandwidth (slower).  Results are
+ * identical either way.  sr_model_code_cache reports whether the cache is in
+ * use (building it if enabled). */
+int sr_model_set_code_cache(sr_model *m, int32_t enabled);
+int sr_model_code_cache(sr_model *m, int32_t *cached);
 
 /* ---------------------------------------------------------------- KV pool */
 /* Device page pool holding num_pages pages of 2*page_tokens*kvDim*layers fp32

@@ -1,6 +1,7 @@
 // common.cuh -- shared definitions for the sm_100a engine-step kernels.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -12,6 +13,10 @@ constexpr int kMaxSessions = 256;    // sessions per step (monolith.go:6248)
 constexpr int kAttnSplit = 512;      // positions per split-K attention item (fast mode)
 
 enum ParamFormat { kF32 = 0, kQ8 = 1, kQ4 = 2 };
+
+// Element of the fast path's tensor-core operand planes: an fp32 activation is
+// carried as two bf16 terms (hi + lo), and Q8/Q4 codes widen to bf16 exactly.
+typedef __nv_bfloat16 op16;
 
 // float32(MaxFloat32 / (2*64*127)): rows with a larger |x| take the fp64 path
 // (q8NeedsWideSum, monolith.go:4346-4354).

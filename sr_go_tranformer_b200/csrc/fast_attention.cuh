@@ -20,6 +20,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <float.h>
 
 #include "common.cuh"
@@ -40,13 +41,14 @@ struct FastAttnArgs {
   float scale;
   float* part_o;   // [items][kv_heads][group][hd]
   float* part_ml;  // [items][kv_heads][group][2]
-  __nv_bfloat16* xh;  // optional: write the output as bf16 hi/lo planes (the
-  __nv_bfloat16* xl;  // next projection's tensor-core operand) instead of fp32 A
+  op16* xh;  // optional: write the output as bf16 hi/lo planes (the next
+  op16* xl;  // projection's tensor-core operand) instead of fp32 A
   int* err;           // raised when a bounded wait for a tile expires
 };
 
-// x ~= hi + lo with |x - hi - lo| <= 2^-17 |x| (two bf16 terms).
-__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+// One fp32 activation as the projection's two bf16 operand terms:
+// x ~= hi + lo with |x - hi - lo| <= 2^-17 |x|.
+__device__ __forceinline__ void split_op(float x, op16* hi, op16* lo) {
   const __nv_bfloat16 h = __float2bfloat16_rn(x);
   *hi = h;
   *lo = __float2bfloat16_rn(x - __bfloat162float(h));
@@ -885,7 +887,7 @@ __global__ void __launch_bounds__(HD) k_attn_combine(FastAttnArgs a) {
   }
   const int64_t o = (int64_t)r * a.dm.qd + (int64_t)h * HD + d;
   if (a.xh)
-    split_bf16(num / den, a.xh + o, a.xl + o);
+    split_op(num / den, a.xh + o, a.xl + o);
   else
     a.A[o] = num / den;
 }

@@ -1,6 +1,14 @@
-// fast_gemm.cuh -- host side of the tensor-core projections (tc_gemm.cuh):
-// bf16 code shadows of every Q8/Q4 matrix (Q|K|V and gate|up fused row-wise),
-// TMA descriptors, the stream-K schedule and the per-layer entry points.
+// fast_gemm.cuh -- host side of the tensor-core projections (tc_gemm.cuh,
+// tc_gemm_direct.cuh): the bf16 code cache of every Q8/Q4 matrix (Q|K|V and
+// gate|up fused row-wise), TMA descriptors, the stream-K schedule and the
+// per-layer entry points.
+//
+// Code cache (the default): each matrix's codes are also kept as bf16 in tile
+// order, 2 bytes per weight (about 1.9x the Q8 payload, 3.8x Q4), so every A
+// tile is one bulk copy (k_gemm_q).  Without it (sr_model_set_code_cache(m, 0),
+// or when the copy does not fit in device memory) k_gemm_direct reads the
+// reference codes through per-parameter TMA maps and widens them in shared
+// memory: no extra device memory, more shared-memory traffic, slower.
 #pragma once
 
 #include <cuda.h>
@@ -11,19 +19,25 @@
 #include "fast_kernels.cuh"
 #include "srstep_internal.h"
 #include "tc_gemm.cuh"
+#include "tc_gemm_direct.cuh"
 
 namespace sr {
 
 struct TcMatrix {
-  uint8_t* wt = nullptr;  // bf16 codes in 32 KiB swizzled (256-feature, 64-column) tiles
+  uint8_t* wt = nullptr;  // bf16 code cache in 32 KiB swizzled (256-feature, 64-column) tiles, or null
   float* scales = nullptr;
   bool own_scales = false;
   int rows = 0, cols = 0;
+  // the reference codes, for k_gemm_direct: up to 3 row-stacked parameters
+  int nseg = 0, fmt = kQ8;
+  CUtensorMap map[3];
 };
 
 struct TcState {
   uint64_t version = ~0ull;
   bool disabled = false;
+  bool cache_wanted = true;  // build the bf16 code cache when it fits
+  bool cached = false;       // the matrices below carry it
   std::vector<TcMatrix> qkv, o, gateup, down;
   TcMatrix head;
   __nv_bfloat16* xh = nullptr;
@@ -67,6 +81,22 @@ inline bool make_map(CUtensorMap* map, void* base, uint64_t cols, uint64_t rows,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The codes of a Q8 / Q4 parameter as stored: uint8 [rows][row bytes], box of
+// 64 rows x one 64-column block's bytes (64 for Q8, 32 packed for Q4), no
+// swizzle; rows past the end read as zero.
+inline bool make_code_map(CUtensorMap* map, const Param& p) {
+  EncodeTiledFn fn = encode_fn();
+  const uint64_t rb = p.format == kQ8 ? (uint64_t)p.cols : (uint64_t)(p.cols + 1) / 2;
+  if (!fn || rb % 16 != 0 || ((uintptr_t)p.values) % 16 != 0) return false;
+  cuuint64_t dims[2] = {rb, (cuuint64_t)p.rows};
+  cuuint64_t strides[1] = {rb};
+  cuuint32_t box[2] = {(cuuint32_t)(p.format == kQ8 ? tc::kKB : tc::kKB / 2), (cuuint32_t)tc::kDirSub};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p.values, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 inline TcState* tc_state(sr_model* m) { return (TcState*)m->tc; }
 
 inline void tc_free(TcState* t) {
@@ -90,21 +120,28 @@ inline bool tc_alloc(TcState* t, void** p, size_t bytes) {
   return true;
 }
 
-// Build one (optionally row-fused) code shadow from parameters.
-inline bool tc_build(sr_model* m, TcState* t, TcMatrix& dst, const std::vector<const Param*>& parts) {
+// One (optionally row-fused) matrix over parameters sharing the input: the
+// concatenated block scales, the code maps (k_gemm_direct: same format and
+// width, every segment but the last a multiple of 64 rows) and, with cache,
+// the bf16 code cache (k_gemm_q).  A false return with dst.wt == nullptr and
+// cache set means only the cache did not fit.
+inline bool tc_build(sr_model* m, TcState* t, TcMatrix& dst, const std::vector<const Param*>& parts, bool cache) {
   int rows = 0;
   const int cols = parts[0]->cols;
-  for (const Param* p : parts) {
-    if (p->format == kF32 || p->cols != cols) return false;
+  dst.nseg = (int)parts.size();
+  dst.fmt = parts[0]->format;
+  for (size_t i = 0; i < parts.size(); i++) {
+    const Param* p = parts[i];
+    if (p->format == kF32 || p->cols != cols || p->format != dst.fmt) return false;
+    if (i + 1 < parts.size() && p->rows % tc::kDirSub) return false;
+    if (!make_code_map(&dst.map[i], *p)) return false;
     rows += p->rows;
   }
+  for (int i = dst.nseg; i < 3; i++) dst.map[i] = dst.map[0];
   const int groups = (cols + kQBlock - 1) / kQBlock;
   const int mt = (rows + tc::kMC - 1) / tc::kMC;
   dst.rows = rows;
   dst.cols = cols;
-  const size_t bytes = (size_t)mt * groups * tc::kTileA;
-  if (!tc_alloc(t, (void**)&dst.wt, bytes)) return false;
-  cudaMemsetAsync(dst.wt, 0, bytes, m->stream);  // padding rows of the last tile
   if (parts.size() == 1) {
     dst.scales = parts[0]->scales;
     dst.own_scales = false;
@@ -114,20 +151,31 @@ inline bool tc_build(sr_model* m, TcState* t, TcMatrix& dst, const std::vector<c
   }
   int r0 = 0;
   for (const Param* p : parts) {
-    const int64_t chunks = (int64_t)p->rows * groups * 8;
-    tc::k_codes_tiled<<<(int)std::min<int64_t>((chunks + 255) / 256, 148 * 64), 256, 0, m->stream>>>(
-        p->values, p->format, p->rows, cols, r0, groups, dst.wt);
     if (dst.own_scales)
       cudaMemcpyAsync(dst.scales + (int64_t)r0 * groups, p->scales, (size_t)p->rows * groups * 4,
                       cudaMemcpyDeviceToDevice, m->stream);
     r0 += p->rows;
   }
+  dst.wt = nullptr;
+  if (!cache) return true;
+  const size_t bytes = (size_t)mt * groups * tc::kTileA;
+  if (!tc_alloc(t, (void**)&dst.wt, bytes)) return false;
+  cudaMemsetAsync(dst.wt, 0, bytes, m->stream);  // padding rows of the last tile
+  r0 = 0;
+  for (const Param* p : parts) {
+    const int64_t chunks = (int64_t)p->rows * groups * 8;
+    tc::k_codes_tiled<<<(int)std::min<int64_t>((chunks + 255) / 256, 148 * 64), 256, 0, m->stream>>>(
+        p->values, p->format, p->rows, cols, r0, groups, dst.wt);
+    r0 += p->rows;
+  }
   return true;
 }
 
-// Lazily (re)build the shadows after the weights change.  Returns false when
-// the tensor-core path is unavailable (f32 weights, shapes, memory).
-inline bool tc_prepare(sr_model* m) {
+// Lazily (re)build the matrices after the weights change.  Returns false when
+// the tensor-core path is unavailable (f32 weights, shapes, memory).  The code
+// cache is all or nothing: if it does not fit, every matrix reads its codes
+// directly.
+inline TcState* tc_state_make(sr_model* m) {
   if (!m->tc) {
     TcState* t = new TcState();
     m->tc = t;
@@ -136,31 +184,43 @@ inline bool tc_prepare(sr_model* m) {
       delete t;
     });
   }
-  TcState* t = tc_state(m);
+  return tc_state(m);
+}
+inline bool tc_build_all(sr_model* m, TcState* t, bool cache) {
+  const ModelDims& dm = m->dm;
+  const int L = dm.layers;
+  t->qkv.assign(L, TcMatrix());
+  t->o.assign(L, TcMatrix());
+  t->gateup.assign(L, TcMatrix());
+  t->down.assign(L, TcMatrix());
+  for (int l = 0; l < L; l++) {
+    const Param* P = &m->params[1 + 9 * l];
+    if (!tc_build(m, t, t->qkv[l], {&P[1], &P[2], &P[3]}, cache) || !tc_build(m, t, t->o[l], {&P[4]}, cache) ||
+        !tc_build(m, t, t->gateup[l], {&P[6], &P[7]}, cache) || !tc_build(m, t, t->down[l], {&P[8]}, cache))
+      return false;
+  }
+  const Param& head = m->d.tied ? m->params[0] : m->params.back();
+  return tc_build(m, t, t->head, {&head}, cache);
+}
+inline bool tc_prepare(sr_model* m) {
+  TcState* t = tc_state_make(m);
   if (t->version == m->weights_version) return !t->disabled;
   tc_free(t);
   t->version = m->weights_version;
   t->disabled = true;
+  t->cached = false;
   const ModelDims& dm = m->dm;
   if (m->d.weight_format == SR_FMT_F32 || dm.dim % 8 || dm.hidden % 8 || dm.qd % 8 || !encode_fn()) return false;
   cudaFuncSetAttribute(tc::k_gemm_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
-  const int L = dm.layers;
-  t->qkv.resize(L);
-  t->o.resize(L);
-  t->gateup.resize(L);
-  t->down.resize(L);
-  for (int l = 0; l < L; l++) {
-    const Param* P = &m->params[1 + 9 * l];
-    if (!tc_build(m, t, t->qkv[l], {&P[1], &P[2], &P[3]}) || !tc_build(m, t, t->o[l], {&P[4]}) ||
-        !tc_build(m, t, t->gateup[l], {&P[6], &P[7]}) || !tc_build(m, t, t->down[l], {&P[8]})) {
+  cudaFuncSetAttribute(tc::k_gemm_direct, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kDirSmemBytes);
+  bool built = t->cache_wanted && tc_build_all(m, t, true);
+  t->cached = built;
+  if (!built) {  // without the cache (not wanted, or it did not fit)
+    tc_free(t);
+    if (!tc_build_all(m, t, false)) {
       tc_free(t);
       return false;
     }
-  }
-  const Param& head = m->d.tied ? m->params[0] : m->params.back();
-  if (!tc_build(m, t, t->head, {&head})) {
-    tc_free(t);
-    return false;
   }
   const int xcols = std::max(std::max(dm.dim, dm.hidden), dm.qd);
   {
@@ -233,7 +293,12 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::Gemm
   const CUtensorMap& xh = in_kind == 1 ? t->xh_h : (in_kind == 2 ? t->xh_q : t->xh_d);
   const CUtensorMap& xl = in_kind == 1 ? t->xl_h : (in_kind == 2 ? t->xl_q : t->xl_d);
   a.wt = W.wt;
-  tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, m->stream>>>(xh, xl, a);
+  a.fmt = W.fmt;
+  if (W.wt)
+    tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, m->stream>>>(xh, xl, a);
+  else
+    tc::k_gemm_direct<<<a.ngroups * a.nt, tc::kDirThreads, tc::kDirSmemBytes, m->stream>>>(xh, xl, W.map[0], W.map[1],
+                                                                                         W.map[2], a);
   sr_count_launch(m);
   // Tiles left in partial slots: every tile when the epilogue needs the
   // residual or the head row map, otherwise only tiles cut by a group boundary.
@@ -323,6 +388,44 @@ inline bool tc_head(sr_model* m, int heads, bool presplit = false) {
   if (!presplit) tc_split_x(m, m->N, heads, dm.dim);
   return tc_gemm(m, tc_state(m)->head, 0, heads, a);
 }
+
+// One matrix parameter on the tensor cores, outside the step (sr_linear in
+// fast mode), with the same code source as the step's matrices; its input
+// width must be one the operand maps cover (dim, hidden, attention width).
+inline bool tc_linear(sr_model* m, const float* X, int n, const Param& W, const LinearOut& O) {
+  if (n < kTcMinRows || (W.format != kQ8 && W.format != kQ4) || !tc_prepare(m)) return false;
+  const ModelDims& dm = m->dm;
+  const int in_kind = W.cols == dm.dim ? 0 : (W.cols == dm.hidden ? 1 : (W.cols == dm.qd ? 2 : -1));
+  if (in_kind < 0) return false;
+  TcState* t = tc_state(m);
+  const size_t before = t->allocs.size();
+  TcMatrix M;
+  bool ok = tc_build(m, t, M, {&W}, t->cached);
+  if (ok) {
+    tc::GemmArgs a{};
+    a.nseg = 1;
+    a.seg[0] = seg(W.rows, O.y, O.ldy, O.bias, O.resid);
+    a.out_map = O.out_map;
+    tc_split_x(m, X, n, W.cols);
+    ok = tc_gemm(m, M, in_kind, n, a);
+  }
+  if (t->allocs.size() > before) {  // the temporary cache of M
+    cudaStreamSynchronize(m->stream);
+    for (size_t i = before; i < t->allocs.size(); i++) cudaFree(t->allocs[i]);
+    t->allocs.resize(before);
+  }
+  return ok;
+}
+
+// sr_model_set_code_cache: rebuild on the next fast step with or without it.
+inline void tc_set_cache(sr_model* m, bool on) {
+  TcState* t = tc_state_make(m);
+  if (t->cache_wanted != on) {
+    t->cache_wanted = on;
+    t->version = ~0ull;
+  }
+}
+inline bool tc_cached(sr_model* m) { return m->tc && tc_state(m)->cached && !tc_state(m)->disabled; }
 
 // After the step's stream synchronize: SR_ETIMEOUT if a bounded wait expired.
 inline int tc_check(sr_model* m) {

@@ -72,8 +72,8 @@ inline int fast_check(sr_model* m) {
 // all-reduced projection: X += T (addInPlace, M:6405/6418), written back.
 __global__ void __launch_bounds__(128)
 k_rmsnorm_fast(float* __restrict__ X, const int32_t* __restrict__ src_map, const float* __restrict__ w,
-               float* __restrict__ Y, int rows, int d, double eps, __nv_bfloat16* __restrict__ yh,
-               __nv_bfloat16* __restrict__ yl, const float* __restrict__ T, const uint4* __restrict__ Tll,
+               float* __restrict__ Y, int rows, int d, double eps, op16* __restrict__ yh,
+               op16* __restrict__ yl, const float* __restrict__ T, const uint4* __restrict__ Tll,
                uint32_t epoch, int* err) {
   __shared__ double red[4];
   const int r = blockIdx.x;
@@ -116,10 +116,10 @@ k_rmsnorm_fast(float* __restrict__ X, const int32_t* __restrict__ src_map, const
       const float4 g = *(const float4*)(w + j);
       const float y0 = v.x * a * g.x, y1 = v.y * a * g.y, y2 = v.z * a * g.z, y3 = v.w * a * g.w;
       if (yh) {
-        split_bf16(y0, yh + o + j, yl + o + j);
-        split_bf16(y1, yh + o + j + 1, yl + o + j + 1);
-        split_bf16(y2, yh + o + j + 2, yl + o + j + 2);
-        split_bf16(y3, yh + o + j + 3, yl + o + j + 3);
+        split_op(y0, yh + o + j, yl + o + j);
+        split_op(y1, yh + o + j + 1, yl + o + j + 1);
+        split_op(y2, yh + o + j + 2, yl + o + j + 2);
+        split_op(y3, yh + o + j + 3, yl + o + j + 3);
       } else {
         *(float4*)(Y + o + j) = make_float4(y0, y1, y2, y3);
       }
@@ -128,7 +128,7 @@ k_rmsnorm_fast(float* __restrict__ X, const int32_t* __restrict__ src_map, const
     for (int j = threadIdx.x; j < d; j += 128) {
       const float y = x[j] * a * w[j];
       if (yh)
-        split_bf16(y, yh + o + j, yl + o + j);
+        split_op(y, yh + o + j, yl + o + j);
       else
         Y[o + j] = y;
     }
@@ -136,7 +136,7 @@ k_rmsnorm_fast(float* __restrict__ X, const int32_t* __restrict__ src_map, const
 }
 
 inline void fast_rmsnorm(sr_model* m, float* X, const int32_t* src_map, const float* w, float* Y, int rows, int d,
-                         double eps, __nv_bfloat16* yh = nullptr, __nv_bfloat16* yl = nullptr,
+                         double eps, op16* yh = nullptr, op16* yl = nullptr,
                          const float* T = nullptr, const uint4* Tll = nullptr, uint32_t epoch = 0,
                          int* err = nullptr) {
   k_rmsnorm_fast<<<rows, 128, 0, m->stream>>>(X, src_map, w, Y, rows, d, eps, yh, yl, T, Tll, epoch, err);
@@ -145,10 +145,10 @@ inline void fast_rmsnorm(sr_model* m, float* X, const int32_t* src_map, const fl
 // SwiGLU h = g/(1+exp(-g)) * u in fp32 (M:6410-6413 reordered), written as the
 // down projection's bf16 hi/lo operand planes.
 __global__ void k_swiglu_split(const float* __restrict__ G, const float* __restrict__ U,
-                               __nv_bfloat16* __restrict__ hh, __nv_bfloat16* __restrict__ hl, int64_t count) {
+                               op16* __restrict__ hh, op16* __restrict__ hl, int64_t count) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
     const float g = G[i];
-    split_bf16(g / (1.f + __expf(-g)) * U[i], hh + i, hl + i);
+    split_op(g / (1.f + __expf(-g)) * U[i], hh + i, hl + i);
   }
 }
 
@@ -219,7 +219,7 @@ inline size_t fa_scratch_floats(const ModelDims& dm, int items, size_t* units_ou
 // Launch split + combine with caller-provided scratch (no allocation).  With
 // xh/xl set, the combine writes bf16 hi/lo operand planes instead of fp32 A.
 inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, const FaWork& items, int layer, float* part_o,
-                               float* part_ml, __nv_bfloat16* xh = nullptr, __nv_bfloat16* xl = nullptr) {
+                               float* part_ml, op16* xh = nullptr, op16* xl = nullptr) {
   const ModelDims& dm = m->dm;
   FastAttnArgs a;
   a.Q = m->Q;
@@ -241,7 +241,7 @@ inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, const
 // Returns false (exact kernel runs instead) for unsupported shapes or when the
 // split scratch would exceed its cap.  The scratch grows on demand.
 inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, const FaWork& work, int layer,
-                               __nv_bfloat16* xh = nullptr, __nv_bfloat16* xl = nullptr) {
+                               op16* xh = nullptr, op16* xl = nullptr) {
   const ModelDims& dm = m->dm;
   if (!fast_attention_supported(dm)) return false;
   FastState* st = fast_state(m);

@@ -787,6 +787,20 @@ extern "C" int sr_model_set_mode(sr_model* m, int32_t mode) {
   return SR_OK;
 }
 
+extern "C" int sr_model_set_code_cache(sr_model* m, int32_t enabled) {
+  if (!m) return sr_fail(SR_EINVAL, "null model");
+  CK(cudaSetDevice(m->device));
+  tc_set_cache(m, enabled != 0);
+  return SR_OK;
+}
+extern "C" int sr_model_code_cache(sr_model* m, int32_t* cached) {
+  if (!m || !cached) return sr_fail(SR_EINVAL, "null argument");
+  CK(cudaSetDevice(m->device));
+  tc_prepare(m);
+  *cached = tc_cached(m) ? 1 : 0;
+  return SR_OK;
+}
+
 // ----------------------------------------------------------------- KV pool --
 extern "C" int sr_kvpool_create(sr_model* m, int64_t num_pages, sr_kvpool** out) {
   if (!m || !out) return sr_fail(SR_EINVAL, "null argument");
@@ -1006,7 +1020,7 @@ static void launch_linear_exact(sr_model* m, const float* X, int n, const Param&
   }
 }
 static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, const BatchInfo& info, int layer,
-                           __nv_bfloat16* xh, __nv_bfloat16* xl);
+                           op16* xh, op16* xl);
 void sr_launch_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O, int cls = SR_PROF_LINEAR) {
   ProfScope ps(m, cls);
   if (m->mode == SR_MODE_FAST && fast_linear(m, X, n, W, O)) return;
@@ -1222,8 +1236,8 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   const bool tc = fast && tc_active(m, n);
   const bool tp = dm.tp_size > 1;
   int rc = SR_OK;
-  __nv_bfloat16* xh = tc ? tc_xh(m) : nullptr;
-  __nv_bfloat16* xl = tc ? tc_xl(m) : nullptr;
+  op16* xh = tc ? tc_xh(m) : nullptr;
+  op16* xl = tc ? tc_xl(m) : nullptr;
   TpSum pending;  // tensor parallel: an all-reduced sum still to be added to X
   int* tp_err = m->peer ? ((PeerHost*)m->peer)->err : nullptr;
   for (int l = 0; l < L; l++) {
@@ -1592,7 +1606,7 @@ extern "C" int sr_step_sample(sr_model* m, sr_kvpool* pool, const sr_batch* batc
 // Fast-mode attention: split-K kernels when the shape is covered (returns true
 // when they also wrote xh/xl, if given), else the exact kernel into fp32 A.
 static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, const BatchInfo& info, int layer,
-                           __nv_bfloat16* xh, __nv_bfloat16* xl) {
+                           op16* xh, op16* xl) {
   if (fast_attention_try(m, pool->data, n, FaWork{info.attn_items, info.attn_single, info.attn_groups}, layer, xh, xl))
     return xh != nullptr;
   launch_attention_exact(m, pool, n, info.max_len, layer);
@@ -1600,11 +1614,12 @@ static bool fast_attention(sr_model* m, sr_kvpool* pool, int n, const BatchInfo&
 }
 
 // Per-call fast projection hook: the decode GEMV for steps of a few rows
-// (gemv.cuh); larger steps go through the tensor-core path (fast_gemm.cuh)
-// directly, and shapes neither covers run the exact kernels.
+// (gemv.cuh), the tensor-core GEMM (fast_gemm.cuh) from kTcMinRows rows; the
+// step calls the fused tensor-core entry points directly, and shapes neither
+// covers run the exact kernels.
 bool sr::fast_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O) {
   const Param* w = &W;
-  return gemv_run(m, X, n, &w, &O, 1);
+  return gemv_run(m, X, n, &w, &O, 1) || tc_linear(m, X, n, W, O);
 }
 
 // ---------------------------------------------------------------- profiling --

@@ -76,6 +76,7 @@ struct GemmArgs {
   Segment seg[3];
   int nseg;
   int* err;
+  int fmt;  // kQ8 or kQ4: the code format k_gemm_direct reads (tc_gemm_direct.cuh)
 };
 
 // Stream-K range of group g over the mt*groups (tile, block) units.  32-bit

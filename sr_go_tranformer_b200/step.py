@@ -151,6 +151,16 @@ class Model:
     def set_mode(self, mode):
         A.check(A.lib().sr_model_set_mode(self.h, {"exact": A.SR_MODE_EXACT, "fast": A.SR_MODE_FAST}.get(mode, mode)))
 
+    def set_code_cache(self, enabled):
+        """Fast mode: keep the fp16 code cache (True, default) or read the
+        reference codes as stored (False); see sr_model_set_code_cache."""
+        A.check(A.lib().sr_model_set_code_cache(self.h, 1 if enabled else 0))
+
+    def code_cache(self):
+        v = C.c_int32()
+        A.check(A.lib().sr_model_code_cache(self.h, C.byref(v)))
+        return bool(v.value)
+
     def param_info(self, i):
         info = A.ParamInfo()
         A.check(A.lib().sr_model_param_info(self.h, i, C.byref(info)))

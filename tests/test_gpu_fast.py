@@ -18,9 +18,10 @@ FAST_ATOL = 5e-4
 FAST_TIE = 2 * FAST_ATOL
 
 
-def run_pair(oracle, srlib, om, prompts, chunk, decode_steps, threads=8):
+def run_pair(oracle, srlib, om, prompts, chunk, decode_steps, threads=8, cache=True):
     from sr_go_tranformer_b200 import step as S
     dm = device_from_oracle(om, srlib, mode="fast")
+    dm.set_code_cache(cache)
     pages = sum((len(p) + decode_steps + om.cfg.page_tokens) // om.cfg.page_tokens + 1 for p in prompts)
     pool = S.PagePool(dm, pages)
     opool = np.zeros(pages * om.page_elements, dtype=np.float32)
@@ -71,15 +72,17 @@ def test_fast_smollm_shape_long_contexts(oracle, srlib):
     assert worst <= FAST_ATOL
 
 
-def test_fast_mistral_shape_one_layer(oracle, srlib):
-    """hd 128, 4 query heads per KV head, Q8; contexts up to 600."""
+@pytest.mark.parametrize("cache", [True, False], ids=["code-cache", "direct-codes"])
+def test_fast_mistral_shape_one_layer(oracle, srlib, cache):
+    """hd 128, 4 query heads per KV head, Q8; contexts up to 600; with the bf16
+    code cache and with the codes read as stored."""
     cfg = oracle.make_config(2048, 4096, 14336, 1, 32, 8, 1024, rope_theta=1e6, tied=False, weight_format="q8",
                              page_tokens=16)
     om = oracle.Model(cfg)
     om.init_synthetic(5, 0.02)
     rng = np.random.default_rng(6)
     prompts = [rng.integers(0, 2048, size=n).tolist() for n in (600, 257, 31)]
-    worst, ties = run_pair(oracle, srlib, om, prompts, chunk=300, decode_steps=2)
+    worst, ties = run_pair(oracle, srlib, om, prompts, chunk=300, decode_steps=2, cache=cache)
     assert worst <= FAST_ATOL
 
 

@@ -210,3 +210,36 @@ def test_fast_decode_gemv(oracle, srlib, fmt, cols):
             err = np.abs(got.astype(np.float64) - want) / np.maximum(bound, 1e-30)
             assert err.max() <= 1e-5, (fmt, cols, index, n, float(err.max()))
     dm.close()
+
+
+@pytest.mark.parametrize("cache", [True, False], ids=["code-cache", "direct-codes"])
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+@pytest.mark.parametrize("cols", [64, 576, 4096, 14336])
+def test_fast_tensor_core_gemm(oracle, srlib, fmt, cols, cache):
+    """SR_MODE_FAST projections of 32 or more rows run the tcgen05 GEMM, with
+    the fp16 code cache or (direct) reading the Q8 / Q4 codes as stored and
+    widening them to bf16 in shared memory.  down_proj [64, cols]: one 256-feature tile whose blocks are cut
+    across up to 56 stream-K groups (the group with the first blocks adds the
+    others' published partial sums); gate [cols, 64]: many whole tiles, the
+    last one partly out of range; the embedding as a head [256, 64].  Row
+    counts cover one partial 128-row tile up to eight.  Each output must be
+    within 3e-5 of sum_j |x_j w_j| of the exact-order oracle (bf16 hi + lo
+    activation planes); both code sources must give identical bits."""
+    dm = model(hidden=cols, fmt=fmt)
+    dm.set_mode("fast")
+    dm.set_code_cache(cache)
+    rng = np.random.default_rng(cols + 7 * (fmt == "q4"))
+    for index, (rows_w, cols_w) in ((DOWN, (64, cols)), (7, (cols, 64)), (EMB, (256, 64))):
+        w = (rng.standard_normal((rows_w, cols_w)) * 0.05).astype(np.float32)
+        vals, sc = oracle.quantize(w, Q8 if fmt == "q8" else Q4)
+        dm.load_param(index, vals, sc)
+        wd = np.abs(dequant(vals, sc, fmt, rows_w, cols_w))
+        for n in (32, 33, 128, 200, 1000):
+            x = rng.standard_normal((n, cols_w)).astype(np.float32)
+            got = dm.linear(index, x)
+            assert dm.code_cache() == cache
+            want = oracle.linear(x, Q8 if fmt == "q8" else Q4, vals, sc, rows_w, cols_w, threads=8).reshape(got.shape)
+            bound = np.abs(x).astype(np.float64) @ wd.T
+            err = np.abs(got.astype(np.float64) - want) / np.maximum(bound, 1e-30)
+            assert err.max() <= 3e-5, (fmt, cols, index, n, float(err.max()))
+    dm.close()
