@@ -18,7 +18,8 @@ import numpy as np
 def simulate(model, requests, limit, max_batch, budget, chunk, mixed_chunk, eos_id=-1, blocked=-1, threads=4,
              prefix_limit=0, prefix_tail=False, stats=None):
     """requests: list of dicts(ids, max_tokens, temperature, top_k, top_p, penalty, seed).
-    Returns ({request index: (output ids, reason)}, trace of per-tick (counts, page tables)).
+    Returns ({request index: (output ids, reason)}, trace of per-tick (counts, page tables at the
+    step, page tables of the sessions still active after the tick)).
     stats, when a dict, receives prefix_hits / prefix_tokens / prefix_pages."""
     from oracle import oracle as O
     pt = model.cfg.page_tokens
@@ -152,6 +153,7 @@ def simulate(model, requests, limit, max_batch, budget, chunk, mixed_chunk, eos_
                 finished[s["rid"]] = (list(s["output"]), reason)
             else:
                 alive.append(s)
+        trace[-1] = trace[-1] + ([list(s["pages"]) for s in alive],)  # page tables after the tick
         sessions = alive
     if stats is not None:
         stats.update(prefix_hits=hits, prefix_tokens=tokens, prefix_pages=snap["pages"])

@@ -135,3 +135,19 @@ def test_fast_qwen_shape_32k_context_decode(oracle, srlib):
     exp = om.step(opool, pos, chunks, [c.pages for c in caches], [True] * len(pos), threads=8)
     err = float(np.abs(got - exp).max())
     assert err <= FAST_ATOL, f"32K-context decode logits differ by {err:.3g}"
+
+
+@pytest.mark.parametrize("rows", [1, 4, 16, 31])
+def test_fast_decode_rows(oracle, srlib, rows):
+    """Fast-mode decode steps of 1, 4, 16 and 31 rows (the decode GEMV up to 8
+    rows, the exact-order kernels up to 31; the tensor cores from 32) on the
+    Mistral-7B layer shape, 2 layers, Q8: `rows` sessions with short prompts,
+    then 3 decode steps, each against the oracle."""
+    cfg = oracle.make_config(2048, 4096, 14336, 2, 32, 8, 512, rope_theta=1e6, tied=False, weight_format="q8",
+                             page_tokens=16)
+    om = oracle.Model(cfg)
+    om.init_synthetic(21, 0.02, threads=8)
+    rng = np.random.default_rng(22 + rows)
+    prompts = [rng.integers(0, 2048, size=int(rng.integers(1, 4))).tolist() for _ in range(rows)]
+    worst, ties = run_pair(oracle, srlib, om, prompts, chunk=4, decode_steps=3)
+    assert worst <= FAST_ATOL
