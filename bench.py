@@ -25,16 +25,20 @@ engine tensor-parallel -- each holds 1/N of the heads, FFN columns and KV pool
 and the step all-reduces after o_proj and down_proj over NCCL -- so total
 work is fixed (strong scaling).  --parallel replicas runs N independent
 engines instead (weak scaling).
-`ttft_p50_ms` comes from a serving run before the decode measurement: the
-            same 256 requests (prompt ids uniform over the vocabulary) are
-            submitted at once to the C++ restatement of the reference engine
-            (admission, scheduleTokens, steps, sampling) on an empty KV pool,
-            with prefill chunks of 1024 tokens (also while sessions decode)
-            and a 1024-row token budget, and it ticks until every request has
-            its first token; TTFT is submit -> first sampled token, host clock
-            after the step's synchronising sample call (M:8441-8447).
+`ttft_p50_ms`, `stream_output_tok_s` (and `serving`) come from a serving run
+            after the decode measurement: the same 256 requests (prompt ids
+            uniform over the vocabulary) are submitted at once to the C++
+            restatement of the reference engine (admission, scheduleTokens,
+            steps, sampling) on an empty KV pool, with prefill chunks of 1024
+            tokens (also while sessions decode: --stream-mixed-chunk, whose
+            reference default is 1) and a 1024-row token budget, until the last
+            request completes.  TTFT is submit -> first sampled token, host
+            clock after the step's synchronising sample call (M:8441-8447);
+            stream tok/s = generated tokens / wall time from submission to the
+            last completion.
 `--impl reference` times the CPU oracle (the C restatement of the reference's
-Go step, all host threads) on a bounded sample of the same workload.
+Go step, all host threads): W untimed and K timed steps, each a decode step of
+8 of the 256 sessions (a bounded sample of the same workload).
 """
 
 import argparse
@@ -240,13 +244,17 @@ def make_model(cfg, device, mode, tp=(0, 1, None)):
     return model
 
 
-def ttft_phase(cfg, model, workload_rank=0, max_ticks=4000):
-    """Serve the workload's requests from an empty pool until each has its first token."""
+def serve_phase(cfg, model, workload_rank=0, mixed_chunk=1024, max_ticks=20000):
+    """Serve the workload's 256 requests from an empty pool through the C++
+    engine (sr_engine_*) until the last one completes: TTFT (submit -> first
+    sampled token) and ITL medians from the engine's own clock, and the
+    stream-level output tok/s = all generated tokens / wall time from
+    submission to the last completion."""
     from sr_go_tranformer_b200.engine import Engine
     prompts, outs, _, _ = workload(cfg, workload_rank, 0)
     n, pt, V = cfg["sessions"], cfg["page_tokens"], cfg["vocab"]
     pages = int(np.sum((prompts + outs + pt - 1) // pt))
-    eng = Engine(model, max_batch=n, token_budget=1024, prefill_chunk=1024, mixed_prefill_chunk=1024,
+    eng = Engine(model, max_batch=n, token_budget=1024, prefill_chunk=1024, mixed_prefill_chunk=mixed_chunk,
                  cache_bytes=pages * model.page_elements * 4)
     ids_rng = np.random.default_rng(cfg["seed"] + 17)
     t, k, p, pen = cfg["sampling"]
@@ -254,17 +262,27 @@ def ttft_phase(cfg, model, workload_rank=0, max_ticks=4000):
         eng.submit(ids_rng.integers(0, V, size=int(prompts[i])), int(outs[i]), t, k, p, pen, seed=cfg["seed"] + i)
     t0 = time.time()
     ticks = rows = 0
-    lat = eng.latency()
-    while lat["first_tokens"] < n and ticks < max_ticks:
+    first_wall = None
+    done = 0
+    while ticks < max_ticks:
         rows += eng.tick()
         ticks += 1
-        lat = eng.latency()
+        while eng.poll() is not None:
+            done += 1
+        if first_wall is None and eng.latency()["first_tokens"] >= n:
+            first_wall = time.time() - t0
+        if done >= n:
+            break
     wall = time.time() - t0
+    lat = eng.latency()
     st = eng.stats()
     eng.close()
-    return {"ttft_p50_ms": lat["ttft_p50_ms"], "first_tokens": lat["first_tokens"], "ticks": ticks,
-            "wall_s": wall, "prompt_tokens": int(np.sum(prompts)), "input_tok_s": st["input_tokens"] / wall,
-            "rows": rows, "settings": "prefill chunk 1024 (also while decoding), token budget 1024, max batch 256"}
+    return {"ttft_p50_ms": lat["ttft_p50_ms"], "itl_p50_ms": lat["itl_p50_ms"], "first_tokens": lat["first_tokens"],
+            "all_first_tokens_s": first_wall, "completed": done, "ticks": ticks, "wall_s": wall,
+            "prompt_tokens": int(np.sum(prompts)), "generated_tokens": int(st["generated_tokens"]),
+            "stream_output_tok_s": st["generated_tokens"] / wall, "input_tok_s": st["input_tokens"] / wall,
+            "rows": rows, "settings": f"prefill chunk 1024, mixed prefill chunk {mixed_chunk} (the reference default is"
+                                      f" 1), token budget 1024, max batch 256, run to the last completion"}
 
 
 def weight_bytes(cfg):
@@ -276,8 +294,10 @@ def weight_bytes(cfg):
     return L * per_layer + head + d * 4
 
 
-def cpu_baseline(cfg, sample_sessions, threads, steps=1):
-    """Time the CPU oracle on `sample_sessions` sessions of the same workload."""
+def cpu_baseline(cfg, sample_sessions, threads, steps=1, warmup=0):
+    """Time the CPU oracle on `sample_sessions` sessions of the same workload:
+    `warmup` untimed then `steps` timed decode steps (each session appends one
+    token per step)."""
     from oracle import oracle as O
     O.build()
     pt = cfg["page_tokens"]
@@ -290,23 +310,28 @@ def cpu_baseline(cfg, sample_sessions, threads, steps=1):
     prompts, outs, offsets, rng = workload(cfg, 0, 3)
     idx = list(range(sample_sessions))
     pos = [int(prompts[i] + offsets[i]) for i in idx]
+    total = warmup + steps
     tables, nxt = [], 0
     for p in pos:
-        k = (p + steps + pt - 1) // pt  # pages for every timed step's position
+        k = (p + total + pt - 1) // pt  # pages for every step's position
         tables.append(list(range(nxt, nxt + k)))
         nxt += k
     pool = np.zeros(nxt * m.page_elements, dtype=np.float32)
     toks = [[int(t)] for t in rng.integers(0, cfg["vocab"], size=len(idx))]
     times = []
-    for s in range(steps):
+    for s in range(total):
         t0 = time.time()
-        m.step(pool, [p + s for p in pos], toks, tables, threads=threads)
-        times.append(time.time() - t0)
-    t = float(np.median(times))
-    return {"value": len(idx) / t, "unit": "output tok/s", "cores": threads, "kind": "port",
-            "sample": f"{len(idx)} of the workload's sessions, one decode step each (contexts {min(pos)}..{max(pos)}),"
-                      f" C oracle restating the Go step, {threads} threads; model init {init_s:.1f}s untimed",
-            "step_s": t}
+        logits = m.step(pool, [p + s for p in pos], toks, tables, threads=threads)
+        dt = time.time() - t0
+        if s >= warmup:
+            times.append(dt)
+        toks = [[int(np.argmax(x))] for x in logits]
+    t = float(np.sum(times))
+    return {"value": len(idx) * steps / t, "unit": "output tok/s", "cores": threads, "kind": "port",
+            "sample": f"{len(idx)} of the workload's 256 sessions (contexts {min(pos)}..{max(pos)}), {warmup} untimed + "
+                      f"{steps} timed decode steps, C oracle restating the Go step, {threads} threads; model init "
+                      f"{init_s:.1f}s untimed",
+            "step_s": t / steps, "steps": steps}
 
 
 def bench_config(cfg, args, world, tp):
@@ -331,12 +356,14 @@ def run_reference(args, cfg):
         args.allreduce = "peer" if args.gpus == 2 else "nccl"
     from oracle import oracle as O
     O.build()
-    # bounded sample: 8 sessions per step (about 10 s of CPU work per step on 32+ cores)
-    res = cpu_baseline(cfg, args.ref_sessions, threads, steps=max(1, min(K, 3)))
+    # bounded sample: each step is one decode step of 8 of the 256 sessions (about
+    # 1.5-2 s of CPU work on 16 cores), W untimed then K timed
+    res = cpu_baseline(cfg, args.ref_sessions, threads, steps=K, warmup=W)
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "output tok/s", "n_gpus": args.gpus,
-            "steps": K, "warmup": W, "ms_per_step": res["step_s"] * 1000.0, "higher_is_better": True,
+            "steps": res["steps"], "warmup": W, "ms_per_step": res["step_s"] * 1000.0, "higher_is_better": True,
             "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": dict(bench_config(cfg, args, args.gpus, tp), sessions_sampled=args.ref_sessions),
+            "config": dict(bench_config(cfg, args, args.gpus, tp), sessions_sampled=args.ref_sessions,
+                           sample="each step decodes 8 of the 256 sessions on the CPU"),
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": "output tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -360,7 +387,10 @@ def main():
                     help="tensor-parallel all-reduce: the library's NVLink peer-memory kernels (flag barriers, or "
                          "peer-ll: flags inside the data, one kernel), NCCL, or auto (peer at 2 ranks, NCCL above: the "
                          "faster one measured at each size)")
-    ap.add_argument("--no-ttft", action="store_true", help="skip the serving run that measures TTFT")
+    ap.add_argument("--no-ttft", action="store_true", help="skip the serving run (TTFT, ITL, stream tok/s)")
+    ap.add_argument("--stream-mixed-chunk", type=int, default=1024,
+                    help="mixed prefill chunk of the serving run (1 = the reference default; slower: with any session "
+                         "decoding, every prompt advances one token per tick)")
     args = ap.parse_args()
     cfg = dict(CONFIG)
     cfg["sessions"] = args.sessions
@@ -427,7 +457,8 @@ def main():
     # The serving run for TTFT comes after the decode measurement (its prefill
     # steps heat the GPU) and needs the memory of the decode state's KV pool.
     st.pool.close()
-    ttft = None if args.no_ttft else ttft_phase(cfg, model, workload_rank=0 if tp else rank)
+    ttft = None if args.no_ttft else serve_phase(cfg, model, workload_rank=0 if tp else rank,
+                                                 mixed_chunk=args.stream_mixed_chunk)
     t = torch.tensor([span_ms, e2e_ms], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -457,9 +488,12 @@ def main():
             "metric": METRIC, "value": value, "unit": "output tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": span_max / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
+            "dtype": ("f32; projections bf16 hi+lo x bf16 codes on tensor cores, fp32 accumulate" if args.mode == "fast"
+                      else "f32"),
+            "data": "synthetic",
             "config": bench_config(cfg, args, world, tp),
             "itl_p50_ms": span_max / K, "ttft_p50_ms": ttft["ttft_p50_ms"] if ttft else None,
+            "stream_output_tok_s": ttft["stream_output_tok_s"] if ttft else None,
             "hbm_gbs_step": step_bytes / (span_max / K / 1000.0) / 1e9,
             "algorithmic_bytes_per_step": step_bytes,
             "e2e": {"value": e2e_val, "unit": "output tok/s",
@@ -473,7 +507,7 @@ def main():
             "clocks": clocks,
         }
         if ttft:
-            line["ttft"] = ttft
+            line["serving"] = ttft
         if world == 1 and not args.no_cpu_baseline:
             try:
                 cb = cpu_baseline(cfg, args.cpu_sessions, os.cpu_count() or 1)

@@ -51,7 +51,7 @@ def test_prefix_cache_keeps_outputs_and_reuses_prefix(oracle, tail):
     if tail:
         assert st["prefix_tokens"] >= (len(reqs) - 1) * 40
     # borrowed snapshot pages (ids >= limit) appear in later page tables
-    assert any(p >= 16 for _, tables in trace for t in tables for p in t)
+    assert any(p >= 16 for _, tables, _ in trace for t in tables for p in t)
 
 
 def test_prefix_cache_with_concurrent_borrowers(oracle):
