@@ -39,6 +39,11 @@ engines instead (weak scaling).
 `--impl reference` times the CPU oracle (the C restatement of the reference's
 Go step, all host threads): W untimed and K timed steps, each a decode step of
 8 of the 256 sessions (a bounded sample of the same workload).
+--config qwen7b measures the Qwen2.5-7B long-context configuration instead:
+16 sessions with 31,744-token prompts (synthetic prefilled KV pages) decoding
+up to 1,024 tokens each, q4-mixed weights, split-K attention over contexts of
+31,744..32,768 positions; tensor-parallel 8 ways on 8 GPUs (each KV head on a
+pair of ranks that split its 7 query heads 4/3).
 """
 
 import argparse
@@ -57,17 +62,30 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 CONFIG = dict(name="mistral7b-q8-256req", vocab=32768, dim=4096, hidden=14336, layers=32, heads=32, kv_heads=8,
-              context=32768, rope_theta=1e6, norm_eps=1e-5, tied=False, fmt="q8", page_tokens=16, sessions=256,
-              prompt_median=1024, prompt_sigma=1.0, prompt_max=8192, out_lo=64, out_hi=512,
-              sampling=(0.8, 40, 0.95, 1.1), seed=20261201)
-METRIC = "output tok/s, Mistral-7B-shape Q8, 256 ragged reqs; p50 TTFT/ITL; HBM GB/s"
+              context=32768, rope_theta=1e6, norm_eps=1e-5, tied=False, qkv_bias=False, fmt="q8", page_tokens=16,
+              sessions=256, prompt_median=1024, prompt_sigma=1.0, prompt_max=8192, out_lo=64, out_hi=512,
+              sampling=(0.8, 40, 0.95, 1.1), seed=20261201,
+              metric="output tok/s, Mistral-7B-shape Q8, 256 ragged reqs; p50 TTFT/ITL; HBM GB/s")
+# The Qwen2.5-7B long-context configuration: 16 sessions whose 31,744-token
+# prompts leave room for 1,024 decode tokens inside the reference's 32,768
+# context (prompt + max_tokens <= Context); decoding through split-K attention.
+QWEN7B = dict(name="qwen2.5-7b-q4mixed-16x31744", vocab=152064, dim=3584, hidden=18944, layers=28, heads=28,
+              kv_heads=4, context=32768, rope_theta=1e6, norm_eps=1e-6, tied=False, qkv_bias=True, fmt="q4-mixed",
+              page_tokens=16, sessions=16, prompt_fixed=31744, out_lo=1024, out_hi=1024,
+              sampling=(0.8, 40, 0.95, 1.1), seed=20261202,
+              metric="output tok/s, Qwen2.5-7B-shape q4-mixed, 16 x 31,744-token prompts decoding 1,024; HBM GB/s")
+CONFIGS = {"mistral7b": CONFIG, "qwen7b": QWEN7B}
+METRIC = CONFIG["metric"]
 
 
 def workload(cfg, rank, warmup_steps):
     rng = np.random.default_rng(cfg["seed"] + 7919 * rank)
     S = cfg["sessions"]
-    prompts = np.clip(np.round(np.exp(np.log(cfg["prompt_median"]) + cfg["prompt_sigma"] * rng.standard_normal(S))),
-                      1, cfg["prompt_max"]).astype(np.int64)
+    if "prompt_fixed" in cfg:
+        prompts = np.full(S, cfg["prompt_fixed"], dtype=np.int64)
+    else:
+        prompts = np.clip(np.round(np.exp(np.log(cfg["prompt_median"]) + cfg["prompt_sigma"] *
+                                          rng.standard_normal(S))), 1, cfg["prompt_max"]).astype(np.int64)
     outs = rng.integers(cfg["out_lo"], cfg["out_hi"] + 1, size=S)
     offsets = np.array([rng.integers(0, max(1, o - warmup_steps)) for o in outs], dtype=np.int64)
     return prompts, outs, offsets, rng
@@ -153,7 +171,7 @@ def advance_sessions(pos, hist, hoff, ids, prompts, outs):
 
 
 class DecodeState:
-    """256 sessions in steady decode over one device model and page pool."""
+    """The workload's sessions in steady decode over one device model and page pool."""
 
     def __init__(self, cfg, model, warmup, workload_rank=0, steps=0):
         """steps: the decode steps that follow the warm-up; the sessions' starting
@@ -236,7 +254,7 @@ class DecodeState:
 def make_model(cfg, device, mode, tp=(0, 1, None)):
     from sr_go_tranformer_b200 import step as S
     d = S.make_desc(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
-                    cfg["context"], cfg["rope_theta"], cfg["norm_eps"], cfg["tied"], False, cfg["fmt"],
+                    cfg["context"], cfg["rope_theta"], cfg["norm_eps"], cfg["tied"], cfg["qkv_bias"], cfg["fmt"],
                     cfg["page_tokens"])
     model = S.Model(d, device, tp_rank=tp[0], tp_size=tp[1], nccl_id=tp[2])
     model.init_synthetic(cfg["seed"], 0.02)
@@ -286,11 +304,17 @@ def serve_phase(cfg, model, workload_rank=0, mixed_chunk=1024, max_ticks=20000):
 
 
 def weight_bytes(cfg):
-    """Matrix bytes read once per step (Q8 values + fp32 scales), embedding excluded."""
+    """Matrix bytes read once per step (codes + fp32 scales per 64-column
+    block; Q4 codes two per byte, the head Q8 under q4-mixed), embedding excluded."""
     d, kd, h, V, L = cfg["dim"], cfg["dim"] // cfg["heads"] * cfg["kv_heads"], cfg["hidden"], cfg["vocab"], cfg["layers"]
+    q4 = cfg["fmt"] in ("q4", "q4-mixed")
+
+    def mat(r, c, q4m):
+        return r * ((c + 1) // 2 if q4m else c) + r * ((c + 63) // 64) * 4
+
     mats = [(d, d), (kd, d), (kd, d), (d, d), (h, d), (h, d), (d, h)]
-    per_layer = sum(r * c + r * ((c + 63) // 64) * 4 for r, c in mats) + 2 * d * 4
-    head = V * d + V * ((d + 63) // 64) * 4
+    per_layer = sum(mat(r, c, q4) for r, c in mats) + 2 * d * 4 + (2 * d + 2 * kd) * 4 * cfg.get("qkv_bias", False)
+    head = mat(V, d, cfg["fmt"] == "q4")
     return L * per_layer + head + d * 4
 
 
@@ -302,7 +326,7 @@ def cpu_baseline(cfg, sample_sessions, threads, steps=1, warmup=0):
     O.build()
     pt = cfg["page_tokens"]
     c = O.make_config(cfg["vocab"], cfg["dim"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
-                      cfg["context"], cfg["rope_theta"], cfg["norm_eps"], cfg["tied"], False, cfg["fmt"], pt)
+                      cfg["context"], cfg["rope_theta"], cfg["norm_eps"], cfg["tied"], cfg["qkv_bias"], cfg["fmt"], pt)
     m = O.Model(c)
     t0 = time.time()
     m.init_synthetic(cfg["seed"], 0.02, threads=threads)
@@ -328,7 +352,7 @@ def cpu_baseline(cfg, sample_sessions, threads, steps=1, warmup=0):
         toks = [[int(np.argmax(x))] for x in logits]
     t = float(np.sum(times))
     return {"value": len(idx) * steps / t, "unit": "output tok/s", "cores": threads, "kind": "port",
-            "sample": f"{len(idx)} of the workload's 256 sessions (contexts {min(pos)}..{max(pos)}), {warmup} untimed + "
+            "sample": f"{len(idx)} of the workload's {cfg['sessions']} sessions (contexts {min(pos)}..{max(pos)}), {warmup} untimed + "
                       f"{steps} timed decode steps, C oracle restating the Go step, {threads} threads; model init "
                       f"{init_s:.1f}s untimed",
             "step_s": t / steps, "steps": steps}
@@ -337,7 +361,9 @@ def cpu_baseline(cfg, sample_sessions, threads, steps=1, warmup=0):
 def bench_config(cfg, args, world, tp):
     """The `config` object of the JSON line (both arms report the same one)."""
     return {"workload": cfg["name"], "sessions": cfg["sessions"], "layers": cfg["layers"],
-            "page_tokens": cfg["page_tokens"], "weights": "q8 (64-col blocks, fp32 scales)",
+            "page_tokens": cfg["page_tokens"],
+            "weights": {"q8": "q8 (64-col blocks, fp32 scales)",
+                        "q4-mixed": "q4-mixed (q4 layers, q8 embedding/head; 64-col blocks, fp32 scales)"}[cfg["fmt"]],
             "mode": args.mode, "parallelism": f"tp{world}" if tp else f"replicas{world}",
             "allreduce": (args.allreduce if tp else None),
             "kv_state": "synthetic prefilled pages (prompt + decode offset)",
@@ -356,14 +382,14 @@ def run_reference(args, cfg):
         args.allreduce = "peer" if args.gpus == 2 else "nccl"
     from oracle import oracle as O
     O.build()
-    # bounded sample: each step is one decode step of 8 of the 256 sessions (about
-    # 1.5-2 s of CPU work on 16 cores), W untimed then K timed
+    # bounded sample: each step is one decode step of 8 of the sessions (about
+    # 1.5-2 s of CPU work on 16 cores for config 4), W untimed then K timed
     res = cpu_baseline(cfg, args.ref_sessions, threads, steps=K, warmup=W)
-    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "output tok/s", "n_gpus": args.gpus,
+    line = {"impl": "reference", "metric": cfg["metric"], "value": res["value"], "unit": "output tok/s", "n_gpus": args.gpus,
             "steps": res["steps"], "warmup": W, "ms_per_step": res["step_s"] * 1000.0, "higher_is_better": True,
             "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": dict(bench_config(cfg, args, args.gpus, tp), sessions_sampled=args.ref_sessions,
-                           sample="each step decodes 8 of the 256 sessions on the CPU"),
+                           sample=f"each step decodes {args.ref_sessions} of the {cfg['sessions']} sessions on the CPU"),
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": "output tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -377,8 +403,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default=os.environ.get("SR_BENCH_MODE", "fast"), choices=["exact", "fast"])
-    ap.add_argument("--sessions", type=int, default=CONFIG["sessions"])
-    ap.add_argument("--layers", type=int, default=CONFIG["layers"])
+    ap.add_argument("--config", default="mistral7b", choices=sorted(CONFIGS),
+                    help="mistral7b: 256 ragged requests, Mistral-7B shape, Q8 (the headline); qwen7b: 16 sessions of "
+                         "31,744-token prompts decoding, Qwen2.5-7B shape, q4-mixed")
+    ap.add_argument("--sessions", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--cpu-sessions", type=int, default=8)
     ap.add_argument("--ref-sessions", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -392,9 +421,11 @@ def main():
                     help="mixed prefill chunk of the serving run (1 = the reference default; slower: with any session "
                          "decoding, every prompt advances one token per tick)")
     args = ap.parse_args()
-    cfg = dict(CONFIG)
-    cfg["sessions"] = args.sessions
-    cfg["layers"] = args.layers
+    cfg = dict(CONFIGS[args.config])
+    cfg["sessions"] = args.sessions or cfg["sessions"]
+    cfg["layers"] = args.layers or cfg["layers"]
+    if args.config != "mistral7b":
+        args.no_ttft = True  # the serving run would prefill 16 x 31,744 tokens first
     if args.impl == "reference":
         return run_reference(args, cfg)
     W = max(3, args.warmup)
@@ -469,14 +500,14 @@ def main():
     e2e_val = tokens / (e2e_max / 1000.0)
     if rank == 0:
         peaks, peak_kind = measured_peaks()
-        kvd = cfg["dim"] // cfg["heads"] * cfg["kv_heads"] // (world if tp else 1)  # this rank's KV width
+        kvd = model.kv_dim  # this rank's KV width
         kv_pos_bytes = 2 * kvd * 4  # K + V row of one position, one layer
         attn_launches = launches[5]
         attn_ms = ms[5] / max(1, attn_launches)
         positions = float(np.mean(ctx_trace))  # sum over sessions of (pos+1) per step
         attn_bytes = positions * kv_pos_bytes + 2 * cfg["sessions"] * cfg["dim"] * 4
         achieved = attn_bytes / (attn_ms / 1000.0) / 1e9
-        tr = traffic_per_position()
+        tr = traffic_per_position() if args.config == "mistral7b" else None  # captured on the config-4 shape
         kv_share = kvd / (cfg["dim"] // cfg["heads"] * cfg["kv_heads"])
         traffic = None if tr is None else float(tr["bytes_per_position_layer"] * kv_share * positions +
                                                 tr.get("fixed_bytes", 0))
@@ -485,7 +516,7 @@ def main():
             4 * cfg["sessions"] * cfg["vocab"]
         cls_total = sum(cls_ms) or 1.0
         line = {
-            "metric": METRIC, "value": value, "unit": "output tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "metric": cfg["metric"], "value": value, "unit": "output tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": span_max / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
             "dtype": ("f32; projections bf16 hi+lo x bf16 codes on tensor cores, fp32 accumulate" if args.mode == "fast"

@@ -131,9 +131,15 @@ int sr_model_create(const sr_model_desc *desc, int device, sr_model **out);
  * The step all-reduces (fp32 sum; NCCL, or peer memory after
  * sr_tp_peer_open) after o_proj and down_proj.  nccl_id is
  * the 128-byte id from sr_tp_unique_id on rank 0, shared with every rank;
- * creation blocks until all ranks have joined.  Requires heads, kv_heads and
- * hidden divisible by tp_size (and, for quantized weights, column shards of
- * whole 64-column blocks).  Parameters are still loaded as full tensors. */
+ * creation blocks until all ranks have joined.  Heads: kv_heads divisible by
+ * tp_size (each rank takes kv_heads/tp_size KV heads with all their query
+ * heads), or tp_size divisible by kv_heads with r = tp_size/kv_heads <= the
+ * query heads per KV head: each KV head is then replicated on r consecutive
+ * ranks that split its query heads, the first (group mod r) taking one more
+ * (Qwen2.5-7B, 28/4 heads, on 8 ranks: 4 and 3 query heads of one KV head).
+ * Requires hidden divisible by tp_size and, for quantized weights, column
+ * shards of whole 64-column blocks.  Parameters are still loaded as full
+ * tensors. */
 int sr_model_create_tp(const sr_model_desc *desc, int device, int32_t tp_rank, int32_t tp_size, const void *nccl_id,
                        sr_model **out);
 /* 128-byte NCCL unique id for sr_model_create_tp (call on rank 0). */

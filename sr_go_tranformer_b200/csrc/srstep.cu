@@ -104,6 +104,35 @@ int sr_model_alloc(sr_model* m, void** p, size_t bytes) {
   return SR_OK;
 }
 
+// Heads of tensor-parallel rank `rank` of `size`: query heads [q0, q0 + nq)
+// and KV heads [g0, g0 + nkv).  Either the KV heads divide over the ranks (each
+// takes kv_heads/size of them with all their query heads), or each KV head is
+// replicated on r = size/kv_heads consecutive ranks that split its `group`
+// query heads, the first (group mod r) of them taking one more: Qwen2.5-7B (28
+// query / 4 KV heads) on 8 ranks gives rank 2g+0 query heads 7g..7g+3 and rank
+// 2g+1 heads 7g+4..7g+6, both holding KV head g.  The o_proj all-reduce then
+// still sums every query head's contribution exactly once; the replicated KV
+// projection is computed on both ranks of the pair.
+bool tp_heads(const sr_model_desc& c, int rank, int size, TpHeads* t) {
+  const int G = c.heads / c.kv_heads;
+  if (c.kv_heads % size == 0) {
+    t->nkv = c.kv_heads / size;
+    t->g0 = rank * t->nkv;
+    t->nq = t->nkv * G;
+    t->q0 = t->g0 * G;
+    return true;
+  }
+  if (size % c.kv_heads) return false;
+  const int r = size / c.kv_heads;
+  if (G < r) return false;
+  const int sub = rank % r, base = G / r, extra = G % r;
+  t->nkv = 1;
+  t->g0 = rank / r;
+  t->nq = base + (sub < extra ? 1 : 0);
+  t->q0 = t->g0 * G + sub * base + std::min(sub, extra);
+  return true;
+}
+
 // Validation shared by the single-GPU and tensor-parallel constructors
 // (Config.validateShapeLimits, M:98-118, plus this implementation's limits).
 static int validate_desc(const sr_model_desc& c, int tp_size) {
@@ -133,33 +162,46 @@ static int validate_desc(const sr_model_desc& c, int tp_size) {
   }
   if (tp_size < 1 || tp_size > 64) return sr_fail(SR_EINVAL, "tensor-parallel size must be 1..64");
   if (tp_size > 1) {
-    if (c.heads % tp_size || c.kv_heads % tp_size || c.hidden % tp_size)
-      return sr_fail(SR_EUNSUPPORTED, "tensor parallelism needs heads, kv_heads and hidden divisible by the rank count");
-    if (c.weight_format != SR_FMT_F32 && ((c.heads / tp_size * hd) % kQBlock || (c.hidden / tp_size) % kQBlock))
+    if (c.hidden % tp_size)
+      return sr_fail(SR_EUNSUPPORTED, "tensor parallelism needs hidden divisible by the rank count");
+    if (c.weight_format != SR_FMT_F32 && (c.hidden / tp_size) % kQBlock)
       return sr_fail(SR_EUNSUPPORTED, "tensor-parallel column shards of quantized matrices must hold whole 64-column blocks");
+    for (int r = 0; r < tp_size; r++) {
+      TpHeads t;
+      if (!tp_heads(c, r, tp_size, &t))
+        return sr_fail(SR_EUNSUPPORTED, "tensor parallelism needs kv_heads divisible by the rank count, or the rank "
+                                        "count divisible by kv_heads with at least one query head per rank");
+      if (c.weight_format != SR_FMT_F32 && (t.nq * hd) % kQBlock)
+        return sr_fail(SR_EUNSUPPORTED, "tensor-parallel column shards of quantized matrices must hold whole 64-column blocks");
+    }
   }
   return SR_OK;
 }
 
 // Parameter table in hfProfileSpecs order (M:407-442) for rank `rank` of
 // `size`: Q/K/V/gate/up keep a contiguous block of rows, O/down and the qkv
-// biases a contiguous block of columns; everything else is replicated.
+// biases a contiguous block of columns (the rank's heads from tp_heads, or its
+// 1/size of the FFN); everything else is replicated.
 int sr_param_table(const sr_model_desc& c, int rank, int size, std::vector<Param>* params,
                    std::vector<Shard>* shards) {
   params->clear();
   shards->clear();
   const int hd = c.dim / c.heads, kd = hd * c.kv_heads;
-  auto add = [&](int rows, int cols, bool matrix, bool eh, int kind) {
+  TpHeads th{0, c.heads, 0, c.kv_heads};
+  if (c.arch != SR_ARCH_GPT2 && !tp_heads(c, rank, size, &th)) return SR_EUNSUPPORTED;
+  const int hs = c.hidden / size;
+  // kind 0: replicated; 1: rows [lo, lo + n); 2: columns [lo, lo + n)
+  auto add = [&](int rows, int cols, bool matrix, bool eh, int kind, int lo = 0, int n = 0) {
     Shard sh{rows, cols, 0, 0};
     Param p;
     p.rows = rows;
     p.cols = cols;
     if (kind == 1) {
-      p.rows = rows / size;
-      sh.row0 = rank * p.rows;
+      p.rows = n;
+      sh.row0 = lo;
     } else if (kind == 2) {
-      p.cols = cols / size;
-      sh.col0 = rank * p.cols;
+      p.cols = n;
+      sh.col0 = lo;
     }
     p.format = matrix ? matrix_format(c.weight_format, eh) : kF32;
     p.values = nullptr;
@@ -189,24 +231,25 @@ int sr_param_table(const sr_model_desc& c, int rank, int size, std::vector<Param
     }
     return SR_OK;
   }
+  const int q0 = th.q0 * hd, nq = th.nq * hd, k0 = th.g0 * hd, nk = th.nkv * hd;
   add(c.vocab, d, true, true, 0);
   for (int l = 0; l < L; l++) {
     add(1, d, false, false, 0);
-    add(d, d, true, false, 1);
-    add(kd, d, true, false, 1);
-    add(kd, d, true, false, 1);
-    add(d, d, true, false, 2);
+    add(d, d, true, false, 1, q0, nq);
+    add(kd, d, true, false, 1, k0, nk);
+    add(kd, d, true, false, 1, k0, nk);
+    add(d, d, true, false, 2, q0, nq);
     add(1, d, false, false, 0);
-    add(h, d, true, false, 1);
-    add(h, d, true, false, 1);
-    add(d, h, true, false, 2);
+    add(h, d, true, false, 1, rank * hs, hs);
+    add(h, d, true, false, 1, rank * hs, hs);
+    add(d, h, true, false, 2, rank * hs, hs);
   }
   add(1, d, false, false, 0);
   if (c.qkv_bias)
     for (int l = 0; l < L; l++) {
-      add(1, d, false, false, 2);
-      add(1, kd, false, false, 2);
-      add(1, kd, false, false, 2);
+      add(1, d, false, false, 2, q0, nq);
+      add(1, kd, false, false, 2, k0, nk);
+      add(1, kd, false, false, 2, k0, nk);
     }
   if (!c.tied) add(c.vocab, d, true, true, 0);
   return SR_OK;
@@ -422,7 +465,9 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
   const sr_model_desc& c = *desc;
   int rc = validate_desc(c, tp_size);
   if (rc != SR_OK) return rc;
-  const int hd = c.dim / c.heads, group = c.heads / c.kv_heads;
+  const int hd = c.dim / c.heads;
+  TpHeads th{0, c.heads, 0, c.kv_heads};
+  if (c.arch != SR_ARCH_GPT2) tp_heads(c, tp_rank, tp_size, &th);  // validated above
   int ndev = 0;
   CK(cudaGetDeviceCount(&ndev));
   if (device < 0 || device >= ndev) return sr_fail(SR_EINVAL, "invalid device ordinal");
@@ -437,13 +482,13 @@ static int model_create(const sr_model_desc* desc, int device, int tp_rank, int 
   dm.dim = c.dim;
   dm.hidden = c.hidden / tp_size;
   dm.layers = c.layers;
-  dm.heads = c.heads / tp_size;
-  dm.kv_heads = c.kv_heads / tp_size;
+  dm.heads = th.nq;
+  dm.kv_heads = th.nkv;
   dm.context = c.context;
   dm.hd = hd;
   dm.kvd = hd * dm.kv_heads;
   dm.qd = hd * dm.heads;
-  dm.group = group;
+  dm.group = th.nq / th.nkv;
   dm.tp_rank = tp_rank;
   dm.tp_size = tp_size;
   dm.page_tokens = c.page_tokens;

@@ -106,6 +106,12 @@ struct sr_kvpool {
 };
 
 int sr_fail(int code, const std::string& msg);
+// Heads of one tensor-parallel rank: query heads [q0, q0 + nq), KV heads
+// [g0, g0 + nkv).
+struct TpHeads {
+  int q0, nq, g0, nkv;
+};
+bool tp_heads(const sr_model_desc& c, int rank, int size, TpHeads* t);
 // Parameter table (hfProfileSpecs order) of one tensor-parallel rank.
 int sr_param_table(const sr_model_desc& c, int rank, int size, std::vector<sr::Param>* params,
                    std::vector<Shard>* shards);

@@ -141,8 +141,11 @@ class Model:
 
     @property
     def kv_dim(self):
-        """KV width held on this device (this rank's KV heads)."""
-        return self.desc.dim // self.desc.heads * (self.desc.kv_heads // self.tp_size)
+        """KV width held on this device (this rank's KV heads: the rows of its
+        layer-0 k_proj shard)."""
+        if self.tp_size == 1:
+            return self.desc.dim // self.desc.heads * self.desc.kv_heads
+        return tp_shard(self.desc, self.tp_rank, self.tp_size, 3)[1]
 
     @property
     def page_elements(self):

@@ -45,10 +45,23 @@ def exchange_handles(m, rank, size, folder):
     return [open(p, "rb").read() for p in paths]
 
 
-def _run(rank, size, nccl_id, mode, q, allreduce="nccl", folder=None):
+# Uneven head ownership: every KV head replicated on a pair of ranks that
+# split its query heads (2/1 at 2 and 4 ranks, 4/3 at 8 ranks: the Qwen2.5-7B
+# shape with its real layer dimensions, 2 layers), q/k/v biases, q4-mixed.
+UNEVEN = {
+    2: dict(vocab=2048, dim=384, hidden=1024, layers=2, heads=3, kv_heads=1, context=1024, rope_theta=1e6,
+            tied=False, qkv_bias=True, weight_format="q4-mixed", page_tokens=16),
+    4: dict(vocab=2048, dim=768, hidden=2048, layers=2, heads=6, kv_heads=2, context=1024, rope_theta=1e6,
+            tied=False, qkv_bias=True, weight_format="q4-mixed", page_tokens=16),
+    8: dict(vocab=152064, dim=3584, hidden=18944, layers=2, heads=28, kv_heads=4, context=1024, rope_theta=1e6,
+            tied=False, qkv_bias=True, weight_format="q4-mixed", page_tokens=16),
+}
+
+
+def _run(rank, size, nccl_id, mode, q, allreduce="nccl", folder=None, desc=None):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     from sr_go_tranformer_b200 import step as S
-    d = S.make_desc(**DESC)
+    d = S.make_desc(**(desc or DESC))
     m = S.Model(d, device=rank, tp_rank=rank, tp_size=size, nccl_id=nccl_id)
     m.init_synthetic(123)
     m.set_mode(mode)
@@ -69,13 +82,14 @@ def _run(rank, size, nccl_id, mode, q, allreduce="nccl", folder=None):
     q.put((rank, outs))
 
 
-def _tp_logits(size, mode, allreduce="nccl", folder=None):
+def _tp_logits(size, mode, allreduce="nccl", folder=None, desc=None):
     import multiprocessing as mp
     from sr_go_tranformer_b200 import step as S
     nccl_id = S.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_run, args=(r, size, nccl_id, mode, q, allreduce, folder)) for r in range(size)]
+    procs = [ctx.Process(target=_run, args=(r, size, nccl_id, mode, q, allreduce, folder, desc))
+             for r in range(size)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in procs)
@@ -85,11 +99,11 @@ def _tp_logits(size, mode, allreduce="nccl", folder=None):
     return res
 
 
-def _single_logits(mode):
+def _single_logits(mode, desc=None):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    p = ctx.Process(target=_run, args=(0, 1, None, mode, q))
+    p = ctx.Process(target=_run, args=(0, 1, None, mode, q, "nccl", None, desc))
     p.start()
     r = q.get(timeout=600)
     p.join(timeout=120)
@@ -112,6 +126,30 @@ def test_tp_matches_single_gpu(mode, size, allreduce, tmp_path):
         err = float(np.abs(tp[0][step] - b).max())
         assert err <= ATOL, f"{mode} step {step}: TP{size} logits differ from 1 GPU by {err:.3g}"
         assert (np.argmax(tp[0][step], 1) == np.argmax(b, 1)).mean() >= 0.75
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+@pytest.mark.parametrize("mode", ["exact", "fast"])
+def test_tp_uneven_heads_matches_single_gpu(mode, size, tmp_path):
+    """KV heads replicated on pairs of ranks with their query heads split
+    unevenly (Qwen2.5-7B's 28/4 heads on 8 ranks: 4 and 3 query heads per
+    rank), against the same model on one GPU; NCCL all-reduce, and the peer
+    kernels at 2 ranks."""
+    if _gpus() < size:
+        pytest.skip(f"needs {size} GPUs")
+    desc = UNEVEN[size]
+    single = _single_logits(mode, desc)
+    for allreduce in (["nccl", "peer"] if size == 2 else ["nccl"]):
+        folder = tmp_path / allreduce
+        folder.mkdir()
+        tp = _tp_logits(size, mode, allreduce, str(folder), desc)
+        for step in range(len(single)):
+            b = single[step]
+            for r in range(1, size):
+                assert np.array_equal(tp[0][step], tp[r][step]), "ranks disagree"
+            err = float(np.abs(tp[0][step] - b).max())
+            assert err <= ATOL, f"{mode} {allreduce} step {step}: TP{size} logits differ from 1 GPU by {err:.3g}"
+            assert (np.argmax(tp[0][step], 1) == np.argmax(b, 1)).mean() >= 0.75
 
 
 def _absent_rank(rank, q, folder, done):
