@@ -1,6 +1,7 @@
-// gemv.cuh -- SR_MODE_FAST decode projections for steps of at most kMaxRows
-// rows: Y[n, out] = X[n, in] W[out, in]^T with W in the reference's Q8 / Q4
-// storage (Param, cmd/monolith/monolith.go:3784-3850), read as stored.
+// gemv.cuh -- SR_MODE_FAST decode projections for steps of fewer than 32
+// rows (one launch per kMaxRows rows): Y[n, out] = X[n, in] W[out, in]^T with
+// W in the reference's Q8 / Q4 storage (Param, cmd/monolith/monolith.go:3784-3850),
+// read as stored.
 //
 // linearQ8Into / linearQ4Into (M:4074-4511) restated for a few rows on CUDA
 // cores, bound by the weight bytes:

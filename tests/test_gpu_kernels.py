@@ -186,11 +186,12 @@ def dequant(vals, sc, fmt, rows, cols):
 @pytest.mark.parametrize("fmt", ["q8", "q4"])
 @pytest.mark.parametrize("cols", [64, 576, 4096, 14336])
 def test_fast_decode_gemv(oracle, srlib, fmt, cols):
-    """SR_MODE_FAST projections of 1..8 rows run the decode GEMV (128-bit code
-    loads, dequantisation in registers): down_proj [64, cols] splits K over
-    CTAs (the split-K reduction), gate [cols, 64] and the embedding as a head
-    [256, 64] do not.  Each output must be within 1e-5 of sum_j |x_j w_j| of
-    the exact-order oracle result (fast mode reorders the fp32 sums)."""
+    """SR_MODE_FAST projections of 1..31 rows run the decode GEMV (128-bit code
+    loads, dequantisation in registers; above 8 rows in passes of 8):
+    down_proj [64, cols] splits K over CTAs (the split-K reduction), gate
+    [cols, 64] and the embedding as a head [256, 64] do not.  Each output must
+    be within 1e-5 of sum_j |x_j w_j| of the exact-order oracle result (fast
+    mode reorders the fp32 sums)."""
     dm = model(hidden=cols, fmt=fmt)
     rng = np.random.default_rng(cols + (fmt == "q4"))
     for index, (rows_w, cols_w) in ((DOWN, (64, cols)), (7, (cols, 64)), (EMB, (256, 64))):
@@ -198,7 +199,7 @@ def test_fast_decode_gemv(oracle, srlib, fmt, cols):
         vals, sc = oracle.quantize(w, Q8 if fmt == "q8" else Q4)
         dm.load_param(index, vals, sc)
         wd = np.abs(dequant(vals, sc, fmt, rows_w, cols_w))
-        for n in range(1, 9):
+        for n in list(range(1, 9)) + [9, 16, 17, 31]:
             x = rng.standard_normal((n, cols_w)).astype(np.float32)
             dm.set_mode("exact")
             exact = dm.linear(index, x)
