@@ -43,9 +43,7 @@ struct TcState {
   __nv_bfloat16* xh = nullptr;
   __nv_bfloat16* xl = nullptr;
   CUtensorMap xh_d, xl_d, xh_h, xl_h, xh_q, xl_q;  // operand maps for in = dim, hidden, attention width
-  float* partial = nullptr;   // [sms][kN][kMC] stream-K partial tiles
-  int* flags = nullptr;       // [sms] stream-K publish flags (zeroed once)
-  uint32_t epoch = 0;         // last flag value handed to a launch
+  float* partial = nullptr;   // [sms][2][kN][kMC] stream-K partial tiles
   int sms = 148;
   int* err = nullptr;
   int* h_err = nullptr;
@@ -111,8 +109,6 @@ inline void tc_free(TcState* t) {
   t->gateup.clear();
   t->down.clear();
   t->partial = nullptr;
-  t->flags = nullptr;
-  t->epoch = 0;
 }
 
 inline bool tc_alloc(TcState* t, void** p, size_t bytes) {
@@ -237,15 +233,13 @@ inline bool tc_prepare(sr_model* m) {
   }
   if (!tc_alloc(t, (void**)&t->xh, (size_t)kMaxRows * xcols * 2) ||
       !tc_alloc(t, (void**)&t->xl, (size_t)kMaxRows * xcols * 2) || !tc_alloc(t, (void**)&t->err, 16) ||
-      !tc_alloc(t, (void**)&t->partial, (size_t)t->sms * tc::kN * tc::kMC * 4) ||
-      !tc_alloc(t, (void**)&t->flags, (size_t)t->sms * 4)) {
+      !tc_alloc(t, (void**)&t->partial, (size_t)t->sms * 2 * tc::kN * tc::kMC * 4)) {
     tc_free(t);
     return false;
   }
   cudaMemsetAsync(t->xh, 0, (size_t)kMaxRows * xcols * 2, m->stream);
   cudaMemsetAsync(t->xl, 0, (size_t)kMaxRows * xcols * 2, m->stream);
   cudaMemsetAsync(t->err, 0, 16, m->stream);
-  cudaMemsetAsync(t->flags, 0, (size_t)t->sms * 4, m->stream);
   if (cudaMallocHost((void**)&t->h_err, 16) != cudaSuccess) {
     cudaGetLastError();
     tc_free(t);
@@ -296,39 +290,27 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::Gemm
   const int64_t units = (int64_t)a.mt * a.groups;
   a.ngroups = (int)std::max<int64_t>(1, std::min<int64_t>(t->sms / a.nt, (units + kSkMinUnits - 1) / kSkMinUnits));
   a.partial = t->partial;
-  a.flags = t->flags;
-  if (++t->epoch == 0) t->epoch = 1;  // flags hold earlier epochs or 0
-  a.epoch = t->epoch;
   const CUtensorMap& xh = in_kind == 1 ? t->xh_h : (in_kind == 2 ? t->xh_q : t->xh_d);
   const CUtensorMap& xl = in_kind == 1 ? t->xl_h : (in_kind == 2 ? t->xl_q : t->xl_d);
   a.wt = W.wt;
   a.fmt = W.fmt;
-  // Cooperative launch: the stream-K fixup waits on other CTAs of the grid,
-  // so every CTA must be resident at once (one per SM; the runtime refuses
-  // the launch otherwise instead of letting it wait).
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeCooperative;
-  attr.val.cooperative = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.ngroups * a.nt);
-  cfg.stream = m->stream;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  cudaError_t e;
-  if (W.wt) {
-    cfg.blockDim = dim3(tc::kThreads);
-    cfg.dynamicSmemBytes = tc::kSmemBytes;
-    e = cudaLaunchKernelEx(&cfg, tc::k_gemm_q, xh, xl, a);
-  } else {
-    cfg.blockDim = dim3(tc::kDirThreads);
-    cfg.dynamicSmemBytes = tc::kDirSmemBytes;
-    e = cudaLaunchKernelEx(&cfg, tc::k_gemm_direct, xh, xl, W.map[0], W.map[1], W.map[2], a);
-  }
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
+  if (W.wt)
+    tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, m->stream>>>(xh, xl, a);
+  else
+    tc::k_gemm_direct<<<a.ngroups * a.nt, tc::kDirThreads, tc::kDirSmemBytes, m->stream>>>(xh, xl, W.map[0], W.map[1],
+                                                                                         W.map[2], a);
   sr_count_launch(m);
+  // Tiles left in partial slots: every tile when the epilogue needs the
+  // residual or the head row map, otherwise only tiles cut by a group boundary.
+  bool all = a.out_map != nullptr;
+  for (int sg = 0; sg < a.nseg; sg++) all = all || a.seg[sg].resid != nullptr;
+  if (all) {
+    tc::k_sk_reduce<<<dim3(a.mt * a.nt, tc::kN / tc::kRedBlockRows), tc::kMC, 0, m->stream>>>(a, 0);
+    sr_count_launch(m);
+  } else if (a.ngroups > 1) {
+    tc::k_sk_reduce<<<dim3((a.ngroups - 1) * a.nt, tc::kN / tc::kRedBlockRows), tc::kMC, 0, m->stream>>>(a, 1);
+    sr_count_launch(m);
+  }
   t->ran = true;
   return true;
 }

@@ -1306,7 +1306,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     pending = TpSum();
     bool done;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_qkv(m, l, n, true));
-    if (tc && !done) return sr_fail(SR_EDEVICE, "tensor-core projection could not run (scratch allocation or cooperative launch failed)");
+    if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done && fast) {  // decode GEMV: Q|K|V in one launch
       const Param* w3[3] = {&P[1], &P[2], &P[3]};
       LinearOut o3[3] = {o, o, o};
@@ -1337,7 +1337,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     const float* ores = tp ? nullptr : m->X;
     o.y = oy; o.ldy = d; o.bias = nullptr; o.resid = ores;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_o(m, l, n, a_split, oy, ores));
-    if (tc && !done) return sr_fail(SR_EDEVICE, "tensor-core projection could not run (scratch allocation or cooperative launch failed)");
+    if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->A, n, P[4], o);
     TpSum tsum;
     if (tp) {
@@ -1350,7 +1350,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
               else k_rmsnorm_exact<<<norm_blocks, kNormWarps * 32, 0, s>>>(m->X, nullptr, (const float*)P[5].values, m->N, n, d, eps));
     o.resid = nullptr;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_gateup(m, l, n, true));
-    if (tc && !done) return sr_fail(SR_EDEVICE, "tensor-core projection could not run (scratch allocation or cooperative launch failed)");
+    if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done && fast) {  // decode GEMV: gate|up in one launch
       const Param* w2[2] = {&P[6], &P[7]};
       LinearOut o2[2] = {o, o};
@@ -1373,7 +1373,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     oy = tp ? m->T : m->X;  // the all-reduce above moved m->T to the other buffer
     o.y = oy; o.ldy = d; o.resid = ores;
     SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_down(m, l, n, true, oy, ores));
-    if (tc && !done) return sr_fail(SR_EDEVICE, "tensor-core projection could not run (scratch allocation or cooperative launch failed)");
+    if (tc && !done) return sr_fail(SR_ENOMEM, "tensor-core projection could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->H, n, P[8], o);
     if (tp && (rc = tp_allreduce(m, n, &pending)) != SR_OK) return rc;
   }
@@ -1399,7 +1399,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
     o.out_map = m->meta.head_dst;
     bool done;
     SR_LAUNCH(m, SR_PROF_HEAD, done = tc_h && tc_head(m, info.heads, true));
-    if (tc_h && !done) return sr_fail(SR_EDEVICE, "tensor-core LM head could not run (scratch allocation or cooperative launch failed)");
+    if (tc_h && !done) return sr_fail(SR_ENOMEM, "tensor-core LM head could not run (scratch allocation failed)");
     if (!done) sr_launch_linear(m, m->N, info.heads, head, o, SR_PROF_HEAD);
   }
   CK(cudaGetLastError());

@@ -23,13 +23,8 @@
 //     (a group holds one CTA per 128-row tile, so the CTAs that read the same
 //     weight tile run together and share it in L2); the pipeline runs through
 //     tile boundaries without refilling.  A tile whose blocks span several
-//     groups is finished inside the kernel (stream-K fixup): the groups that
-//     hold its later blocks handle them first and publish a partial tile and
-//     a per-launch flag; the group that holds its first block reaches it last,
-//     waits for those flags (the waits come only at the end of a range, so no
-//     group waits on a group that is itself waiting), adds the partials in
-//     block order (deterministic) and applies bias, residual or the head row
-//     map.
+//     groups leaves one partial sum per group, and k_sk_reduce adds them in
+//     block order (deterministic) and applies the epilogue.
 // Every mbarrier wait is bounded (globaltimer); on expiry the kernel records an
 // error flag, stops waiting and finishes, and the host reports SR_ETIMEOUT.
 #pragma once
@@ -76,9 +71,7 @@ struct GemmArgs {
   int mt, nt;        // 256-feature tiles, 128-row tiles
   int ngroups;       // stream-K groups (nt CTAs each); grid = ngroups * nt
   const float* scales;   // [out][groups] (concatenated for fused segments)
-  float* partial;        // [ngroups*nt][kN][kMC] each CTA's published first segment
-  int* flags;            // [ngroups*nt] = epoch once the CTA's partial is published
-  uint32_t epoch;        // this launch's flag value (never 0, never reused by the next launch)
+  float* partial;        // [ngroups*nt][2][kN][kMC] partial tiles (first / last segment of a CTA)
   const int32_t* out_map;  // compacted head rows -> destination row (never combined with a residual)
   Segment seg[3];
   int nseg;
@@ -248,113 +241,6 @@ __device__ __forceinline__ OutCol out_col(const GemmArgs& a, int o) {
   return c;
 }
 
-// Bounded acquire-wait for flag == want (the stream-K fixup).  Returns false
-// (and raises *err) when it expires or another thread raised the error.
-__device__ __forceinline__ bool flag_wait(const int* flag, int want, int* err) {
-  uint64_t t0 = 0;
-  for (uint32_t it = 0;; it++) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-    if (v == want) return true;
-    if ((it & 15) == 0) {
-      if (*(volatile int*)err) return false;
-      const uint64_t now = globaltimer();
-      if (t0 == 0) t0 = now;
-      else if (now - t0 > kWaitNs) {
-        atomicExch(err, 1);
-        return false;
-      }
-    }
-  }
-}
-
-// End of this CTA's segment of tile m (blocks kb_s..kb_e), run by every
-// epilogue thread (feature f of the tile, acc[] = its kN rows).  Three cases,
-// uniform over the CTA:
-//  * the segment is the tile's tail (kb_s > 0: the CTA's first segment): it
-//    goes to the CTA's partial slot and the slot's flag is raised;
-//  * the segment is the whole tile: stored;
-//  * the segment is the tile's head and later groups hold the rest (the CTA's
-//    last segment): their published partials are added in group (= block)
-//    order, then stored.
-// Stores add the bias, then the residual (y = resid + Wx, resid may alias y),
-// or scatter rows through the head's row map.  acc[] is cleared.
-__device__ __forceinline__ void seg_end(const GemmArgs& a, float (&acc)[kN], int m, int kb_s, int kb_e, int f,
-                                        int n0, bool ok, bool leader) {
-  const int K = a.groups, units = a.mt * K;
-  const int g = blockIdx.x / a.nt, j = blockIdx.x % a.nt;
-  const int lane = threadIdx.x & 31;
-  const int o = m * kMC + f;
-  const bool publish = kb_s > 0;
-  if (!publish && kb_e < K - 1) {  // finish: add the later groups' partials
-    const int gl = sk_group_of(m * K + K - 1, units, a.ngroups);
-    if (lane == 0)
-      for (int gs = g + 1; gs <= gl; gs++) ok = flag_wait(a.flags + gs * a.nt + j, (int)a.epoch, a.err) && ok;
-    __syncwarp();
-    // chunks of 8 rows outside, groups inside: few registers beyond acc[],
-    // and each element still adds the groups in order
-#pragma unroll
-    for (int c = 0; c < kN; c += 8) {
-      for (int gs = g + 1; gs <= gl; gs++) {
-        const float* P = a.partial + (int64_t)(gs * a.nt + j) * kN * kMC + (int64_t)c * kMC + f;
-        float v[8];
-#pragma unroll
-        for (int jj = 0; jj < 8; jj++) v[jj] = __ldcg(P + jj * kMC);
-#pragma unroll
-        for (int jj = 0; jj < 8; jj++) acc[c + jj] += v[jj];
-      }
-    }
-  }
-  // One store loop over (dst, ld, nr), as in a plain tile: bias and residual
-  // are added by their own uniform loops first (resid + x == x + resid).
-  float* dst = a.partial + (int64_t)blockIdx.x * kN * kMC + f;
-  int ld = kMC;
-  int nr = kN;
-  const int32_t* map = nullptr;
-  if (!publish) {
-    nr = 0;
-    if (o < a.out) {
-      const OutCol oc = out_col(a, o);
-      nr = min(kN, a.n - n0);
-      ld = oc.ldy;
-      dst = oc.y + (int64_t)n0 * ld;
-      if (oc.has_bias) {
-#pragma unroll
-        for (int jj = 0; jj < kN; jj++) acc[jj] += oc.bias;
-      }
-      if (oc.resid) {
-        const float* rs = oc.resid + (int64_t)n0 * ld;
-#pragma unroll
-        for (int jj = 0; jj < kN; jj++)
-          if (jj < nr) acc[jj] += rs[jj * ld];
-      }
-      if (a.out_map) {
-        map = a.out_map + n0;
-        dst = oc.y;
-      }
-    }
-  }
-  if (map) {
-#pragma unroll
-    for (int jj = 0; jj < kN; jj++) {
-      if (jj < nr) dst[(int64_t)map[jj] * ld] = acc[jj];
-      acc[jj] = 0.f;
-    }
-  } else {
-#pragma unroll
-    for (int jj = 0; jj < kN; jj++) {
-      if (jj < nr) dst[jj * ld] = acc[jj];
-      acc[jj] = 0.f;
-    }
-  }
-  if (publish) {
-    __threadfence();
-    asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");  // all epilogue warps have written
-    if (leader)
-      asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(a.flags + blockIdx.x), "r"((int)a.epoch) : "memory");
-  }
-}
-
 // grid: ngroups * nt CTAs, one per SM (197 KiB of shared memory each).
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_q(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl, GemmArgs a) {
@@ -480,7 +366,43 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUte
         }
       }
       if (kb != K - 1 && i != nu - 1) continue;
-      seg_end(a, acc, m, kb_s, kb, f, n0, ok, threadIdx.x == kEpiWarp0 * 32);
+      const int kb_e = kb;
+      // ---- the group's segment of tile (m, j) ends here.  A whole tile that
+      // needs only a bias goes straight to the output; every other segment
+      // goes to this CTA's partial slot (first segment: 0, later ones: 1) for
+      // k_sk_reduce.  (This store shape keeps acc[] in registers: a per-element
+      // select of the bias, or a dynamic row bound inside the loop, did not.)
+      const bool whole = (kb_s == 0 && kb_e == K - 1);
+      bool direct = false;
+      float* dst;
+      int ld;
+      bool hb = false;
+      float bias = 0.f;
+      if (whole && o < a.out) {
+        const OutCol oc = out_col(a, o);
+        direct = !oc.resid && !a.out_map;
+        if (direct) {
+          dst = oc.y + (int64_t)n0 * oc.ldy;
+          ld = oc.ldy;
+          hb = oc.has_bias;
+          bias = oc.bias;
+        }
+      }
+      if (!direct) {
+        dst = a.partial + ((int)blockIdx.x * 2 + ((m == m_first) ? 0 : 1)) * kN * kMC + f;
+        ld = kMC;
+      }
+      const bool write = direct || !whole || o < a.out;
+      const int nr = write ? min(kN, a.n - n0) : 0;
+      if (hb) {
+#pragma unroll
+        for (int jj = 0; jj < kN; jj++) acc[jj] += bias;
+      }
+#pragma unroll
+      for (int jj = 0; jj < kN; jj++) {
+        if (jj < nr) dst[jj * ld] = acc[jj];
+        acc[jj] = 0.f;
+      }
     }
   }
   tc_fence_before();
@@ -488,6 +410,89 @@ k_gemm_q(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUte
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kAcc * kMH * kN));
+  }
+}
+
+// Tiles a stream-K launch left in partial slots (split tiles, and whole tiles
+// that need the residual or the head row map): out[row][o] = the groups'
+// partials added in block order, then bias / residual / head row map.
+// grid (tiles*nt, kN/kRedBlockRows), block kMC threads (one output feature
+// each) over kRedBlockRows rows in chunks of kRedRows.
+// by_boundary: blockIdx.x / nt is a group boundary b (1..ngroups-1) and the
+// block finishes the tile it cuts (once per tile: at its first inner
+// boundary); otherwise blockIdx.x / nt is the tile.  The partials of up to 8
+// groups for a chunk are loaded before any add.
+constexpr int kRedRows = 8;
+constexpr int kRedBlockRows = 32;
+__global__ void __launch_bounds__(kMC, 2) k_sk_reduce(GemmArgs a, int by_boundary) {
+  const int K = a.groups, units = a.mt * K;
+  const int j = blockIdx.x % a.nt;
+  int m = blockIdx.x / a.nt;
+  if (by_boundary) {
+    const int bnd = m + 1, u = sk_begin(bnd, units, a.ngroups);
+    m = u / K;
+    if (u == m * K) return;                                              // boundary on a tile edge
+    if (bnd > 1 && sk_begin(bnd - 1, units, a.ngroups) > m * K) return;  // tile owned by an earlier boundary
+  }
+  const int gf = sk_group_of(m * K, units, a.ngroups), gl = sk_group_of(m * K + K - 1, units, a.ngroups);
+  const int f = threadIdx.x, o = m * kMC + f;
+  const int n0 = j * kN;
+  if (o >= a.out) return;
+  const OutCol oc = out_col(a, o);
+  if (gf == gl && !oc.resid && !a.out_map) return;  // the GEMM stored this tile
+  const int ns = gl - gf + 1;
+  int off[8];  // partial slot of each group (first segment of a group: slot 0)
+#pragma unroll
+  for (int q = 0; q < 8; q++) {
+    const int gs = min(gf + q, gl);
+    const int sl = (sk_begin(gs, units, a.ngroups) / K == m) ? 0 : 1;
+    off[q] = ((gs * a.nt + j) * 2 + sl) * kN * kMC + f;
+  }
+  for (int r0 = blockIdx.y * kRedBlockRows; r0 < (int)(blockIdx.y + 1) * kRedBlockRows && n0 + r0 < a.n;
+       r0 += kRedRows) {
+    float v[kRedRows];
+#pragma unroll
+    for (int jj = 0; jj < kRedRows; jj++) v[jj] = 0.f;
+    if (ns <= 8) {
+      float p[8][kRedRows];
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+#pragma unroll
+        for (int jj = 0; jj < kRedRows; jj++) p[q][jj] = (q < ns) ? __ldcg(a.partial + off[q] + (r0 + jj) * kMC) : 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; q++)
+#pragma unroll
+        for (int jj = 0; jj < kRedRows; jj++)
+          if (q < ns) v[jj] += p[q][jj];
+    } else {
+      for (int gs = gf; gs <= gl; gs++) {
+        const int sl = (sk_begin(gs, units, a.ngroups) / K == m) ? 0 : 1;
+        const float* P = a.partial + ((gs * a.nt + j) * 2 + sl) * kN * kMC + r0 * kMC + f;
+#pragma unroll
+        for (int jj = 0; jj < kRedRows; jj++) v[jj] += __ldcg(P + jj * kMC);
+      }
+    }
+    float pre[kRedRows];
+#pragma unroll
+    for (int jj = 0; jj < kRedRows; jj++) {
+      const int row = n0 + r0 + jj;
+      pre[jj] = 0.f;
+      if (row < a.n) {
+        if (a.out_map) pre[jj] = __int_as_float(a.out_map[row]);
+        else if (oc.resid) pre[jj] = oc.resid[(int64_t)row * oc.ldy];
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < kRedRows; jj++) {
+      const int row = n0 + r0 + jj;
+      if (row < a.n) {
+        const int64_t orow = a.out_map ? (int64_t)__float_as_int(pre[jj]) : (int64_t)row;
+        float x = v[jj];
+        if (oc.has_bias) x += oc.bias;
+        if (oc.resid) x = pre[jj] + x;
+        oc.y[orow * oc.ldy] = x;
+      }
+    }
   }
 }
 

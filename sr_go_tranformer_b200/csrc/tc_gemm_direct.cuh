@@ -11,7 +11,7 @@
 //     places the biased code in a float's mantissa and one subtraction removes
 //     the bias) in the MMA's 128-byte swizzled K-major layout, into one of two A
 //     tiles;
-//   * MMA, epilogue and the stream-K schedule with its in-kernel fixup are k_gemm_q's.
+//   * MMA, epilogue, stream-K schedule and k_sk_reduce are k_gemm_q's.
 // It needs no device memory beyond the model's own codes, but moves about 224
 // KiB through shared memory per (256-feature, 128-row, 64-column) unit against
 // k_gemm_q's 192 KiB (the widening reads 16 and writes 32 KiB), so it runs
@@ -154,7 +154,7 @@ __device__ __forceinline__ bool dir_convert(const GemmArgs& a, int u, int ct) {
 
 // grid: ngroups * nt CTAs, one per SM.  tm_w*: the segments' code maps
 // (uint8, box kDirSub rows x one block's bytes), tm_x*: the activation planes.
-// Same epilogue, partial slots and flags as k_gemm_q.
+// Leaves the same partial slots as k_gemm_q for k_sk_reduce.
 __global__ void __launch_bounds__(kDirThreads, 1)
 k_gemm_direct(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
               const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
@@ -264,8 +264,8 @@ k_gemm_direct(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__
     for (int u = 0; u < nu; u++)
       if (!dir_convert(a, u, ct)) break;
   } else {  // epilogue warps 4..11: TMEM lane quarter = warp % 4, MMA half = (warp - 4) / 4
-    // k_gemm_q's epilogue (per-block scale FMAs, then seg_end: the stream-K
-    // fixup and the stores)
+    // k_gemm_q's epilogue (per-block scale FMAs; whole plain tiles stored,
+    // the rest to the CTA's partial slots for k_sk_reduce)
     const int q = warp & 3, h = (warp - kDirEpiWarp0) >> 2;
     const int f = h * kM + q * 32 + lane;  // feature within the tile
     bool ok = true;
@@ -305,7 +305,38 @@ k_gemm_direct(const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__
         }
       }
       if (kb != K - 1 && i != nu - 1) continue;
-      seg_end(a, acc, m, kb_s, kb, f, n0, ok, threadIdx.x == kDirEpiWarp0 * 32);
+      const int kb_e = kb;
+      const bool whole = (kb_s == 0 && kb_e == K - 1);
+      bool direct = false;
+      float* dst;
+      int ld;
+      bool hb = false;
+      float bias = 0.f;
+      if (whole && o < a.out) {
+        const OutCol oc = out_col(a, o);
+        direct = !oc.resid && !a.out_map;
+        if (direct) {
+          dst = oc.y + (int64_t)n0 * oc.ldy;
+          ld = oc.ldy;
+          hb = oc.has_bias;
+          bias = oc.bias;
+        }
+      }
+      if (!direct) {
+        dst = a.partial + ((int)blockIdx.x * 2 + ((m == m_first) ? 0 : 1)) * kN * kMC + f;
+        ld = kMC;
+      }
+      const bool write = direct || !whole || o < a.out;
+      const int nr = write ? min(kN, a.n - n0) : 0;
+      if (hb) {
+#pragma unroll
+        for (int jj = 0; jj < kN; jj++) acc[jj] += bias;
+      }
+#pragma unroll
+      for (int jj = 0; jj < kN; jj++) {
+        if (jj < nr) dst[jj * ld] = acc[jj];
+        acc[jj] = 0.f;
+      }
     }
   }
   tc_fence_before();
