@@ -13,6 +13,9 @@ hold each session's prompt and the decode tokens before its starting offset
 (synthetic values: a prefilled cache); offsets are uniform in the session's
 output budget so contexts are ragged, as in a running server.
 
+With --split, a one-GPU fast step of at least 128 rows runs as two halves on two SM
+partitions (green contexts), so one half's attention overlaps the other
+half's projections (`--split`; `config.step_halves` = 2).
 `value`   = output tokens / s over all ranks from the device span of each step
             (first to last kernel, CUDA events on the library's stream).
 `e2e`     = the same metric through the C ABI call sr_step_sample with host
@@ -417,6 +420,9 @@ def main():
                          "peer-ll: flags inside the data, one kernel), NCCL, or auto (peer at 2 ranks, NCCL above: the "
                          "faster one measured at each size)")
     ap.add_argument("--no-ttft", action="store_true", help="skip the serving run (TTFT, ITL, stream tok/s)")
+    ap.add_argument("--split", action="store_true",
+                    help="run a one-GPU fast step of >= 128 rows as two halves on two SM partitions, overlapping one "
+                         "half's attention with the other's projections")
     ap.add_argument("--stream-mixed-chunk", type=int, default=1024,
                     help="mixed prefill chunk of the serving run (1 = the reference default; slower: with any session "
                          "decoding, every prompt advances one token per tick)")
@@ -448,6 +454,7 @@ def main():
             dist.broadcast_object_list(obj, src=0)
             tp_args = (rank, world, obj[0])
     model = make_model(cfg, local, args.mode, tp=tp_args)
+    model.set_split(args.split)
     if args.allreduce == "auto":
         args.allreduce = "peer" if world == 2 else "nccl"
     if tp and args.allreduce in ("peer", "peer-ll"):
@@ -505,12 +512,14 @@ def main():
         attn_launches = launches[5]
         attn_ms = ms[5] / max(1, attn_launches)
         positions = float(np.mean(ctx_trace))  # sum over sessions of (pos+1) per step
-        attn_bytes = positions * kv_pos_bytes + 2 * cfg["sessions"] * cfg["dim"] * 4
+        # a launch covers one layer of the whole step, or of one half of a split step
+        halves = max(1, round(attn_launches / max(1, cfg["layers"] * K)))
+        attn_bytes = (positions * kv_pos_bytes + 2 * cfg["sessions"] * cfg["dim"] * 4) / halves
         achieved = attn_bytes / (attn_ms / 1000.0) / 1e9
         tr = traffic_per_position() if args.config == "mistral7b" else None  # captured on the config-4 shape
         kv_share = kvd / (cfg["dim"] // cfg["heads"] * cfg["kv_heads"])
         traffic = None if tr is None else float(tr["bytes_per_position_layer"] * kv_share * positions +
-                                                tr.get("fixed_bytes", 0))
+                                                tr.get("fixed_bytes", 0)) / halves
         wbytes = weight_bytes(cfg) / (world if tp else 1)  # this rank's share (embedding/head replicated: approx)
         step_bytes = wbytes + cfg["layers"] * (positions * kv_pos_bytes + cfg["sessions"] * kv_pos_bytes) + \
             4 * cfg["sessions"] * cfg["vocab"]
@@ -522,7 +531,7 @@ def main():
             "dtype": ("f32; projections bf16 hi+lo x bf16 codes on tensor cores, fp32 accumulate" if args.mode == "fast"
                       else "f32"),
             "data": "synthetic",
-            "config": bench_config(cfg, args, world, tp),
+            "config": dict(bench_config(cfg, args, world, tp), step_halves=halves),
             "itl_p50_ms": span_max / K, "ttft_p50_ms": ttft["ttft_p50_ms"] if ttft else None,
             "stream_output_tok_s": ttft["stream_output_tok_s"] if ttft else None,
             "hbm_gbs_step": step_bytes / (span_max / K / 1000.0) / 1e9,

@@ -213,6 +213,15 @@ int sr_model_set_mode(sr_model *m, int32_t mode);
  * use (building it if enabled). */
 int sr_model_set_code_cache(sr_model *m, int32_t enabled);
 int sr_model_code_cache(sr_model *m, int32_t *cached);
+/* Split steps (no counterpart in the reference, which runs on CPU cores):
+ * with enabled = 1, a SR_MODE_FAST step on one GPU whose rows can
+ * be cut at a session boundary into two halves of 64..512 rows runs as those
+ * two halves on two SM partitions of the GPU (CUDA green contexts, made on the
+ * first such step), so that one half's projections run while the other half's
+ * attention reads its KV pages.  Per-row results equal the unsplit fast step's
+ * within the fast-mode tolerance (the projections' partial sums are grouped
+ * differently).  0 (the default) runs every step whole. */
+int sr_model_set_split(sr_model *m, int32_t enabled);
 
 /* ---------------------------------------------------------------- KV pool */
 /* Device page pool holding num_pages pages of 2*page_tokens*kvDim*layers fp32

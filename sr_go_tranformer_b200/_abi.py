@@ -32,7 +32,7 @@ EXPORTED = [
     "sr_kvpool_copy_rows", "sr_engine_clear_prefix", "sr_tp_peer_handle", "sr_tp_peer_open",
     "sr_text_decoder_create", "sr_text_decoder_destroy", "sr_text_decoder_push", "sr_text_decoder_push_token",
     "sr_tp_peer_set_protocol", "sr_engine_set_pieces", "sr_engine_poll_token", "sr_sample_logits",
-    "sr_linear", "sr_model_set_code_cache", "sr_model_code_cache",
+    "sr_linear", "sr_model_set_code_cache", "sr_model_code_cache", "sr_model_set_split",
 ]
 PROF_CLASSES = ["meta", "embed", "norm", "linear", "rope_kv", "attention", "swiglu", "head", "sample"]
 
@@ -139,6 +139,7 @@ def lib():
         "sr_linear": (C.c_int, [P, I32, I32, P, P]),
         "sr_model_set_code_cache": (C.c_int, [P, I32]),
         "sr_model_code_cache": (C.c_int, [P, C.POINTER(I32)]),
+        "sr_model_set_split": (C.c_int, [P, I32]),
         "sr_step_sample": (C.c_int, [P, P, C.POINTER(Batch), P, P, P, P, I32, P]),
         "sr_engine_create": (C.c_int, [P, C.POINTER(EngineConfig), C.POINTER(P)]),
         "sr_engine_destroy": (C.c_int, [P]),

@@ -437,8 +437,8 @@ k_linear_f32_exact(const float* __restrict__ X, int n, int in, int out, Param W,
 // are written into the row's page (KVCache.row M:6038-6043, copy M:6393-6395).
 __global__ void k_rope_kv_exact(float* __restrict__ Q, const float* __restrict__ K, const float* __restrict__ V,
                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t, StepMeta meta,
-                                float* __restrict__ pool, ModelDims dm, int layer) {
-  const int r = blockIdx.x;
+                                float* __restrict__ pool, ModelDims dm, int layer, int row0) {
+  const int r = row0 + blockIdx.x;  // row0: first row of a split step's half (else 0)
   const int pos = meta.row_pos[r];
   const int half = dm.hd / 2;
   const float* ct = cos_t + (int64_t)pos * half;

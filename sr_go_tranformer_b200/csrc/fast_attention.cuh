@@ -44,6 +44,10 @@ struct FastAttnArgs {
   op16* xh;  // optional: write the output as bf16 hi/lo planes (the next
   op16* xl;  // projection's tensor-core operand) instead of fp32 A
   int* err;           // raised when a bounded wait for a tile expires
+  // One half of a split step: its first row and its first entries of the
+  // single / group / item lists (all zero for a whole step).  The combine
+  // runs over the half's rows and writes the planes from the half's row 0.
+  int row0 = 0, single0 = 0, grp0 = 0, item0 = 0;
 };
 
 // One fp32 activation as the projection's two bf16 operand terms:
@@ -200,7 +204,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_warp128(FastAttnArgs a) {
   constexpr int HD = 128, MT = kWpMT;
   constexpr int ROUNDS = (G + 3) / 4;  // softmax passes: 4 heads x 8 positions per pass
   extern __shared__ __align__(16) float fsm[];
-  const int rs = a.meta.single_rs[blockIdx.x], kh = blockIdx.y;
+  const int rs = a.meta.single_rs[a.single0 + blockIdx.x], kh = blockIdx.y;
   const int r = rs >> 16, split = rs & 0xffff;
   const int L = a.meta.row_pos[r] + 1;
   const int s0 = split * kFaSplit;
@@ -349,7 +353,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_rows128(FastAttnArgs a) {
   constexpr int HD = 128, RT = kRwTile, NS = kRwStages;
   constexpr int ROUNDS = (G + 3) / 4;
   extern __shared__ __align__(16) float fsm[];
-  const int gr = a.meta.grp_rs[blockIdx.x], kh = blockIdx.y;
+  const int gr = a.meta.grp_rs[a.grp0 + blockIdx.x], kh = blockIdx.y;
   const int r0 = gr >> 16, nr = ((gr >> 13) & 7) + 1, split = gr & 0x1fff;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int s0 = split * kFaSplit;
@@ -495,7 +499,7 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
 __global__ void __launch_bounds__(kMmWarps * 32) k_attn_mma128(FastAttnArgs a) {
   constexpr int HD = 128, T = kMmTile, ST = kMmStride, G = 4;
   extern __shared__ __align__(16) float fsm[];
-  const int gr = a.meta.grp_rs[blockIdx.x], kh = blockIdx.y;
+  const int gr = a.meta.grp_rs[a.grp0 + blockIdx.x], kh = blockIdx.y;
   const int r0 = gr >> 16, nr = ((gr >> 13) & 7) + 1, split = gr & 0x1fff;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
@@ -730,7 +734,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_tile(FastAttnArgs a) {
   float* l_s = m_s + GP;                    // [GP]
   float* red = fsm;                         // reuses the tiles after the loop
 
-  const int rs = a.meta.item_rs[blockIdx.x], kh = blockIdx.y;
+  const int rs = a.meta.item_rs[a.item0 + blockIdx.x], kh = blockIdx.y;
   const int r = rs >> 16, split = rs & 0xffff;
   const int L = a.meta.row_pos[r] + 1;
   const int s0 = split * kFaSplit;
@@ -853,7 +857,7 @@ __global__ void __launch_bounds__(kFaThreads) k_attn_tile(FastAttnArgs a) {
 // Merge the splits of each (row, query head) and write the attention output.
 template <int HD>
 __global__ void __launch_bounds__(HD) k_attn_combine(FastAttnArgs a) {
-  const int r = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int r = a.row0 + blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int G = a.dm.group, kh = h / G, g = h % G;
   const int L = a.meta.row_pos[r] + 1;
   const int ns = (L + kFaSplit - 1) / kFaSplit;
@@ -885,11 +889,13 @@ __global__ void __launch_bounds__(HD) k_attn_combine(FastAttnArgs a) {
     }
     M = Mc;
   }
-  const int64_t o = (int64_t)r * a.dm.qd + (int64_t)h * HD + d;
-  if (a.xh)
+  const int64_t hd_off = (int64_t)h * HD + d;
+  if (a.xh) {
+    const int64_t o = (int64_t)blockIdx.x * a.dm.qd + hd_off;  // the planes start at the half's row 0
     split_op(num / den, a.xh + o, a.xl + o);
-  else
-    a.A[o] = num / den;
+  } else {
+    a.A[(int64_t)r * a.dm.qd + hd_off] = num / den;
+  }
 }
 
 template <int HD, int G>

@@ -42,8 +42,12 @@ struct TcState {
   TcMatrix head;
   __nv_bfloat16* xh = nullptr;
   __nv_bfloat16* xl = nullptr;
-  CUtensorMap xh_d, xl_d, xh_h, xl_h, xh_q, xl_q;  // operand maps for in = dim, hidden, attention width
-  float* partial = nullptr;   // [sms][2][kN][kMC] stream-K partial tiles
+  // Operand maps for in = dim, hidden, attention width, per plane slot: slot
+  // 0 starts at row 0 of the planes (a whole step, or the first half of a
+  // split step), slot 1 at row kLaneRows (the second half).
+  CUtensorMap xh_d[2], xl_d[2], xh_h[2], xl_h[2], xh_q[2], xl_q[2];
+  int xcols = 0;              // row stride bound of the planes: max(dim, hidden, attention width)
+  float* partial[2] = {nullptr, nullptr};  // per slot: [sms][2][kN][kMC] stream-K partial tiles
   int sms = 148;
   int* err = nullptr;
   int* h_err = nullptr;
@@ -99,6 +103,17 @@ inline bool make_code_map(CUtensorMap* map, const Param& p) {
 
 inline TcState* tc_state(sr_model* m) { return (TcState*)m->tc; }
 
+// (kLaneRows: the second half of a split step has its operand planes from
+// that row of the plane buffers on.)
+// One half of a split step: its stream, operand-plane slot (0 or 1), the SM
+// count of its partition and its first step row.
+struct TcLane {
+  cudaStream_t s;
+  int slot;
+  int sms;
+  int row0;
+};
+
 inline void tc_free(TcState* t) {
   for (void* p : t->allocs) cudaFree(p);
   t->allocs.clear();
@@ -108,7 +123,7 @@ inline void tc_free(TcState* t) {
   t->o.clear();
   t->gateup.clear();
   t->down.clear();
-  t->partial = nullptr;
+  t->partial[0] = t->partial[1] = nullptr;
 }
 
 inline bool tc_alloc(TcState* t, void** p, size_t bytes) {
@@ -233,7 +248,8 @@ inline bool tc_prepare(sr_model* m) {
   }
   if (!tc_alloc(t, (void**)&t->xh, (size_t)kMaxRows * xcols * 2) ||
       !tc_alloc(t, (void**)&t->xl, (size_t)kMaxRows * xcols * 2) || !tc_alloc(t, (void**)&t->err, 16) ||
-      !tc_alloc(t, (void**)&t->partial, (size_t)t->sms * 2 * tc::kN * tc::kMC * 4)) {
+      !tc_alloc(t, (void**)&t->partial[0], (size_t)t->sms * 2 * tc::kN * tc::kMC * 4) ||
+      !tc_alloc(t, (void**)&t->partial[1], (size_t)t->sms * 2 * tc::kN * tc::kMC * 4)) {
     tc_free(t);
     return false;
   }
@@ -245,12 +261,19 @@ inline bool tc_prepare(sr_model* m) {
     tc_free(t);
     return false;
   }
-  if (!make_map(&t->xh_d, t->xh, dm.dim, kMaxRows, tc::kN) || !make_map(&t->xl_d, t->xl, dm.dim, kMaxRows, tc::kN) ||
-      !make_map(&t->xh_h, t->xh, dm.hidden, kMaxRows, tc::kN) ||
-      !make_map(&t->xl_h, t->xl, dm.hidden, kMaxRows, tc::kN) || !make_map(&t->xh_q, t->xh, dm.qd, kMaxRows, tc::kN) ||
-      !make_map(&t->xl_q, t->xl, dm.qd, kMaxRows, tc::kN)) {
-    tc_free(t);
-    return false;
+  t->xcols = xcols;
+  for (int sl = 0; sl < 2; sl++) {
+    const size_t off = (size_t)sl * kLaneRows * xcols;
+    const uint64_t rows = sl == 0 ? kMaxRows : kLaneRows;
+    if (!make_map(&t->xh_d[sl], t->xh + off, dm.dim, rows, tc::kN) ||
+        !make_map(&t->xl_d[sl], t->xl + off, dm.dim, rows, tc::kN) ||
+        !make_map(&t->xh_h[sl], t->xh + off, dm.hidden, rows, tc::kN) ||
+        !make_map(&t->xl_h[sl], t->xl + off, dm.hidden, rows, tc::kN) ||
+        !make_map(&t->xh_q[sl], t->xh + off, dm.qd, rows, tc::kN) ||
+        !make_map(&t->xl_q[sl], t->xl + off, dm.qd, rows, tc::kN)) {
+      tc_free(t);
+      return false;
+    }
   }
   if (cudaStreamSynchronize(m->stream) != cudaSuccess) {
     cudaGetLastError();
@@ -276,8 +299,10 @@ inline void tc_split_x(sr_model* m, const float* X, int n, int in) {
 // Stream-K schedule: groups of nt CTAs (one per 128-row tile) fill the SMs,
 // each group taking at least kSkMinUnits (tile, block) units.
 constexpr int kSkMinUnits = 4;
-inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::GemmArgs a) {
+inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::GemmArgs a, const TcLane* lane = nullptr) {
   TcState* t = tc_state(m);
+  const int slot = lane ? lane->slot : 0, sms = lane ? lane->sms : t->sms;
+  cudaStream_t stream = lane ? lane->s : m->stream;
   a.n = n;
   a.out = W.rows;
   a.in = W.cols;
@@ -286,29 +311,29 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::Gemm
   a.err = t->err;
   a.mt = (W.rows + tc::kMC - 1) / tc::kMC;
   a.nt = (n + tc::kN - 1) / tc::kN;
-  if (a.nt > t->sms || (int64_t)a.mt * a.groups * t->sms >= ((int64_t)1 << 31)) return false;  // 32-bit schedule math
+  if (a.nt > sms || (int64_t)a.mt * a.groups * sms >= ((int64_t)1 << 31)) return false;  // 32-bit schedule math
   const int64_t units = (int64_t)a.mt * a.groups;
-  a.ngroups = (int)std::max<int64_t>(1, std::min<int64_t>(t->sms / a.nt, (units + kSkMinUnits - 1) / kSkMinUnits));
-  a.partial = t->partial;
-  const CUtensorMap& xh = in_kind == 1 ? t->xh_h : (in_kind == 2 ? t->xh_q : t->xh_d);
-  const CUtensorMap& xl = in_kind == 1 ? t->xl_h : (in_kind == 2 ? t->xl_q : t->xl_d);
+  a.ngroups = (int)std::max<int64_t>(1, std::min<int64_t>(sms / a.nt, (units + kSkMinUnits - 1) / kSkMinUnits));
+  a.partial = t->partial[slot];
+  const CUtensorMap& xh = in_kind == 1 ? t->xh_h[slot] : (in_kind == 2 ? t->xh_q[slot] : t->xh_d[slot]);
+  const CUtensorMap& xl = in_kind == 1 ? t->xl_h[slot] : (in_kind == 2 ? t->xl_q[slot] : t->xl_d[slot]);
   a.wt = W.wt;
   a.fmt = W.fmt;
   if (W.wt)
-    tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, m->stream>>>(xh, xl, a);
+    tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, stream>>>(xh, xl, a);
   else
-    tc::k_gemm_direct<<<a.ngroups * a.nt, tc::kDirThreads, tc::kDirSmemBytes, m->stream>>>(xh, xl, W.map[0], W.map[1],
-                                                                                         W.map[2], a);
+    tc::k_gemm_direct<<<a.ngroups * a.nt, tc::kDirThreads, tc::kDirSmemBytes, stream>>>(xh, xl, W.map[0], W.map[1],
+                                                                                       W.map[2], a);
   sr_count_launch(m);
   // Tiles left in partial slots: every tile when the epilogue needs the
   // residual or the head row map, otherwise only tiles cut by a group boundary.
   bool all = a.out_map != nullptr;
   for (int sg = 0; sg < a.nseg; sg++) all = all || a.seg[sg].resid != nullptr;
   if (all) {
-    tc::k_sk_reduce<<<dim3(a.mt * a.nt, tc::kN / tc::kRedBlockRows), tc::kMC, 0, m->stream>>>(a, 0);
+    tc::k_sk_reduce<<<dim3(a.mt * a.nt, tc::kN / tc::kRedBlockRows), tc::kMC, 0, stream>>>(a, 0);
     sr_count_launch(m);
   } else if (a.ngroups > 1) {
-    tc::k_sk_reduce<<<dim3((a.ngroups - 1) * a.nt, tc::kN / tc::kRedBlockRows), tc::kMC, 0, m->stream>>>(a, 1);
+    tc::k_sk_reduce<<<dim3((a.ngroups - 1) * a.nt, tc::kN / tc::kRedBlockRows), tc::kMC, 0, stream>>>(a, 1);
     sr_count_launch(m);
   }
   t->ran = true;
@@ -333,50 +358,64 @@ inline __nv_bfloat16* tc_xl(sr_model* m) { return tc_state(m)->xl; }
 
 // Q|K|V in one GEMM (+ qwen2 biases).  presplit: the producer already wrote
 // the operand planes.
-inline bool tc_qkv(sr_model* m, int l, int n, bool presplit = false) {
+// With a lane (one half of a split step), n is the half's row count, the
+// operand planes are the lane's slot and the outputs start at row lane->row0.
+inline bool tc_qkv(sr_model* m, int l, int n, bool presplit = false, const TcLane* lane = nullptr) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
   const ModelDims& dm = m->dm;
   const Param* B = m->d.qkv_bias ? &m->params[2 + 9 * dm.layers + 3 * l] : nullptr;
+  const int64_t r0 = lane ? lane->row0 : 0;
   tc::GemmArgs a{};
   a.nseg = 3;
-  a.seg[0] = seg(dm.qd, m->Q, dm.qd, B ? (const float*)B[0].values : nullptr, nullptr);
-  a.seg[1] = seg(dm.kvd, m->K, dm.kvd, B ? (const float*)B[1].values : nullptr, nullptr);
-  a.seg[2] = seg(dm.kvd, m->V, dm.kvd, B ? (const float*)B[2].values : nullptr, nullptr);
+  a.seg[0] = seg(dm.qd, m->Q + r0 * dm.qd, dm.qd, B ? (const float*)B[0].values : nullptr, nullptr);
+  a.seg[1] = seg(dm.kvd, m->K + r0 * dm.kvd, dm.kvd, B ? (const float*)B[1].values : nullptr, nullptr);
+  a.seg[2] = seg(dm.kvd, m->V + r0 * dm.kvd, dm.kvd, B ? (const float*)B[2].values : nullptr, nullptr);
   a.out_map = nullptr;
   if (!presplit) tc_split_x(m, m->N, n, dm.dim);
-  return tc_gemm(m, tc_state(m)->qkv[l], 0, n, a);
+  return tc_gemm(m, tc_state(m)->qkv[l], 0, n, a, lane);
 }
 // gate|up in one GEMM.
-inline bool tc_gateup(sr_model* m, int l, int n, bool presplit = false) {
+inline bool tc_gateup(sr_model* m, int l, int n, bool presplit = false, const TcLane* lane = nullptr) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
   const ModelDims& dm = m->dm;
+  const int64_t r0 = lane ? lane->row0 : 0;
   tc::GemmArgs a{};
   a.nseg = 2;
-  a.seg[0] = seg(dm.hidden, m->G, dm.hidden, nullptr, nullptr);
-  a.seg[1] = seg(dm.hidden, m->U, dm.hidden, nullptr, nullptr);
+  a.seg[0] = seg(dm.hidden, m->G + r0 * dm.hidden, dm.hidden, nullptr, nullptr);
+  a.seg[1] = seg(dm.hidden, m->U + r0 * dm.hidden, dm.hidden, nullptr, nullptr);
   a.out_map = nullptr;
   if (!presplit) tc_split_x(m, m->N, n, dm.dim);
-  return tc_gemm(m, tc_state(m)->gateup[l], 0, n, a);
+  return tc_gemm(m, tc_state(m)->gateup[l], 0, n, a, lane);
 }
 // O / down projection into y (with the residual add y = resid + W x when
 // resid is set; tensor-parallel ranks write their partial sum instead).
+// (y and resid point at the first output row: the caller offsets them for a lane.)
 inline bool tc_proj(sr_model* m, const TcMatrix& W, const float* X, int n, int in_kind, bool presplit, float* y,
-                    const float* resid) {
+                    const float* resid, const TcLane* lane = nullptr) {
   const ModelDims& dm = m->dm;
   tc::GemmArgs a{};
   a.nseg = 1;
   a.seg[0] = seg(dm.dim, y, dm.dim, nullptr, resid);
   a.out_map = nullptr;
   if (!presplit) tc_split_x(m, X, n, in_kind == 1 ? dm.hidden : (in_kind == 2 ? dm.qd : dm.dim));
-  return tc_gemm(m, W, in_kind, n, a);
+  return tc_gemm(m, W, in_kind, n, a, lane);
 }
-inline bool tc_o(sr_model* m, int l, int n, bool presplit, float* y, const float* resid) {
+inline bool tc_o(sr_model* m, int l, int n, bool presplit, float* y, const float* resid,
+                 const TcLane* lane = nullptr) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
-  return tc_proj(m, tc_state(m)->o[l], m->A, n, 2, presplit, y, resid);
+  return tc_proj(m, tc_state(m)->o[l], m->A, n, 2, presplit, y, resid, lane);
 }
-inline bool tc_down(sr_model* m, int l, int n, bool presplit, float* y, const float* resid) {
+inline bool tc_down(sr_model* m, int l, int n, bool presplit, float* y, const float* resid,
+                    const TcLane* lane = nullptr) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
-  return tc_proj(m, tc_state(m)->down[l], m->H, n, 1, presplit, y, resid);
+  return tc_proj(m, tc_state(m)->down[l], m->H, n, 1, presplit, y, resid, lane);
+}
+// The operand planes of slot `slot` (row 0 of a lane's rows).
+inline void tc_planes(sr_model* m, int slot, __nv_bfloat16** xh, __nv_bfloat16** xl) {
+  TcState* t = tc_state(m);
+  const size_t off = (size_t)slot * kLaneRows * t->xcols;
+  *xh = t->xh + off;
+  *xl = t->xl + off;
 }
 inline bool tc_head(sr_model* m, int heads, bool presplit = false) {
   if (heads < kTcMinRows || !tc_prepare(m)) return false;

@@ -138,8 +138,9 @@ k_rmsnorm_fast(float* __restrict__ X, const int32_t* __restrict__ src_map, const
 inline void fast_rmsnorm(sr_model* m, float* X, const int32_t* src_map, const float* w, float* Y, int rows, int d,
                          double eps, op16* yh = nullptr, op16* yl = nullptr,
                          const float* T = nullptr, const uint4* Tll = nullptr, uint32_t epoch = 0,
-                         int* err = nullptr) {
-  k_rmsnorm_fast<<<rows, 128, 0, m->stream>>>(X, src_map, w, Y, rows, d, eps, yh, yl, T, Tll, epoch, err);
+                         int* err = nullptr, cudaStream_t stream = nullptr) {
+  k_rmsnorm_fast<<<rows, 128, 0, stream ? stream : m->stream>>>(X, src_map, w, Y, rows, d, eps, yh, yl, T, Tll, epoch,
+                                                                 err);
 }
 
 // SwiGLU h = g/(1+exp(-g)) * u in fp32 (M:6410-6413 reordered), written as the
@@ -160,46 +161,46 @@ struct FaWork {
 };
 
 template <int HD, int G>
-inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n, const FaWork& w) {
+inline bool fa_launch(sr_model* m, const FastAttnArgs& a, int n, const FaWork& w, cudaStream_t stream) {
   const size_t smem = fa_smem_bytes<HD, G>();
   if constexpr (HD == 128) {
     if (w.single > 0) {  // decode rows: 4 warps split each row's positions
       cudaFuncSetAttribute(k_attn_warp128<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      k_attn_warp128<G><<<dim3(w.single, a.dm.kv_heads), kFaThreads, smem, m->stream>>>(a);
+      k_attn_warp128<G><<<dim3(w.single, a.dm.kv_heads), kFaThreads, smem, stream>>>(a);
       sr_count_launch(m);
     }
     if (w.groups > 0) {  // prefill rows
       if constexpr (G == 4) {  // 4 rows x 4 heads: one tensor-core M tile
         cudaFuncSetAttribute(k_attn_mma128, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MmaSmem::BYTES);
-        k_attn_mma128<<<dim3(w.groups, a.dm.kv_heads), kMmWarps * 32, MmaSmem::BYTES, m->stream>>>(a);
+        k_attn_mma128<<<dim3(w.groups, a.dm.kv_heads), kMmWarps * 32, MmaSmem::BYTES, stream>>>(a);
       } else {  // one warp per row, shared K/V tiles
         const size_t rsm = RowsSmem<G>::BYTES;
         cudaFuncSetAttribute(k_attn_rows128<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
-        k_attn_rows128<G><<<dim3(w.groups, a.dm.kv_heads), kFaThreads, rsm, m->stream>>>(a);
+        k_attn_rows128<G><<<dim3(w.groups, a.dm.kv_heads), kFaThreads, rsm, stream>>>(a);
       }
       sr_count_launch(m);
     }
   } else {
     cudaFuncSetAttribute(k_attn_tile<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_attn_tile<HD, G><<<dim3(w.items, a.dm.kv_heads), kFaThreads, smem, m->stream>>>(a);
+    k_attn_tile<HD, G><<<dim3(w.items, a.dm.kv_heads), kFaThreads, smem, stream>>>(a);
     sr_count_launch(m);
   }
-  k_attn_combine<HD><<<dim3(n, a.dm.heads), HD, 0, m->stream>>>(a);
+  k_attn_combine<HD><<<dim3(n, a.dm.heads), HD, 0, stream>>>(a);
   sr_count_launch(m);
   return true;
 }
 
 template <int HD>
-inline bool fa_dispatch_g(sr_model* m, const FastAttnArgs& a, int n, const FaWork& items) {
+inline bool fa_dispatch_g(sr_model* m, const FastAttnArgs& a, int n, const FaWork& items, cudaStream_t s) {
   switch (a.dm.group) {
-    case 1: return fa_launch<HD, 1>(m, a, n, items);
-    case 2: return fa_launch<HD, 2>(m, a, n, items);
-    case 3: return fa_launch<HD, 3>(m, a, n, items);
-    case 4: return fa_launch<HD, 4>(m, a, n, items);
-    case 5: return fa_launch<HD, 5>(m, a, n, items);
-    case 6: return fa_launch<HD, 6>(m, a, n, items);
-    case 7: return fa_launch<HD, 7>(m, a, n, items);
-    case 8: return fa_launch<HD, 8>(m, a, n, items);
+    case 1: return fa_launch<HD, 1>(m, a, n, items, s);
+    case 2: return fa_launch<HD, 2>(m, a, n, items, s);
+    case 3: return fa_launch<HD, 3>(m, a, n, items, s);
+    case 4: return fa_launch<HD, 4>(m, a, n, items, s);
+    case 5: return fa_launch<HD, 5>(m, a, n, items, s);
+    case 6: return fa_launch<HD, 6>(m, a, n, items, s);
+    case 7: return fa_launch<HD, 7>(m, a, n, items, s);
+    case 8: return fa_launch<HD, 8>(m, a, n, items, s);
     default: return false;
   }
 }
@@ -216,10 +217,19 @@ inline size_t fa_scratch_floats(const ModelDims& dm, int items, size_t* units_ou
   return units * dm.group * (dm.hd + 2);
 }
 
+// One half of a split step for the attention: its stream, first row and the
+// first entries of its item lists (the halves cut the lists at a session).
+struct FaLane {
+  cudaStream_t s;
+  int row0;
+  FaWork base;
+};
+
 // Launch split + combine with caller-provided scratch (no allocation).  With
 // xh/xl set, the combine writes bf16 hi/lo operand planes instead of fp32 A.
+// With a lane, n and items are the half's and xh/xl its planes.
 inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, const FaWork& items, int layer, float* part_o,
-                               float* part_ml, op16* xh = nullptr, op16* xl = nullptr) {
+                               float* part_ml, op16* xh = nullptr, op16* xl = nullptr, const FaLane* lane = nullptr) {
   const ModelDims& dm = m->dm;
   FastAttnArgs a;
   a.Q = m->Q;
@@ -234,19 +244,25 @@ inline bool fast_attention_run(sr_model* m, const float* pool_data, int n, const
   a.xh = xh;
   a.xl = xl;
   a.err = fast_state(m)->err;
+  if (lane) {
+    a.row0 = lane->row0;
+    a.single0 = lane->base.single;
+    a.grp0 = lane->base.groups;
+    a.item0 = lane->base.items;
+  }
   fast_state(m)->ran = true;
-  return dm.hd == 128 ? fa_dispatch_g<128>(m, a, n, items) : fa_dispatch_g<64>(m, a, n, items);
+  cudaStream_t s = lane ? lane->s : m->stream;
+  return dm.hd == 128 ? fa_dispatch_g<128>(m, a, n, items, s) : fa_dispatch_g<64>(m, a, n, items, s);
 }
 
-// Returns false (exact kernel runs instead) for unsupported shapes or when the
-// split scratch would exceed its cap.  The scratch grows on demand.
-inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, const FaWork& work, int layer,
-                               op16* xh = nullptr, op16* xl = nullptr) {
+// Grow the split scratch to cover `work_items` (row, split) items; false when
+// the shape is unsupported or the scratch would exceed its cap.
+inline bool fa_reserve(sr_model* m, int work_items) {
   const ModelDims& dm = m->dm;
   if (!fast_attention_supported(dm)) return false;
   FastState* st = fast_state(m);
   size_t items = 0;
-  fa_scratch_floats(dm, work.items, &items);
+  fa_scratch_floats(dm, work_items, &items);
   const size_t o_bytes = items * dm.group * dm.hd * 4;
   if (o_bytes > ((size_t)1 << 30)) return false;
   if (items > st->items_cap) {
@@ -268,7 +284,18 @@ inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, const
     }
     st->items_cap = cap;
   }
-  return fast_attention_run(m, pool_data, n, work, layer, st->part_o, st->part_ml, xh, xl);
+  return true;
+}
+
+// Returns false (exact kernel runs instead) for unsupported shapes or when the
+// split scratch would exceed its cap.  The scratch grows on demand (a split
+// step reserves it for all its items before its halves start).
+inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, const FaWork& work, int layer,
+                               op16* xh = nullptr, op16* xl = nullptr, const FaLane* lane = nullptr) {
+  const int all_items = lane ? lane->base.items + work.items : work.items;
+  if (!fa_reserve(m, all_items)) return false;
+  FastState* st = fast_state(m);
+  return fast_attention_run(m, pool_data, n, work, layer, st->part_o, st->part_ml, xh, xl, lane);
 }
 
 // ------------------------------------------------------------------- linear --

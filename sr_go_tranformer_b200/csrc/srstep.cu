@@ -955,7 +955,9 @@ int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* 
   if (b->token_offsets[0] != 0 || b->page_offsets[0] != 0) return sr_fail(SR_EINVAL, "offsets must start at 0");
   const int pt = c.page_tokens;
   int64_t n = 0, max_end = 0, heads = 0, items = 0, single = 0, groups = 0;
+  int64_t pre[kMaxSessions + 1][4];  // rows, items, single, groups before session i
   for (int i = 0; i < S; i++) {
+    pre[i][0] = n, pre[i][1] = items, pre[i][2] = single, pre[i][3] = groups;
     int64_t len = (int64_t)b->token_offsets[i + 1] - b->token_offsets[i];
     if (len < 1 || len > kMaxRows - n)
       return sr_fail(SR_EINVAL, "prefill requires nonempty chunks totaling at most 1024 tokens");
@@ -1022,6 +1024,25 @@ int sr_validate_batch(const sr_model* m, const sr_kvpool* pool, const sr_batch* 
   info->attn_items = (int)items;
   info->attn_single = (int)single;
   info->attn_groups = (int)groups;
+  // Split point for a step run as two halves: the session boundary closest to
+  // half the rows with both halves between kSplitMinRows and kLaneRows rows.
+  info->split_rows = info->split_items = info->split_single = info->split_groups = 0;
+  {
+    int best = -1;
+    int64_t best_d = 0;
+    for (int i = 1; i < S; i++) {
+      const int64_t a = pre[i][0], bh = n - a;
+      if (a < kSplitMinRows || bh < kSplitMinRows || a > kLaneRows || bh > kLaneRows) continue;
+      const int64_t dd = a > n - a ? 2 * a - n : n - 2 * a;
+      if (best < 0 || dd < best_d) best = i, best_d = dd;
+    }
+    if (best > 0) {
+      info->split_rows = (int)pre[best][0];
+      info->split_items = (int)pre[best][1];
+      info->split_single = (int)pre[best][2];
+      info->split_groups = (int)pre[best][3];
+    }
+  }
   return SR_OK;
 }
 
@@ -1262,6 +1283,209 @@ static int gpt2_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info
   return SR_OK;
 }
 
+// ------------------------------------------------------------- split steps --
+// A fast-mode step whose rows can be cut at a session boundary into two
+// halves of 64..512 rows runs as two halves on two SM partitions of the GPU
+// (CUDA green contexts, 72 and 76 SMs on a B200), each with its own stream.
+// Per layer a half is HBM-bound in its attention (it streams its sessions' KV
+// pages) and tensor-bound in its four projections; the two halves' attentions
+// alternate (events), so one half's projections run while the other half's
+// attention has the HBM to itself.  The halves share the weights, the KV pool
+// (disjoint pages) and the model buffers (disjoint rows); each has its own
+// operand planes, stream-K scratch and attention item range.  The step's
+// results per row are the same arithmetic as the unsplit fast step except the
+// stream-K cut of each projection (the partition's SM count changes which
+// block ranges are summed first).
+namespace {
+
+struct SplitState {
+  bool ok = false;
+  CUgreenCtx g[2] = {nullptr, nullptr};
+  cudaStream_t s[2] = {nullptr, nullptr};
+  int sms[2] = {0, 0};
+  cudaEvent_t fork = nullptr, join[2] = {nullptr, nullptr}, attn[2] = {nullptr, nullptr};
+  decltype(&cuStreamDestroy) stream_destroy = nullptr;
+  decltype(&cuGreenCtxDestroy) ctx_destroy = nullptr;
+};
+
+template <typename F>
+bool driver_fn(const char* name, F* out) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess ||
+      !p) {
+    cudaGetLastError();
+    return false;
+  }
+  *out = (F)p;
+  return true;
+}
+
+void split_free(SplitState* sp) {
+  for (int i = 0; i < 2; i++) {
+    if (sp->s[i] && sp->stream_destroy) sp->stream_destroy((CUstream)sp->s[i]);
+    if (sp->join[i]) cudaEventDestroy(sp->join[i]);
+    if (sp->attn[i]) cudaEventDestroy(sp->attn[i]);
+    if (sp->g[i] && sp->ctx_destroy) sp->ctx_destroy(sp->g[i]);
+  }
+  if (sp->fork) cudaEventDestroy(sp->fork);
+  delete sp;
+}
+
+// The partitions and streams, made on the first split step (with the model's
+// device current).  Returns null when the device or driver cannot partition.
+SplitState* split_state(sr_model* m) {
+  if (m->split) {
+    SplitState* sp = (SplitState*)m->split;
+    return sp->ok ? sp : nullptr;
+  }
+  SplitState* sp = new SplitState();
+  m->split = sp;
+  m->fast_free.push_back([sp]() { split_free(sp); });
+  decltype(&cuDeviceGet) device_get;
+  decltype(&cuDeviceGetDevResource) get_resource;
+  decltype(&cuDevSmResourceSplitByCount) split_by_count;
+  decltype(&cuDevResourceGenerateDesc) generate_desc;
+  decltype(&cuGreenCtxCreate) ctx_create;
+  decltype(&cuGreenCtxStreamCreate) stream_create;
+  if (!driver_fn("cuDeviceGet", &device_get) || !driver_fn("cuDeviceGetDevResource", &get_resource) ||
+      !driver_fn("cuDevSmResourceSplitByCount", &split_by_count) ||
+      !driver_fn("cuDevResourceGenerateDesc", &generate_desc) || !driver_fn("cuGreenCtxCreate", &ctx_create) ||
+      !driver_fn("cuGreenCtxStreamCreate", &stream_create) || !driver_fn("cuStreamDestroy", &sp->stream_destroy) ||
+      !driver_fn("cuGreenCtxDestroy", &sp->ctx_destroy))
+    return nullptr;
+  CUdevice dev;
+  CUdevResource all, groups[2], rest;
+  unsigned ng = 2;
+  if (device_get(&dev, m->device) != CUDA_SUCCESS || get_resource(dev, &all, CU_DEV_RESOURCE_TYPE_SM) != CUDA_SUCCESS)
+    return nullptr;
+  // two equal groups in the partition granularity (8 SMs), the rest to the second
+  const unsigned half = all.sm.smCount / 2 / 8 * 8;
+  if (half < 16 || split_by_count(groups, &ng, &all, &rest, 0, half) != CUDA_SUCCESS || ng != 2) return nullptr;
+  CUdevResource second[2] = {groups[1], rest};
+  CUdevResourceDesc desc[2];
+  if (generate_desc(&desc[0], &groups[0], 1) != CUDA_SUCCESS ||
+      generate_desc(&desc[1], second, rest.sm.smCount ? 2 : 1) != CUDA_SUCCESS)
+    return nullptr;
+  sp->sms[0] = (int)groups[0].sm.smCount;
+  sp->sms[1] = (int)(groups[1].sm.smCount + rest.sm.smCount);
+  for (int i = 0; i < 2; i++) {
+    CUstream cs = nullptr;
+    if (ctx_create(&sp->g[i], desc[i], dev, CU_GREEN_CTX_DEFAULT_STREAM) != CUDA_SUCCESS ||
+        stream_create(&cs, sp->g[i], CU_STREAM_NON_BLOCKING, 0) != CUDA_SUCCESS)
+      return nullptr;
+    sp->s[i] = (cudaStream_t)cs;
+    if (cudaEventCreateWithFlags(&sp->join[i], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&sp->attn[i], cudaEventDisableTiming) != cudaSuccess)
+      return nullptr;
+  }
+  if (cudaEventCreateWithFlags(&sp->fork, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  cudaGetLastError();
+  sp->ok = true;
+  return sp;
+}
+
+}  // namespace
+
+extern "C" int sr_model_set_split(sr_model* m, int32_t enabled) {
+  if (!m) return sr_fail(SR_EINVAL, "null model");
+  if (enabled != 0 && enabled != 1) return sr_fail(SR_EINVAL, "enabled must be 0 or 1");
+  m->split_mode = enabled;
+  return SR_OK;
+}
+
+// The layers of a split step (fast mode, tensor-core projections, one GPU).
+// Returns SR_EUNSUPPORTED before enqueueing anything when the step cannot be
+// split (the caller then runs the whole-step layers).
+static int split_layers(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel) {
+  const ModelDims& dm = m->dm;
+  if (!m->split_mode || info.split_rows == 0 || dm.tp_size > 1 || !fast_attention_supported(dm))
+    return SR_EUNSUPPORTED;
+  SplitState* sp = split_state(m);
+  if (!sp || !fa_reserve(m, info.attn_items)) return SR_EUNSUPPORTED;
+  const int n = info.rows, d = dm.dim, L = dm.layers;
+  const double eps = m->d.norm_eps;
+  struct Half {
+    int r0, rows;
+    FaWork work, base;
+    TcLane lane;
+    FaLane fa;
+    op16 *xh, *xl;
+  } h[2];
+  const FaWork a_work{info.split_items, info.split_single, info.split_groups};
+  for (int i = 0; i < 2; i++) {
+    Half& x = h[i];
+    x.r0 = i == 0 ? 0 : info.split_rows;
+    x.rows = i == 0 ? info.split_rows : n - info.split_rows;
+    x.base = i == 0 ? FaWork{0, 0, 0} : a_work;
+    x.work = i == 0 ? a_work
+                    : FaWork{info.attn_items - a_work.items, info.attn_single - a_work.single,
+                             info.attn_groups - a_work.groups};
+    x.lane = TcLane{sp->s[i], i, sp->sms[i], x.r0};
+    x.fa = FaLane{sp->s[i], x.r0, x.base};
+    tc_planes(m, i, &x.xh, &x.xl);
+  }
+  CK(cudaEventRecord(sp->fork, m->stream));
+  for (int i = 0; i < 2; i++) CK(cudaStreamWaitEvent(sp->s[i], sp->fork, 0));
+  auto join = [&]() {
+    for (int i = 0; i < 2; i++) {
+      cudaEventRecord(sp->join[i], sp->s[i]);
+      cudaStreamWaitEvent(m->stream, sp->join[i], 0);
+    }
+  };
+  for (int l = 0; l < L; l++) {
+    if (cancel && *cancel) {
+      join();
+      sr_prof_span_end(m);
+      cudaStreamSynchronize(m->stream);
+      sr_prof_resolve(m);
+      return sr_fail(SR_ECANCELED, "step canceled between layers");
+    }
+    const Param* P = &m->params[1 + 9 * l];
+    for (int i = 0; i < 2; i++) {
+      const Half& x = h[i];
+      cudaStream_t s = sp->s[i];
+      float* X = m->X + (int64_t)x.r0 * d;
+      float* N = m->N + (int64_t)x.r0 * d;
+      bool ok = true;
+      SR_LAUNCH_ON(m, SR_PROF_NORM, s,
+                   fast_rmsnorm(m, X, nullptr, (const float*)P[0].values, N, x.rows, d, eps, x.xh, x.xl, nullptr,
+                                nullptr, 0, nullptr, s));
+      SR_LAUNCH_ON(m, SR_PROF_LINEAR, s, ok = tc_qkv(m, l, x.rows, true, &x.lane));
+      SR_LAUNCH_ON(m, SR_PROF_ROPE_KV, s,
+                   k_rope_kv_exact<<<x.rows, 128, 0, s>>>(m->Q, m->K, m->V, m->cos_t, m->sin_t, m->meta, pool->data,
+                                                          dm, l, x.r0));
+      sr_count_launch(m, 3);  // two norms and RoPE/KV of this half-layer
+      // the halves' attentions alternate: half 1 after half 0's of this layer,
+      // half 0 after half 1's of the previous layer
+      if (i == 1) CK(cudaStreamWaitEvent(s, sp->attn[0], 0));
+      else if (l > 0) CK(cudaStreamWaitEvent(s, sp->attn[1], 0));
+      SR_LAUNCH_ON(m, SR_PROF_ATTENTION, s,
+                   ok = ok && fast_attention_try(m, pool->data, x.rows, x.work, l, x.xh, x.xl, &x.fa));
+      CK(cudaEventRecord(sp->attn[i], s));
+      SR_LAUNCH_ON(m, SR_PROF_LINEAR, s, ok = ok && tc_o(m, l, x.rows, true, X, X, &x.lane));
+      SR_LAUNCH_ON(m, SR_PROF_NORM, s,
+                   fast_rmsnorm(m, X, nullptr, (const float*)P[5].values, N, x.rows, d, eps, x.xh, x.xl, nullptr,
+                                nullptr, 0, nullptr, s));
+      SR_LAUNCH_ON(m, SR_PROF_LINEAR, s, ok = ok && tc_gateup(m, l, x.rows, true, &x.lane));
+      const int64_t cnt = (int64_t)x.rows * dm.hidden;
+      const int sw_blocks = (int)std::min<int64_t>((cnt + 255) / 256, 148 * 16);
+      SR_LAUNCH_ON(m, SR_PROF_SWIGLU, s,
+                   k_swiglu_split<<<sw_blocks, 256, 0, s>>>(m->G + (int64_t)x.r0 * dm.hidden,
+                                                            m->U + (int64_t)x.r0 * dm.hidden, x.xh, x.xl, cnt));
+      sr_count_launch(m);
+      SR_LAUNCH_ON(m, SR_PROF_LINEAR, s, ok = ok && tc_down(m, l, x.rows, true, X, X, &x.lane));
+      if (!ok) {
+        join();
+        return sr_fail(SR_ENOMEM, "split step: a projection or the attention could not run (scratch allocation failed)");
+      }
+    }
+  }
+  join();
+  CK(cudaGetLastError());
+  return SR_OK;
+}
+
 int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel,
                     const StepScratch* scratch) {
   if (m->d.arch == SR_ARCH_GPT2) return gpt2_step_enqueue(m, pool, info, cancel);
@@ -1285,7 +1509,14 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
   op16* xl = tc ? tc_xl(m) : nullptr;
   TpSum pending;  // tensor parallel: an all-reduced sum still to be added to X
   int* tp_err = m->peer ? ((PeerHost*)m->peer)->err : nullptr;
-  for (int l = 0; l < L; l++) {
+  bool split = false;
+  if (tc && !tp) {
+    rc = split_layers(m, pool, info, cancel);
+    if (rc != SR_OK && rc != SR_EUNSUPPORTED) return rc;
+    split = rc == SR_OK;
+    rc = SR_OK;
+  }
+  for (int l = 0; l < (split ? 0 : L); l++) {
     if (cancel && *cancel) {
       sr_prof_span_end(m);
       cudaStreamSynchronize(s);
@@ -1324,7 +1555,7 @@ int sr_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const v
       sr_launch_linear(m, m->N, n, P[3], o);
     }
     SR_LAUNCH(m, SR_PROF_ROPE_KV,
-              k_rope_kv_exact<<<n, 128, 0, s>>>(m->Q, m->K, m->V, m->cos_t, m->sin_t, m->meta, pool->data, dm, l));
+              k_rope_kv_exact<<<n, 128, 0, s>>>(m->Q, m->K, m->V, m->cos_t, m->sin_t, m->meta, pool->data, dm, l, 0));
     sr_count_launch(m, 3);  // two norms and RoPE/KV of this layer
     bool a_split = false;   // attention wrote the O projection's operand planes
     SR_LAUNCH(m, SR_PROF_ATTENTION,

@@ -39,7 +39,14 @@ struct BatchInfo {
   int attn_items;  // (row, kAttnSplit-position split) pairs of the split-K attention
   int attn_single;  // of those, the items of rows from 1-token chunks
   int attn_groups;  // (group of up to 4 consecutive rows of a longer chunk, split) pairs
+  // Rows and attention counts of the first half when the step can run as two
+  // halves cut at a session boundary (split_rows == 0: it cannot).
+  int split_rows, split_items, split_single, split_groups;
 };
+// Rows of one half of a split step: at least a tensor-core tile's worth, at
+// most half the step's row bound (each half has its own operand planes).
+constexpr int kSplitMinRows = 64;
+constexpr int kLaneRows = sr::kMaxRows / 2;
 
 // Event-based per-kernel-class timing on the model's stream.
 struct Profiler {
@@ -95,6 +102,8 @@ struct sr_model {
   // fast-mode state (owned by fast_kernels.cuh)
   void* fast = nullptr;
   void* tc = nullptr;  // tensor-core shadows (fast_gemm.cuh)
+  void* split = nullptr;       // split-step partitions and streams (srstep.cu), made on first use
+  int split_mode = 0;          // sr_model_set_split: fast-mode steps may run as two overlapped halves
   std::vector<std::function<void()>> fast_free;
 };
 
@@ -121,12 +130,15 @@ int sr_param_table(const sr_model_desc& c, int rank, int size, std::vector<sr::P
 inline void sr_count_launch(sr_model* m, int k = 1) { m->prof.total_launches += k; }
 
 // RAII scope around one kernel launch: counts it and, when its class is
-// selected, brackets it with a pair of events on the model's stream.
+// selected, brackets it with a pair of events on the model's stream (or on
+// the stream of a split step's half).
 struct ProfScope {
   sr_model* m;
   int cls;
   bool timed;
-  ProfScope(sr_model* m_, int cls_) : m(m_), cls(cls_), timed((m_->prof.mask >> cls_) & 1u) {
+  cudaStream_t s;
+  ProfScope(sr_model* m_, int cls_, cudaStream_t s_ = nullptr)
+      : m(m_), cls(cls_), timed((m_->prof.mask >> cls_) & 1u), s(s_ ? s_ : m_->stream) {
     if (timed) {
       Profiler& p = m->prof;
       while (p.events.size() < p.used + 2) {
@@ -134,14 +146,14 @@ struct ProfScope {
         cudaEventCreate(&e);
         p.events.push_back(e);
       }
-      cudaEventRecord(p.events[p.used], m->stream);
+      cudaEventRecord(p.events[p.used], s);
     }
   }
   ~ProfScope() {
     Profiler& p = m->prof;
     p.launches[cls]++;
     if (timed) {
-      cudaEventRecord(p.events[p.used + 1], m->stream);
+      cudaEventRecord(p.events[p.used + 1], s);
       p.used += 2;
       p.pending.push_back(cls);
     }
@@ -151,6 +163,11 @@ struct ProfScope {
   do {                         \
     ProfScope ps_((m), (cls)); \
     __VA_ARGS__;               \
+  } while (0)
+#define SR_LAUNCH_ON(m, cls, stream, ...) \
+  do {                                    \
+    ProfScope ps_((m), (cls), (stream));  \
+    __VA_ARGS__;                          \
   } while (0)
 void sr_prof_span_begin(sr_model* m);
 void sr_prof_span_end(sr_model* m);

@@ -164,6 +164,11 @@ class Model:
         A.check(A.lib().sr_model_code_cache(self.h, C.byref(v)))
         return bool(v.value)
 
+    def set_split(self, enabled):
+        """Fast-mode steps of enough rows run as two halves on two SM
+        partitions (True) or whole (False, the default); see sr_model_set_split."""
+        A.check(A.lib().sr_model_set_split(self.h, 1 if enabled else 0))
+
     def param_info(self, i):
         info = A.ParamInfo()
         A.check(A.lib().sr_model_param_info(self.h, i, C.byref(info)))

@@ -7,6 +7,8 @@ an absolute tolerance of FAST_ATOL on logits of magnitude ~1 and greedy ids
 must agree except on recorded near-ties (margin below FAST_TIE).
 """
 
+import ctypes as C
+
 import numpy as np
 import pytest
 
@@ -151,3 +153,60 @@ def test_fast_decode_rows(oracle, srlib, rows):
     prompts = [rng.integers(0, 2048, size=int(rng.integers(1, 4))).tolist() for _ in range(rows)]
     worst, ties = run_pair(oracle, srlib, om, prompts, chunk=4, decode_steps=3)
     assert worst <= FAST_ATOL
+
+
+def _launches(dm):
+    from sr_go_tranformer_b200 import _abi as A
+    ms = (C.c_double * len(A.PROF_CLASSES))()
+    la = (C.c_int64 * len(A.PROF_CLASSES))()
+    span, steps, total = C.c_double(), C.c_int64(), C.c_int64()
+    A.check(A.lib().sr_profile_read(dm.h, ms, la, C.byref(span), C.byref(steps), C.byref(total), 1))
+    return total.value
+
+
+@pytest.mark.parametrize("shape", ["decode", "ragged"])
+def test_split_step_matches_oracle_and_whole_step(oracle, srlib, shape):
+    """Split steps: a fast-mode step whose rows can be cut at a session boundary
+    into two halves of 64..512 rows runs as two halves on two SM partitions.
+    Mistral-7B layer shape, 2 layers, Q8.  "decode": 130 sessions with short
+    prompts, then 2 decode steps of 130 rows (halves of 65).  "ragged": prefill
+    chunks of 300, 120 and 40 rows beside 140 one-row sessions.  Each step's
+    logits are checked against the oracle and against the same model stepping
+    whole (split off), and the split model must launch more kernels (each half
+    launches its own)."""
+    from sr_go_tranformer_b200 import step as S
+    cfg = oracle.make_config(2048, 4096, 14336, 2, 32, 8, 1024, rope_theta=1e6, tied=False, weight_format="q8",
+                             page_tokens=16)
+    om = oracle.Model(cfg)
+    om.init_synthetic(31, 0.02, threads=8)
+    rng = np.random.default_rng(32 if shape == "decode" else 33)
+    if shape == "decode":
+        prompts = [rng.integers(0, 2048, size=int(rng.integers(1, 4))).tolist() for _ in range(130)]
+    else:
+        prompts = [rng.integers(0, 2048, size=n).tolist() for n in (300, 120, 40)] + \
+                  [rng.integers(0, 2048, size=1).tolist() for _ in range(140)]
+    models = []
+    for split in (True, False):
+        dm = device_from_oracle(om, srlib, mode="fast")
+        dm.set_split(split)
+        pages = sum((len(p) + 3 + 16) // 16 + 1 for p in prompts)
+        pool = S.PagePool(dm, pages)
+        models.append((dm, pool, [dm.new_cache(pool) for _ in prompts]))
+    opool = np.zeros(sum((len(p) + 3 + 16) // 16 + 1 for p in prompts) * om.page_elements, dtype=np.float32)
+    ocaches = models[1][2]  # page tables match: both pools hand out pages in the same order
+    chunks = prompts
+    launches = []
+    for step in range(3):
+        pos = [c.pos for c in ocaches]
+        got = [dm.prefill_selected(caches, chunks) for dm, _, caches in models]
+        launches.append([_launches(dm) for dm, _, _ in models])
+        want = om.step(opool, pos, chunks, [c.pages for c in ocaches], threads=8)
+        for g in got:
+            err = float(np.abs(g - want).max())
+            assert err <= FAST_ATOL, f"step {step}: split-step logits differ from the oracle by {err:.3g}"
+        assert float(np.abs(got[0] - got[1]).max()) <= FAST_ATOL
+        chunks = [[int(t)] for t in want.argmax(axis=1)]
+    assert all(a > b for a, b in launches), launches
+    for dm, pool, _ in models:
+        pool.close()
+        dm.close()
