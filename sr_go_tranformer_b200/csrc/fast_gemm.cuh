@@ -19,12 +19,14 @@
 #include "fast_kernels.cuh"
 #include "srstep_internal.h"
 #include "tc_gemm.cuh"
+#include "tc_gemm2.cuh"
 #include "tc_gemm_direct.cuh"
 
 namespace sr {
 
 struct TcMatrix {
   uint8_t* wt = nullptr;  // bf16 code cache in 32 KiB swizzled (256-feature, 64-column) tiles, or null
+  CUtensorMap cmap;       // the cache as [tiles * 256][64] bf16 rows, 128-row boxes (k_gemm_q2)
   float* scales = nullptr;
   bool own_scales = false;
   int rows = 0, cols = 0;
@@ -49,6 +51,7 @@ struct TcState {
   int xcols = 0;              // row stride bound of the planes: max(dim, hidden, attention width)
   float* partial[2] = {nullptr, nullptr};  // per slot: [sms][2][kN][kMC] stream-K partial tiles
   int sms = 148;
+  int pairs = 0;              // SM pairs (2-CTA clusters of k_gemm_q2) that fit at once; 0: pair MMAs off
   int* err = nullptr;
   int* h_err = nullptr;
   bool ran = false;
@@ -82,6 +85,21 @@ inline bool make_map(CUtensorMap* map, void* base, uint64_t cols, uint64_t rows,
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The bf16 code cache as [rows][64] (128-byte rows, already in the MMA's
+// swizzled order), boxes of 128 rows copied as they are: one CTA's half of a
+// 256-feature tile.
+inline bool make_cache_map(CUtensorMap* map, void* base, uint64_t rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || ((uintptr_t)base) % 16 != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)tc::kKB, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)tc::kKB * 2};
+  cuuint32_t box[2] = {(cuuint32_t)tc::kKB, (cuuint32_t)tc::kM};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -175,6 +193,7 @@ inline bool tc_build(sr_model* m, TcState* t, TcMatrix& dst, const std::vector<c
   if (!cache) return true;
   const size_t bytes = (size_t)mt * groups * tc::kTileA;
   if (!tc_alloc(t, (void**)&dst.wt, bytes)) return false;
+  if (!make_cache_map(&dst.cmap, dst.wt, (uint64_t)mt * groups * tc::kMC)) return false;
   cudaMemsetAsync(dst.wt, 0, bytes, m->stream);  // padding rows of the last tile
   r0 = 0;
   for (const Param* p : parts) {
@@ -228,6 +247,7 @@ inline bool tc_prepare(sr_model* m) {
   if (m->d.weight_format == SR_FMT_F32 || dm.dim % 8 || dm.hidden % 8 || dm.qd % 8 || !encode_fn()) return false;
   cudaFuncSetAttribute(tc::k_gemm_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
   cudaFuncSetAttribute(tc::k_gemm_direct, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kDirSmemBytes);
+  cudaFuncSetAttribute(tc::k_gemm_q2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes2);
   bool built = t->cache_wanted && tc_build_all(m, t, true);
   t->cached = built;
   if (!built) {  // without the cache (not wanted, or it did not fit)
@@ -245,6 +265,24 @@ inline bool tc_prepare(sr_model* m) {
       sms = 148;
     }
     t->sms = sms;
+    // how many 2-CTA clusters of k_gemm_q2 can be resident at once
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.gridDim = dim3(sms / 2 * 2);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = tc::kSmemBytes2;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, tc::k_gemm_q2, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      clusters = 0;
+    }
+    t->pairs = std::min(clusters, sms / 2);
   }
   if (!tc_alloc(t, (void**)&t->xh, (size_t)kMaxRows * xcols * 2) ||
       !tc_alloc(t, (void**)&t->xl, (size_t)kMaxRows * xcols * 2) || !tc_alloc(t, (void**)&t->err, 16) ||
@@ -296,8 +334,9 @@ inline void tc_split_x(sr_model* m, const float* X, int n, int in) {
 }
 
 // in_kind: 0 = the residual width (dim), 1 = hidden, 2 = the attention width (qd).
-// Stream-K schedule: groups of nt CTAs (one per 128-row tile) fill the SMs,
-// each group taking at least kSkMinUnits (tile, block) units.
+// Stream-K schedule: groups of nt CTAs (one per 128-row tile), or of nt2 SM
+// pairs (one per 256-row tile), fill the SMs, each group taking at least
+// kSkMinUnits (tile, block) units.
 constexpr int kSkMinUnits = 4;
 inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::GemmArgs a, const TcLane* lane = nullptr) {
   TcState* t = tc_state(m);
@@ -310,20 +349,45 @@ inline bool tc_gemm(sr_model* m, const TcMatrix& W, int in_kind, int n, tc::Gemm
   a.scales = W.scales;
   a.err = t->err;
   a.mt = (W.rows + tc::kMC - 1) / tc::kMC;
-  a.nt = (n + tc::kN - 1) / tc::kN;
-  if (a.nt > sms || (int64_t)a.mt * a.groups * sms >= ((int64_t)1 << 31)) return false;  // 32-bit schedule math
   const int64_t units = (int64_t)a.mt * a.groups;
-  a.ngroups = (int)std::max<int64_t>(1, std::min<int64_t>(sms / a.nt, (units + kSkMinUnits - 1) / kSkMinUnits));
   a.partial = t->partial[slot];
   const CUtensorMap& xh = in_kind == 1 ? t->xh_h[slot] : (in_kind == 2 ? t->xh_q[slot] : t->xh_d[slot]);
   const CUtensorMap& xl = in_kind == 1 ? t->xl_h[slot] : (in_kind == 2 ? t->xl_q[slot] : t->xl_d[slot]);
   a.wt = W.wt;
   a.fmt = W.fmt;
-  if (W.wt)
-    tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, stream>>>(xh, xl, a);
-  else
-    tc::k_gemm_direct<<<a.ngroups * a.nt, tc::kDirThreads, tc::kDirSmemBytes, stream>>>(xh, xl, W.map[0], W.map[1],
-                                                                                       W.map[2], a);
+  // Pairs of SMs (k_gemm_q2) for a whole step of more than one 128-row tile
+  // with the code cache: groups of nt2 2-CTA clusters, one per 256-row tile.
+  const int nt2 = (n + tc::kN2 - 1) / tc::kN2;
+  if (W.wt && !lane && n > tc::kN && t->pairs > 0 && nt2 <= t->pairs &&
+      units * t->pairs < ((int64_t)1 << 31)) {
+    a.nt = 2 * nt2;  // 128-row tiles, as the partial slots and k_sk_reduce count them
+    a.ngroups = (int)std::max<int64_t>(1, std::min<int64_t>(t->pairs / nt2, (units + kSkMinUnits - 1) / kSkMinUnits));
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.ngroups * nt2 * 2);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = tc::kSmemBytes2;
+    cfg.stream = stream;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, tc::k_gemm_q2, W.cmap, xh, xl, a) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+  } else {
+    a.nt = (n + tc::kN - 1) / tc::kN;
+    if (a.nt > sms || units * sms >= ((int64_t)1 << 31)) return false;  // 32-bit schedule math
+    a.ngroups = (int)std::max<int64_t>(1, std::min<int64_t>(sms / a.nt, (units + kSkMinUnits - 1) / kSkMinUnits));
+    if (W.wt)
+      tc::k_gemm_q<<<a.ngroups * a.nt, tc::kThreads, tc::kSmemBytes, stream>>>(xh, xl, a);
+    else
+      tc::k_gemm_direct<<<a.ngroups * a.nt, tc::kDirThreads, tc::kDirSmemBytes, stream>>>(xh, xl, W.map[0],
+                                                                                         W.map[1], W.map[2], a);
+  }
   sr_count_launch(m);
   // Tiles left in partial slots: every tile when the epilogue needs the
   // residual or the head row map, otherwise only tiles cut by a group boundary.

@@ -218,14 +218,15 @@ def test_fast_decode_gemv(oracle, srlib, fmt, cols):
 @pytest.mark.parametrize("cols", [64, 576, 4096, 14336])
 def test_fast_tensor_core_gemm(oracle, srlib, fmt, cols, cache):
     """SR_MODE_FAST projections of 32 or more rows run the tcgen05 GEMM, with
-    the fp16 code cache or (direct) reading the Q8 / Q4 codes as stored and
-    widening them to bf16 in shared memory.  down_proj [64, cols]: one 256-feature tile whose blocks are cut
-    across up to 56 stream-K groups (the group with the first blocks adds the
-    others' published partial sums); gate [cols, 64]: many whole tiles, the
-    last one partly out of range; the embedding as a head [256, 64].  Row
-    counts cover one partial 128-row tile up to eight.  Each output must be
-    within 3e-5 of sum_j |x_j w_j| of the exact-order oracle (bf16 hi + lo
-    activation planes); both code sources must give identical bits."""
+    the bf16 code cache or (direct) reading the Q8 / Q4 codes as stored and
+    widening them to bf16 in shared memory; with the cache, steps of more than
+    128 rows run on SM pairs (k_gemm_q2).  down_proj [64, cols]: one
+    256-feature tile whose blocks are cut across up to 56 stream-K groups
+    (k_sk_reduce adds their partial sums); gate [cols, 64]: many whole tiles,
+    the last one partly out of range; the embedding as a head [256, 64].  Row
+    counts cover one partial 128-row tile up to four 256-row pair tiles.  Each
+    output must be within 3e-5 of sum_j |x_j w_j| of the exact-order oracle
+    (bf16 hi + lo activation planes)."""
     dm = model(hidden=cols, fmt=fmt)
     dm.set_mode("fast")
     dm.set_code_cache(cache)
@@ -235,7 +236,7 @@ def test_fast_tensor_core_gemm(oracle, srlib, fmt, cols, cache):
         vals, sc = oracle.quantize(w, Q8 if fmt == "q8" else Q4)
         dm.load_param(index, vals, sc)
         wd = np.abs(dequant(vals, sc, fmt, rows_w, cols_w))
-        for n in (32, 33, 128, 200, 1000):
+        for n in (32, 33, 128, 200, 256, 512, 1000):
             x = rng.standard_normal((n, cols_w)).astype(np.float32)
             got = dm.linear(index, x)
             assert dm.code_cache() == cache
