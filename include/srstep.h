@@ -51,8 +51,9 @@ enum { SR_PARAM_F32 = 0, SR_PARAM_Q8 = 1, SR_PARAM_Q4 = 2 };
  *   (sequential fp32 dots, 4-strided Q8/Q4 partials per 64-block, fp64 norm,
  *   softmax and SwiGLU sums) on CUDA cores, without FMA contraction.
  * SR_MODE_FAST uses fused multiply-adds, split-K attention and, for the Q8/Q4
- *   projections, a decode GEMV on CUDA cores below 32 step rows and tcgen05
- *   tensor cores from 32; it matches the reference within a stated tolerance. */
+ *   projections, a decode GEMV on CUDA cores for steps of 1 or 2 rows and
+ *   tcgen05 tensor cores from 3; it matches the reference within a stated
+ *   tolerance. */
 enum { SR_MODE_EXACT = 0, SR_MODE_FAST = 1 };
 
 /* Model description: Config (cmd/monolith/monolith.go:56-66) plus the HF

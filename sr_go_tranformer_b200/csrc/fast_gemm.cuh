@@ -322,8 +322,11 @@ inline bool tc_prepare(sr_model* m) {
   return true;
 }
 
-// Minimum step rows for the tensor-core path (below it the CUDA-core kernels run).
-constexpr int kTcMinRows = 32;
+// Minimum step rows for the tensor-core path: its time is the same for 1 to 128
+// rows, and from 3 rows it beats the decode GEMV (gemv.cuh), which serves the
+// 1- and 2-row steps.
+constexpr int kTcMinRows = 3;
+static_assert(kTcMinRows == gv::kMaxRows + 1, "every fast step has a projection kernel");
 
 inline void tc_split_x(sr_model* m, const float* X, int n, int in) {
   TcState* t = tc_state(m);

@@ -303,15 +303,10 @@ inline bool fast_attention_try(sr_model* m, const float* pool_data, int n, const
 bool fast_linear(sr_model* m, const float* X, int n, const Param& W, LinearOut O);
 
 // ------------------------------------------------------------- decode GEMV --
-// Steps of up to kGemvPassRows rows run the decode GEMV, in passes of at
-// most gv::kMaxRows rows (each pass reads the weights once); from 32 rows the
-// tensor cores take over.
-constexpr int kGemvPassRows = 31;
-
-// Whether the decode GEMV covers matrix W: Q8 rows of a multiple of 16
-// columns, Q4 of 32 (16-byte aligned rows of codes).
+// Whether the decode GEMV covers matrix W for n step rows (1..gv::kMaxRows):
+// Q8 rows of a multiple of 16 columns, Q4 of 32 (16-byte aligned rows of codes).
 inline bool gemv_covers(const Param& W, int n) {
-  if (n < 1 || n > kGemvPassRows) return false;
+  if (n < 1 || n > gv::kMaxRows) return false;
   if (W.format == kQ8) return W.cols % 16 == 0;
   if (W.format == kQ4) return W.cols % 32 == 0;
   return false;
@@ -323,13 +318,19 @@ inline void gemv_launch(const gv::Args& a, dim3 grid, cudaStream_t s) {
   else gv::k_gemv<kQ4, NR><<<grid, gv::kThreads, 0, s>>>(a);
 }
 
-// Arguments, grid and scratch of one pass of n <= gv::kMaxRows rows.  False
-// when scratch cannot be allocated (nothing launched).
-inline bool gemv_prepare(sr_model* m, const float* X, int n, const Param* const* W, const LinearOut* O, int nseg,
-                         gv::Args* out, dim3* grid, int* nr_out) {
+// Y = X W^T for up to 3 matrices sharing X (same format and width), each with
+// its own output.  Returns false when the shapes are not covered or scratch
+// cannot be allocated; then nothing was launched and the caller runs the
+// tensor-core or exact kernels.
+inline bool gemv_run(sr_model* m, const float* X, int n, const Param* const* W, const LinearOut* O, int nseg) {
+  if (nseg < 1 || nseg > gv::kMaxSeg) return false;
+  for (int i = 0; i < nseg; i++)
+    if (!gemv_covers(*W[i], n) || W[i]->format != W[0]->format || W[i]->cols != W[0]->cols ||
+        (O[i].out_map != O[0].out_map))
+      return false;
   FastState* st = fast_state(m);
-  const int nr = n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8;
-  gv::Args& a = *out;
+  const int nr = n;  // 1 or 2
+  gv::Args a;
   a.x = X;
   a.n = n;
   a.in = W[0]->cols;
@@ -393,51 +394,10 @@ inline bool gemv_prepare(sr_model* m, const float* X, int n, const Param* const*
     a.part = st->gv_part;
     a.counters = st->gv_count;
   }
-  *grid = dim3(tiles, a.ksplit);
-  *nr_out = nr;
-  return true;
-}
-
-// Y = X W^T for up to 3 matrices sharing X (same format and width), each with
-// its own output.  Returns false when the shapes are not covered or scratch
-// cannot be allocated; then nothing was launched and the caller runs the
-// exact kernels.  Above gv::kMaxRows rows it runs passes of gv::kMaxRows rows
-// (the scratch of the largest pass is reserved before the first launch, so a
-// residual output is never half updated).
-inline bool gemv_run(sr_model* m, const float* X, int n, const Param* const* W, const LinearOut* O, int nseg) {
-  if (nseg < 1 || nseg > gv::kMaxSeg) return false;
-  for (int i = 0; i < nseg; i++)
-    if (!gemv_covers(*W[i], n) || W[i]->format != W[0]->format || W[i]->cols != W[0]->cols ||
-        (O[i].out_map != O[0].out_map))
-      return false;
-  gv::Args a;
-  dim3 grid;
-  int nr;
-  const int in = W[0]->cols;
-  if (!gemv_prepare(m, X, std::min(n, gv::kMaxRows), W, O, nseg, &a, &grid, &nr)) return false;
-  for (int r0 = 0; r0 < n; r0 += gv::kMaxRows) {
-    const int rows = std::min(gv::kMaxRows, n - r0);
-    if (r0 > 0) {  // this pass's rows: inputs, outputs and residuals (or head row map) from row r0
-      LinearOut P[gv::kMaxSeg];
-      for (int i = 0; i < nseg; i++) {
-        P[i] = O[i];
-        if (O[i].out_map) {
-          P[i].out_map = O[i].out_map + r0;
-        } else {
-          P[i].y = O[i].y + (int64_t)r0 * O[i].ldy;
-          if (O[i].resid) P[i].resid = O[i].resid + (int64_t)r0 * O[i].ldy;
-        }
-      }
-      if (!gemv_prepare(m, X + (int64_t)r0 * in, rows, W, P, nseg, &a, &grid, &nr)) return false;  // fits: reserved above
-    }
-    switch (nr) {
-      case 1: gemv_launch<1>(a, grid, m->stream); break;
-      case 2: gemv_launch<2>(a, grid, m->stream); break;
-      case 4: gemv_launch<4>(a, grid, m->stream); break;
-      default: gemv_launch<8>(a, grid, m->stream); break;
-    }
-    sr_count_launch(m);
-  }
+  const dim3 grid(tiles, a.ksplit);
+  if (nr == 1) gemv_launch<1>(a, grid, m->stream);
+  else gemv_launch<2>(a, grid, m->stream);
+  sr_count_launch(m);
   return true;
 }
 

@@ -1,5 +1,5 @@
-// gemv.cuh -- SR_MODE_FAST decode projections for steps of fewer than 32
-// rows (one launch per kMaxRows rows): Y[n, out] = X[n, in] W[out, in]^T with
+// gemv.cuh -- SR_MODE_FAST decode projections for steps of 1 or 2 rows:
+// Y[n, out] = X[n, in] W[out, in]^T with
 // W in the reference's Q8 / Q4 storage (Param, cmd/monolith/monolith.go:3784-3850),
 // read as stored.
 //
@@ -31,7 +31,11 @@ namespace gv {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSeg = 3;
-constexpr int kMaxRows = 8;  // rows of the largest instantiation
+// Rows of the largest instantiation.  With more step rows the FMAs per weight
+// byte (one per row) bound the kernel below the tensor cores' time (measured on
+// the Mistral-7B step: 1 row 3.8 ms, 2 rows 4.3 ms, 4 rows 7.2 ms against 5.3 ms
+// for the tcgen05 path at any row count up to 128).
+constexpr int kMaxRows = 2;
 // Weight rows per warp (more rows share each staged activation read) and per CTA.
 __host__ __device__ constexpr int rows_per_warp(int nr) { return nr <= 2 ? 8 : 4; }
 __host__ __device__ constexpr int rows_per_cta(int nr) { return kWarps * rows_per_warp(nr); }

@@ -139,12 +139,12 @@ def test_fast_qwen_shape_32k_context_decode(oracle, srlib):
     assert err <= FAST_ATOL, f"32K-context decode logits differ by {err:.3g}"
 
 
-@pytest.mark.parametrize("rows", [1, 4, 16, 31])
+@pytest.mark.parametrize("rows", [1, 2, 4, 16, 31])
 def test_fast_decode_rows(oracle, srlib, rows):
-    """Fast-mode decode steps of 1, 4, 16 and 31 rows (the decode GEMV, in
-    passes of 8 rows above 8; the tensor cores from 32) on the Mistral-7B
-    layer shape, 2 layers, Q8: `rows` sessions with short prompts, then 3
-    decode steps, each against the oracle."""
+    """Fast-mode decode steps of 1, 4, 16 and 31 rows (the decode GEMV at 1
+    row, the tensor cores from 3) on the Mistral-7B layer shape, 2 layers, Q8:
+    `rows` sessions with short prompts, then 3 decode steps, each against the
+    oracle."""
     cfg = oracle.make_config(2048, 4096, 14336, 2, 32, 8, 512, rope_theta=1e6, tied=False, weight_format="q8",
                              page_tokens=16)
     om = oracle.Model(cfg)
