@@ -98,6 +98,14 @@ __device__ __forceinline__ double penalized(const SampleArgs& a, const uint32_t*
   return x;
 }
 
+// The penalized logit of a value already loaded (penalized() above reads it).
+__device__ __forceinline__ double penalized_value(const uint32_t* seen, bool use_seen, double pen, float v, int id) {
+  double x = (double)v;
+  if (use_seen && ((seen[id >> 5] >> (id & 31)) & 1u)) x = x > 0 ? __ddiv_rn(x, pen) : __dmul_rn(x, pen);
+  return x;
+}
+constexpr int kSampleUnroll = 8;
+
 __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
   extern __shared__ __align__(16) uint32_t seen[];  // ceil(V/32) words
   __shared__ int hist[256];
@@ -196,11 +204,23 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
     const uint64_t phi = s_phi;
     const uint32_t plo = s_plo;
     const int nd = s_nd;
-    for (int id = tid; id < V; id += blockDim.x) {
-      if (id == a.blocked) continue;
-      uint64_t hi = ord64(penalized(a, seen, use_seen, st.penalty, lg, id));
-      uint32_t lo = 0xffffffffu - (uint32_t)id;
-      if (key_cmp_prefix(hi, lo, phi, plo, nd) == 0) atomicAdd(&hist[key_digit(hi, lo, d)], 1);
+    // kSampleUnroll logits per thread are loaded before any is used (the
+    // scan is bound by load latency: one CTA walks the whole vocabulary)
+    for (int id0 = tid; id0 < V; id0 += blockDim.x * kSampleUnroll) {
+      float v[kSampleUnroll];
+#pragma unroll
+      for (int u = 0; u < kSampleUnroll; u++) {
+        const int id = id0 + u * blockDim.x;
+        v[u] = id < V ? lg[id] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kSampleUnroll; u++) {
+        const int id = id0 + u * blockDim.x;
+        if (id >= V || id == a.blocked) continue;
+        uint64_t hi = ord64(penalized_value(seen, use_seen, st.penalty, v[u], id));
+        uint32_t lo = 0xffffffffu - (uint32_t)id;
+        if (key_cmp_prefix(hi, lo, phi, plo, nd) == 0) atomicAdd(&hist[key_digit(hi, lo, d)], 1);
+      }
     }
     __syncthreads();
     if (tid == 0) {
@@ -228,16 +248,26 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
     const uint64_t phi = s_phi;
     const uint32_t plo = s_plo;
     const int nd = s_nd;
-    for (int id = tid; id < V; id += blockDim.x) {
-      if (id == a.blocked) continue;
-      double x = penalized(a, seen, use_seen, st.penalty, lg, id);
-      uint64_t hi = ord64(x);
-      uint32_t lo = 0xffffffffu - (uint32_t)id;
-      if (key_cmp_prefix(hi, lo, phi, plo, nd) >= 0) {
-        int slot = atomicAdd(&s_count, 1);
-        if (slot < kMaxTopK) {
-          cx[slot] = x;
-          cid[slot] = id;
+    for (int id0 = tid; id0 < V; id0 += blockDim.x * kSampleUnroll) {
+      float v[kSampleUnroll];
+#pragma unroll
+      for (int u = 0; u < kSampleUnroll; u++) {
+        const int id = id0 + u * blockDim.x;
+        v[u] = id < V ? lg[id] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kSampleUnroll; u++) {
+        const int id = id0 + u * blockDim.x;
+        if (id >= V || id == a.blocked) continue;
+        double x = penalized_value(seen, use_seen, st.penalty, v[u], id);
+        uint64_t hi = ord64(x);
+        uint32_t lo = 0xffffffffu - (uint32_t)id;
+        if (key_cmp_prefix(hi, lo, phi, plo, nd) >= 0) {
+          int slot = atomicAdd(&s_count, 1);
+          if (slot < kMaxTopK) {
+            cx[slot] = x;
+            cid[slot] = id;
+          }
         }
       }
     }
