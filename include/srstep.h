@@ -74,7 +74,7 @@ typedef struct sr_model_desc {
      * = n_inner), tied head, kv_heads == heads, no RoPE.  Parameters follow
      * loadGPT2's order with [out, in] matrices: wte, wpe, ln_f.weight,
      * ln_f.bias, then per layer ln_1 w/b, q, k, v, q/k/v biases, o, o bias, ln_2
-     * w/b, c_fc, c_fc bias, c_proj, c_proj bias.  Exact mode only, one GPU. */
+     * w/b, c_fc, c_fc bias, c_proj, c_proj bias.  Exact or fast mode, one GPU. */
     int32_t arch;          /* SR_ARCH_LLAMA (0) or SR_ARCH_GPT2 (1) */
     int32_t positions;     /* GPT-2 position-table rows (n_positions) */
 } sr_model_desc;

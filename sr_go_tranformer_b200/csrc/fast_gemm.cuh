@@ -228,6 +228,13 @@ inline bool tc_build_all(sr_model* m, TcState* t, bool cache) {
   t->gateup.assign(L, TcMatrix());
   t->down.assign(L, TcMatrix());
   for (int l = 0; l < L; l++) {
+    if (m->d.arch == SR_ARCH_GPT2) {  // loadGPT2's layer order: q, k, v at +2..4, o +8, c_fc +12, c_proj +14
+      const Param* P = &m->params[4 + 16 * l];
+      if (!tc_build(m, t, t->qkv[l], {&P[2], &P[3], &P[4]}, cache) || !tc_build(m, t, t->o[l], {&P[8]}, cache) ||
+          !tc_build(m, t, t->gateup[l], {&P[12]}, cache) || !tc_build(m, t, t->down[l], {&P[14]}, cache))
+        return false;
+      continue;
+    }
     const Param* P = &m->params[1 + 9 * l];
     if (!tc_build(m, t, t->qkv[l], {&P[1], &P[2], &P[3]}, cache) || !tc_build(m, t, t->o[l], {&P[4]}, cache) ||
         !tc_build(m, t, t->gateup[l], {&P[6], &P[7]}, cache) || !tc_build(m, t, t->down[l], {&P[8]}, cache))
@@ -427,19 +434,35 @@ inline __nv_bfloat16* tc_xl(sr_model* m) { return tc_state(m)->xl; }
 // the operand planes.
 // With a lane (one half of a split step), n is the half's row count, the
 // operand planes are the lane's slot and the outputs start at row lane->row0.
-inline bool tc_qkv(sr_model* m, int l, int n, bool presplit = false, const TcLane* lane = nullptr) {
+// Q|K|V with explicit biases (each may be null).
+inline bool tc_qkv_bias(sr_model* m, int l, int n, bool presplit, const TcLane* lane, const float* bq,
+                        const float* bk, const float* bv) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
   const ModelDims& dm = m->dm;
-  const Param* B = m->d.qkv_bias ? &m->params[2 + 9 * dm.layers + 3 * l] : nullptr;
   const int64_t r0 = lane ? lane->row0 : 0;
   tc::GemmArgs a{};
   a.nseg = 3;
-  a.seg[0] = seg(dm.qd, m->Q + r0 * dm.qd, dm.qd, B ? (const float*)B[0].values : nullptr, nullptr);
-  a.seg[1] = seg(dm.kvd, m->K + r0 * dm.kvd, dm.kvd, B ? (const float*)B[1].values : nullptr, nullptr);
-  a.seg[2] = seg(dm.kvd, m->V + r0 * dm.kvd, dm.kvd, B ? (const float*)B[2].values : nullptr, nullptr);
+  a.seg[0] = seg(dm.qd, m->Q + r0 * dm.qd, dm.qd, bq, nullptr);
+  a.seg[1] = seg(dm.kvd, m->K + r0 * dm.kvd, dm.kvd, bk, nullptr);
+  a.seg[2] = seg(dm.kvd, m->V + r0 * dm.kvd, dm.kvd, bv, nullptr);
   a.out_map = nullptr;
   if (!presplit) tc_split_x(m, m->N, n, dm.dim);
   return tc_gemm(m, tc_state(m)->qkv[l], 0, n, a, lane);
+}
+inline bool tc_qkv(sr_model* m, int l, int n, bool presplit = false, const TcLane* lane = nullptr) {
+  const Param* B = m->d.qkv_bias ? &m->params[2 + 9 * m->dm.layers + 3 * l] : nullptr;
+  return tc_qkv_bias(m, l, n, presplit, lane, B ? (const float*)B[0].values : nullptr,
+                     B ? (const float*)B[1].values : nullptr, B ? (const float*)B[2].values : nullptr);
+}
+// GPT-2's c_fc (+ bias) into G, from operand planes a producer already wrote.
+inline bool tc_fc(sr_model* m, int l, int n, const float* bias) {
+  if (n < kTcMinRows || !tc_prepare(m)) return false;
+  const ModelDims& dm = m->dm;
+  tc::GemmArgs a{};
+  a.nseg = 1;
+  a.seg[0] = seg(dm.hidden, m->G, dm.hidden, bias, nullptr);
+  a.out_map = nullptr;
+  return tc_gemm(m, tc_state(m)->gateup[l], 0, n, a);
 }
 // gate|up in one GEMM.
 inline bool tc_gateup(sr_model* m, int l, int n, bool presplit = false, const TcLane* lane = nullptr) {
@@ -458,24 +481,24 @@ inline bool tc_gateup(sr_model* m, int l, int n, bool presplit = false, const Tc
 // resid is set; tensor-parallel ranks write their partial sum instead).
 // (y and resid point at the first output row: the caller offsets them for a lane.)
 inline bool tc_proj(sr_model* m, const TcMatrix& W, const float* X, int n, int in_kind, bool presplit, float* y,
-                    const float* resid, const TcLane* lane = nullptr) {
+                    const float* resid, const TcLane* lane = nullptr, const float* bias = nullptr) {
   const ModelDims& dm = m->dm;
   tc::GemmArgs a{};
   a.nseg = 1;
-  a.seg[0] = seg(dm.dim, y, dm.dim, nullptr, resid);
+  a.seg[0] = seg(dm.dim, y, dm.dim, bias, resid);
   a.out_map = nullptr;
   if (!presplit) tc_split_x(m, X, n, in_kind == 1 ? dm.hidden : (in_kind == 2 ? dm.qd : dm.dim));
   return tc_gemm(m, W, in_kind, n, a, lane);
 }
 inline bool tc_o(sr_model* m, int l, int n, bool presplit, float* y, const float* resid,
-                 const TcLane* lane = nullptr) {
+                 const TcLane* lane = nullptr, const float* bias = nullptr) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
-  return tc_proj(m, tc_state(m)->o[l], m->A, n, 2, presplit, y, resid, lane);
+  return tc_proj(m, tc_state(m)->o[l], m->A, n, 2, presplit, y, resid, lane, bias);
 }
 inline bool tc_down(sr_model* m, int l, int n, bool presplit, float* y, const float* resid,
-                    const TcLane* lane = nullptr) {
+                    const TcLane* lane = nullptr, const float* bias = nullptr) {
   if (n < kTcMinRows || !tc_prepare(m)) return false;
-  return tc_proj(m, tc_state(m)->down[l], m->H, n, 1, presplit, y, resid, lane);
+  return tc_proj(m, tc_state(m)->down[l], m->H, n, 1, presplit, y, resid, lane, bias);
 }
 // The operand planes of slot `slot` (row 0 of a lane's rows).
 inline void tc_planes(sr_model* m, int slot, __nv_bfloat16** xh, __nv_bfloat16** xl) {

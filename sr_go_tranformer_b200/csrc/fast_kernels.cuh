@@ -153,6 +153,64 @@ __global__ void k_swiglu_split(const float* __restrict__ G, const float* __restr
   }
 }
 
+// ------------------------------------------------------------ GPT-2, fast --
+// layerNormInto (M:5167-5185) reordered: one 128-thread block per row, the sum
+// and then the sum of squared deviations in fp64 over strided partial sums,
+// y = float32((x - mean) * inv) * w + b with an FMA, written as fp32 Y or as the
+// next projection's bf16 hi/lo operand planes (yh/yl, row r at r * d).
+// src_map (optional) gathers input rows.
+__global__ void __launch_bounds__(128)
+k_layernorm_fast(const float* __restrict__ X, const int32_t* __restrict__ src_map, const float* __restrict__ w,
+                 const float* __restrict__ b, float* __restrict__ Y, int rows, int d, double eps,
+                 op16* __restrict__ yh, op16* __restrict__ yl) {
+  __shared__ double red[2][4];
+  const int r = blockIdx.x;
+  const int srow = src_map ? src_map[r] : r;
+  const float* x = X + (int64_t)srow * d;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  double s = 0.0;
+  for (int j = threadIdx.x; j < d; j += 128) s += (double)x[j];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) red[0][warp] = s;
+  __syncthreads();
+  const double mean = (red[0][0] + red[0][1] + red[0][2] + red[0][3]) / (double)d;
+  double v = 0.0;
+  for (int j = threadIdx.x; j < d; j += 128) {
+    const double z = (double)x[j] - mean;
+    v += z * z;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  if (lane == 0) red[1][warp] = v;
+  __syncthreads();
+  const double var = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+  const double inv = 1.0 / sqrt(var / (double)d + eps);
+  const int64_t o = (int64_t)r * d;
+  for (int j = threadIdx.x; j < d; j += 128) {
+    const float y = fmaf((float)(((double)x[j] - mean) * inv), w[j], b[j]);
+    if (yh)
+      split_op(y, yh + o + j, yl + o + j);
+    else
+      Y[o + j] = y;
+  }
+}
+
+// gelu_new (M:6405-6407) in fp32: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
+// written as fp32 H or as the c_proj projection's bf16 hi/lo operand planes.
+__global__ void k_gelu_fast(const float* __restrict__ G, float* __restrict__ H, op16* __restrict__ hh,
+                            op16* __restrict__ hl, int64_t count) {
+  const float c = 0.7978845608028654f;  // sqrt(2/pi)
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+    const float g = G[i];
+    const float y = 0.5f * g * (1.f + tanhf(c * (g + 0.044715f * g * g * g)));
+    if (hh)
+      split_op(y, hh + i, hl + i);
+    else
+      H[i] = y;
+  }
+}
+
 // ---------------------------------------------------------------- attention --
 // Work counts of one step's fast attention: all (row, split) items, those of
 // rows from 1-token chunks, and the (row group, split) pairs of longer chunks.

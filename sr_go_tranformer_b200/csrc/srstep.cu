@@ -826,8 +826,6 @@ extern "C" int sr_model_load_param_f32(sr_model* m, int32_t index, const float* 
 extern "C" int sr_model_set_mode(sr_model* m, int32_t mode) {
   if (!m) return sr_fail(SR_EINVAL, "null model");
   if (mode != SR_MODE_EXACT && mode != SR_MODE_FAST) return sr_fail(SR_EINVAL, "invalid mode");
-  if (mode == SR_MODE_FAST && m->d.arch == SR_ARCH_GPT2)
-    return sr_fail(SR_EUNSUPPORTED, "the GPT-2 profile runs in the exact mode only");
   m->mode = mode;
   return SR_OK;
 }
@@ -1203,8 +1201,118 @@ static void tp_add(sr_model* m, int n, const TpSum& t) {
 // then per layer LayerNorm, Q/K/V with bias, K/V write without RoPE,
 // attention, O with bias + residual, LayerNorm, c_fc with bias, GELU-tanh,
 // c_proj with bias + residual; the selected head is LayerNorm + tied wte.
+// The GPT-2 profile in SR_MODE_FAST: the same steps as gpt2_step_enqueue
+// with the fast kernels -- LayerNorm and GELU in fp32 with fp64 statistics
+// (k_layernorm_fast, k_gelu_fast) writing the next projection's bf16 hi/lo
+// operand planes, the projections with their biases (and residuals) on the
+// tensor cores from 3 rows (the decode GEMV or, for f32 weights, the exact
+// kernels below that), split-K attention where the head dimension is 64 or
+// 128.  Matches the exact step within the fast-mode tolerance.
+static int gpt2_fast_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info,
+                                  const volatile int32_t* cancel) {
+  const ModelDims& dm = m->dm;
+  const int n = info.rows, d = dm.dim, L = dm.layers;
+  const double eps = m->d.norm_eps;
+  cudaStream_t s = m->stream;
+  auto fv = [&](int i) { return (const float*)m->params[i].values; };
+  sr_prof_span_begin(m);
+  SR_LAUNCH(m, SR_PROF_META, k_meta<<<1, 1024, 0, s>>>(m->meta, info.sessions, n));
+  SR_LAUNCH(m, SR_PROF_EMBED, k_embed<<<n, 256, 0, s>>>(m->params[0], m->meta.tokens, m->X, d);
+            k_add_position<<<n, 256, 0, s>>>(m->X, fv(1), m->meta, d));
+  sr_count_launch(m, 3);
+  const bool tc = tc_active(m, n);
+  op16* xh = tc ? tc_xh(m) : nullptr;
+  op16* xl = tc ? tc_xl(m) : nullptr;
+  const int64_t hcnt = (int64_t)n * dm.hidden;
+  const int gelu_blocks = (int)std::min<int64_t>((hcnt + 255) / 256, 148 * 16);
+  const char* tc_fail = "tensor-core projection could not run (scratch allocation failed)";
+  for (int l = 0; l < L; l++) {
+    if (cancel && *cancel) {
+      sr_prof_span_end(m);
+      cudaStreamSynchronize(s);
+      sr_prof_resolve(m);
+      return sr_fail(SR_ECANCELED, "step canceled between layers");
+    }
+    const int b = 4 + 16 * l;
+    const Param* P = &m->params[b];
+    LinearOut o;
+    o.resid = nullptr;
+    o.out_map = nullptr;
+    SR_LAUNCH(m, SR_PROF_NORM,
+              k_layernorm_fast<<<n, 128, 0, s>>>(m->X, nullptr, fv(b), fv(b + 1), m->N, n, d, eps, xh, xl));
+    bool done;
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_qkv_bias(m, l, n, true, nullptr, fv(b + 5), fv(b + 6), fv(b + 7)));
+    if (tc && !done) return sr_fail(SR_ENOMEM, tc_fail);
+    if (!done) {
+      float* qkv[3] = {m->Q, m->K, m->V};
+      for (int k = 0; k < 3; k++) {
+        o.y = qkv[k];
+        o.ldy = d;
+        o.bias = fv(b + 5 + k);
+        sr_launch_linear(m, m->N, n, P[2 + k], o);
+      }
+    }
+    SR_LAUNCH(m, SR_PROF_ROPE_KV, k_kv_write_exact<<<n, 128, 0, s>>>(m->K, m->V, m->meta, pool->data, dm, l));
+    sr_count_launch(m, 3);  // norm, kv write, second norm
+    bool a_split = false;   // the attention wrote the O projection's operand planes
+    SR_LAUNCH(m, SR_PROF_ATTENTION, a_split = fast_attention(m, pool, n, info, l, xh, xl));
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_o(m, l, n, a_split, m->X, m->X, nullptr, fv(b + 9)));
+    if (tc && !done) return sr_fail(SR_ENOMEM, tc_fail);
+    if (!done) {
+      o.y = m->X;  // X += O(a) + bias (M:6398-6400)
+      o.ldy = d;
+      o.bias = fv(b + 9);
+      o.resid = m->X;
+      sr_launch_linear(m, m->A, n, P[8], o);
+    }
+    SR_LAUNCH(m, SR_PROF_NORM,
+              k_layernorm_fast<<<n, 128, 0, s>>>(m->X, nullptr, fv(b + 10), fv(b + 11), m->N, n, d, eps, xh, xl));
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_fc(m, l, n, fv(b + 13)));
+    if (tc && !done) return sr_fail(SR_ENOMEM, tc_fail);
+    if (!done) {
+      o.y = m->G;
+      o.ldy = dm.hidden;
+      o.bias = fv(b + 13);
+      o.resid = nullptr;
+      sr_launch_linear(m, m->N, n, P[12], o);
+    }
+    SR_LAUNCH(m, SR_PROF_SWIGLU, k_gelu_fast<<<gelu_blocks, 256, 0, s>>>(m->G, m->H, xh, xl, hcnt));
+    sr_count_launch(m);
+    SR_LAUNCH(m, SR_PROF_LINEAR, done = tc && tc_down(m, l, n, true, m->X, m->X, nullptr, fv(b + 15)));
+    if (tc && !done) return sr_fail(SR_ENOMEM, tc_fail);
+    if (!done) {
+      o.y = m->X;  // X += c_proj(h) + bias (M:6415-6417)
+      o.ldy = d;
+      o.bias = fv(b + 15);
+      o.resid = m->X;
+      sr_launch_linear(m, m->H, n, P[14], o);
+    }
+  }
+  CK(cudaMemsetAsync(m->logits, 0, (size_t)info.sessions * dm.vocab * 4, s));
+  if (info.heads > 0) {
+    const bool tc_h = tc_active(m, info.heads);
+    SR_LAUNCH(m, SR_PROF_HEAD,
+              k_layernorm_fast<<<info.heads, 128, 0, s>>>(m->X, m->meta.head_src, fv(2), fv(3), m->N, info.heads, d,
+                                                          eps, tc_h ? tc_xh(m) : nullptr, tc_h ? tc_xl(m) : nullptr));
+    sr_count_launch(m);
+    LinearOut o;
+    o.y = m->logits;
+    o.ldy = dm.vocab;
+    o.bias = nullptr;
+    o.resid = nullptr;
+    o.out_map = m->meta.head_dst;
+    bool done;
+    SR_LAUNCH(m, SR_PROF_HEAD, done = tc_h && tc_head(m, info.heads, true));
+    if (tc_h && !done) return sr_fail(SR_ENOMEM, "tensor-core LM head could not run (scratch allocation failed)");
+    if (!done) sr_launch_linear(m, m->N, info.heads, m->params[0], o, SR_PROF_HEAD);
+  }
+  CK(cudaGetLastError());
+  return SR_OK;
+}
+
 static int gpt2_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info, const volatile int32_t* cancel) {
   const ModelDims& dm = m->dm;
+  if (m->mode == SR_MODE_FAST) return gpt2_fast_step_enqueue(m, pool, info, cancel);
   const int n = info.rows, d = dm.dim, L = dm.layers;
   const double eps = m->d.norm_eps;
   cudaStream_t s = m->stream;
