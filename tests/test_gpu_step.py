@@ -417,18 +417,31 @@ def test_engine_prefix_config_errors(oracle, srlib):
     e.close()
 
 
-def test_engine_token_events(oracle, srlib):
+@pytest.mark.parametrize("table", ["hf-bytes", "mistral-fallback"])
+def test_engine_token_events(oracle, srlib, table):
     """TokenEvent (M:8451-8462): one event per sampled token, in order, whose
     texts concatenate to the decoder's text of the request's pieces; the last
-    is final."""
+    is final.  "hf-bytes": byte-level pieces where some ids hold half of a
+    multi-byte character.  "mistral-fallback": a SentencePiece-style table where
+    a third of the ids are byte-fallback tokens holding single bytes of
+    multi-byte characters (runs may end a request part-way: the final event
+    flushes them) and the rest are pieces with the leading-space marker."""
     from sr_go_tranformer_b200.engine import Engine
     from sr_go_tranformer_b200.text import TextDecoder
     om, dm = synthetic_pair(oracle, srlib, "q8", 16, vocab=300)
-    euro = "€".encode()
-    pieces = [bytes([97 + i % 26]) if i % 7 else euro[:2] if i % 2 else euro[2:] for i in range(300)]
+    if table == "hf-bytes":
+        euro = "€".encode()
+        pieces = [bytes([97 + i % 26]) if i % 7 else euro[:2] if i % 2 else euro[2:] for i in range(300)]
+        flags, fallback = dict(hf=True), None
+    else:
+        utf8 = "€ü世".encode()  # 3 + 2 + 3 bytes
+        fallback = np.array([1 if i % 3 == 0 else 0 for i in range(300)], dtype=np.uint8)
+        pieces = [bytes([utf8[(i // 3) % len(utf8)]]) if fallback[i] else ("\u2581" * (i % 2) + chr(97 + i % 26)).encode()
+                  for i in range(300)]
+        flags = dict(mistral=True, fallback=fallback)
     eng = Engine(dm, max_batch=2, token_budget=16, prefill_chunk=8, mixed_prefill_chunk=1,
                  cache_bytes=24 * om.page_elements * 4)
-    eng.set_pieces(pieces, hf=True)
+    eng.set_pieces(pieces, **flags)
     rng = np.random.default_rng(3)
     rids = [eng.submit(rng.integers(0, 300, size=int(rng.integers(2, 20))).tolist(), int(rng.integers(2, 9)),
                        0.9, 20, 0.9, 1.0, 11 + i) for i in range(3)]
@@ -444,7 +457,7 @@ def test_engine_token_events(oracle, srlib):
         evs = events[rid]
         assert [t for t, _, _ in evs] == out
         assert [f for _, _, f in evs] == [False] * (len(out) - 1) + [True]
-        d = TextDecoder(hf=True)
+        d = TextDecoder(**flags)
         want = "".join(d.push_token(t, pieces[t], k == len(out) - 1) for k, t in enumerate(out))
         assert "".join(x for _, x, _ in evs) == want
     eng.close()
