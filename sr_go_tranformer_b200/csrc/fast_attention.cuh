@@ -136,6 +136,28 @@ __device__ __forceinline__ void warp_tile8(const float* kt, const float* vt, int
       kk += __shfl_xor_sync(0xffffffffu, b1 ? k0 : k1, 2);
       kk += __shfl_xor_sync(0xffffffffu, kk, 4);
       if ((lane & 4) == 0) sc[(2 * (int)b0 + (int)b1) * MT + s] = s < tn ? kk : -INFINITY;
+    } else if constexpr (G > 4) {
+      // 5..8 heads, padded to 8: reduce-scatter over the position's 8 lanes
+      // (7 shuffles instead of 3 per head); lane bits (b0, b1, b2) end up
+      // holding head 4*b0 + 2*b1 + b2
+      float h8[8];
+#pragma unroll
+      for (int g = 0; g < 8; g++) h8[g] = g < G ? part[g] : 0.f;
+      const bool b0 = lane & 1, b1 = lane & 2, b2 = lane & 4;
+      float k4[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float keep = b0 ? h8[4 + j] : h8[j], send = b0 ? h8[j] : h8[4 + j];
+        k4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+      }
+      float m0 = b1 ? k4[2] : k4[0], m1 = b1 ? k4[3] : k4[1];
+      const float s0 = b1 ? k4[0] : k4[2], s1 = b1 ? k4[1] : k4[3];
+      m0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+      m1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+      float kk = b2 ? m1 : m0;
+      kk += __shfl_xor_sync(0xffffffffu, b2 ? m0 : m1, 4);
+      const int h = 4 * (int)b0 + 2 * (int)b1 + (int)b2;
+      if (h < G) sc[h * MT + s] = s < tn ? kk : -INFINITY;
     } else {
 #pragma unroll
       for (int off = 1; off < 8; off <<= 1)
