@@ -207,8 +207,6 @@ def test_peer_allreduce_absent_rank_times_out(tmp_path):
     assert pos == 0
 
 
-@pytest.mark.skipif(os.environ.get("SR_GPU_PEER_LL") != "1",
-                    reason="the LL peer protocol has not yet run on a GPU (set SR_GPU_PEER_LL=1)")
 @pytest.mark.parametrize("size", [2, 4])
 @pytest.mark.parametrize("mode", ["exact", "fast"])
 def test_peer_ll_protocol_equals_barrier_protocol(mode, size, tmp_path):
