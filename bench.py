@@ -316,7 +316,7 @@ def weight_bytes(cfg):
         return r * ((c + 1) // 2 if q4m else c) + r * ((c + 63) // 64) * 4
 
     mats = [(d, d), (kd, d), (kd, d), (d, d), (h, d), (h, d), (d, h)]
-    per_layer = sum(mat(r, c, q4) for r, c in mats) + 2 * d * 4 + (2 * d + 2 * kd) * 4 * cfg.get("qkv_bias", False)
+    per_layer = sum(mat(r, c, q4) for r, c in mats) + 2 * d * 4 + (d + 2 * kd) * 4 * cfg.get("qkv_bias", False)
     head = mat(V, d, cfg["fmt"] == "q4")
     return L * per_layer + head + d * 4
 
