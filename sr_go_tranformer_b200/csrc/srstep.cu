@@ -1403,7 +1403,11 @@ static int gpt2_step_enqueue(sr_model* m, sr_kvpool* pool, const BatchInfo& info
 // operand planes, stream-K scratch and attention item range.  The step's
 // results per row are the same arithmetic as the unsplit fast step except the
 // stream-K cut of each projection (the partition's SM count changes which
-// block ranges are summed first).
+// block ranges are summed first).  Off by default (sr_model_set_split): on the
+// Mistral-7B step one half's attention on 72 SMs reaches only 45% of the HBM
+// bandwidth (the kernel is bound by instruction issue per SM as much as by
+// HBM), so two alternating half-speed attentions take as long as the whole
+// step's and the split step is slower (10.55 against 7.96 ms per 8 layers).
 namespace {
 
 struct SplitState {
