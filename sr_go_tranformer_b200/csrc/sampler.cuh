@@ -37,7 +37,7 @@ struct SampleArgs {
   int32_t* status;  // 0 ok, 1 nonfinite logit, 2 empty distribution, 3 unsupported
 };
 
-constexpr int kSampleThreads = 256;
+constexpr int kSampleThreads = 1024;  // one CTA per session walks its whole vocabulary
 constexpr int kMaxTopK = 256;
 constexpr int kSampleFullThreads = 1024;
 constexpr int kSampleFullStage = 2048;  // fp64 values staged in shared memory per sequential chunk
@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
   }
   __syncthreads();
   for (int d = 0; d < 12; d++) {
-    hist[tid] = 0;
+    if (tid < 256) hist[tid] = 0;
     __syncthreads();
     const uint64_t phi = s_phi;
     const uint32_t plo = s_plo;
