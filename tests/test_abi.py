@@ -44,3 +44,22 @@ def test_error_path_without_device(srlib):
     assert b"null" in srlib.sr_last_error()
     assert b"sm_100a" in srlib.sr_version()
     assert isinstance(ctypes.c_int(rc).value, int)
+
+
+def test_null_model_rejected_before_any_device_call(srlib):
+    """Every model entry point added beside the step (mode, code cache, split
+    steps, single projection, sampler over host logits) refuses a null model
+    with SR_EINVAL and a message, touching no device."""
+    from sr_go_tranformer_b200 import _abi
+    out = ctypes.c_int32()
+    calls = [
+        lambda: srlib.sr_model_set_mode(None, 1),
+        lambda: srlib.sr_model_set_code_cache(None, 1),
+        lambda: srlib.sr_model_code_cache(None, ctypes.byref(out)),
+        lambda: srlib.sr_model_set_split(None, 1),
+        lambda: srlib.sr_linear(None, 0, 1, None, None),
+        lambda: srlib.sr_sample_logits(None, 1, 8, None, None, None, None, None, -1, None),
+    ]
+    for call in calls:
+        assert call() == _abi.SR_EINVAL
+        assert b"null" in srlib.sr_last_error()
